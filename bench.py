@@ -1,0 +1,362 @@
+"""Benchmark of the quantized matrix hot path on B200.
+
+Headline (one JSON line on rank 0): MoE layer throughput, token-layers per second,
+of the batch-union routed-expert FFN over a Gemma-4-shaped 30-layer stack of resident
+q4_0 experts (BASELINE configs 3 and 5: 128 experts x 30 layers = 3840 experts,
+12.85 GB in HBM; D 2816, inter 704, top-8, Zipf(1.1)-skewed routing, S tokens per step).
+One step = every layer of the stack applied to S tokens; each layer reads ~428 MB of
+distinct expert weights, far beyond the 126 MB L2, so no L2 flush is needed.
+Sub-benchmarks in the same line: the config-1 q4_0 GEMV (HBM GB/s), the config-2
+decode experts, the S=4096 prefill layer (int8 TOPS) and the Maple tq2 layer.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl zz|reference]
+Under torchrun (N > 1) experts are sharded across ranks (expert parallelism) and the
+routed q8_0 activations move with an NCCL all-to-all; see zunzuncito_b200/ep.py.
+"""
+import argparse
+import json
+import os
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+D, MI, E, K = 2816, 704, 128, 8
+LAYERS = 30
+EXPERT_BYTES = 3345408        # 2*(704*88*18) + 2816*22*18 (q40.h:313)
+GEMV_BYTES = 2816 * 1584 + 2816 + 88 * 4 + 2816 * 4   # config 1, per 2816x2816 GEMV
+MACS_PER_PAIR = 3 * MI * D    # gate + up + down per (token, expert)
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="zz", choices=["zz", "reference"])
+    ap.add_argument("--tokens", type=int, default=512)
+    ap.add_argument("--layers", type=int, default=LAYERS)
+    ap.add_argument("--no-sub", action="store_true", help="skip the sub-benchmarks")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
+    return ap.parse_args()
+
+
+# ----------------------------------------------------------------------------- clocks
+class ClockSampler:
+    """nvidia-smi samples during the timed region (clocks + throttle reasons)."""
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index, self.rows, self.proc = index, [], None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}",
+                                          "--format=csv,noheader,nounits", "-lms", "100"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except OSError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.rows.append([c.strip() for c in line.split(",")])
+
+    def __exit__(self, *a):
+        if self.proc:
+            self.proc.terminate()
+            self.proc.wait()
+            self.t.join(timeout=2)
+
+    def summary(self):
+        if not self.rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = [float(r[1]) for r in self.rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in self.rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({n for r in self.rows for n, v in zip(names, r[5:9]) if v.lower() == "active"})
+        return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(self.rows)}
+
+
+# ----------------------------------------------------------------------------- data
+def make_stack(zz, torch, layers, seed, keep_host_layer0=False):
+    """layers x 128 q4_0 experts quantized on device (bit-exact with q40_quant_row),
+    packed into expert banks; optionally a host copy of layer 0's reference blobs."""
+    stride = zz.expert_blob_bytes(zz.GPU_FMT_Q40, D, MI)
+    gb = zz.ref_tensor_bytes(zz.GPU_FMT_Q40, MI, D)
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    banks, host0 = [], None
+    for layer in range(layers):
+        blobs = torch.empty((E, stride), dtype=torch.uint8, device="cuda")
+        for i, (O, I) in enumerate([(MI, D), (MI, D), (D, MI)]):
+            w = torch.randn((E * O, I), generator=g, device="cuda") * 0.02
+            q = zz.quant_rows(zz.GPU_FMT_Q40, w).view(E, -1)
+            blobs[:, i * gb:i * gb + q.shape[1]] = q
+            del w, q
+        banks.append(zz.ExpertBankDev(zz.GPU_FMT_Q40, blobs, D, MI))
+        if keep_host_layer0 and layer == 0:
+            host0 = blobs.cpu().numpy()
+        del blobs
+    torch.cuda.synchronize()
+    return banks, host0
+
+
+def routing(synth, layers, S, seed):
+    return [synth.zipf_routing(seed + 17 * l, S, E, K)[:2] for l in range(layers)]
+
+
+def timed(torch, fn, steps, warmup, stream):
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record(stream)
+    for _ in range(steps):
+        fn()
+    t1.record(stream)
+    torch.cuda.synchronize()
+    return t0.elapsed_time(t1) / steps
+
+
+# ----------------------------------------------------------------------------- CPU
+def cpu_baseline_moe(host_blobs, S, seed):
+    """The reference's own gemma4.c expert_apply over the batch union (oracle/_ref),
+    all host threads, one layer of the same workload."""
+    import oracle
+    from zunzuncito_b200 import synth
+    if oracle.reference_available():
+        lib, kind = oracle.Reference(), "reference"
+        lib.set_threads(os.cpu_count())
+        cores = lib.max_threads()
+    else:
+        lib, kind, cores = oracle.Oracle(), "port", 1
+    X = synth.gaussian(seed, (S, D))
+    eidx, ewt, _ = synth.zipf_routing(seed + 1, S, E, K)
+    lib.moe_layer(0, host_blobs, X[:8], eidx[:8], ewt[:8], D, MI)   # warm-up
+    t = time.perf_counter()
+    lib.moe_layer(0, host_blobs, X, eidx, ewt, D, MI)
+    dt = time.perf_counter() - t
+    return {"value": S / dt, "unit": "token-layers/s", "cores": cores, "kind": kind,
+            "sample": f"one Gemma-4 MoE layer, S={S} tokens, 128 q4_0 experts, top-8 (1 of {LAYERS} layers)",
+            "seconds": dt}
+
+
+def run_reference_arm(a, rank):
+    """--impl reference: the reference's CPU path on the host cores (rank 0 only)."""
+    if rank != 0:
+        return
+    import oracle
+    from zunzuncito_b200 import synth
+    if not oracle.reference_available():
+        oracle.build()
+    if oracle.reference_available():
+        lib, kind = oracle.Reference(), "reference"
+        lib.set_threads(os.cpu_count())
+        cores = lib.max_threads()
+    else:
+        lib, kind, cores = oracle.Oracle(), "port", 1
+    S = a.tokens
+    stride = 2 * (MI * (D // 32) * 18) + D * (MI // 32) * 18
+    r = synth.rng(5)
+    # random q4_0 bytes with sane fp16 scales (every byte pattern is a valid block)
+    blobs = r.integers(0, 256, size=(E, stride), dtype=np.uint8)
+    for off, rows, nb in [(0, 2 * MI, D // 32), (2 * MI * (D // 32) * 18, D, MI // 32)]:
+        v = blobs[:, off:off + rows * nb * 18].reshape(E, rows * nb, 18)
+        v[:, :, 0:2] = np.frombuffer(np.full(E * rows * nb, 0.002, np.float16).tobytes(), np.uint8).reshape(E, -1, 2)
+    X = synth.gaussian(6, (S, D))
+    eidx, ewt, _ = synth.zipf_routing(7, S, E, K)
+    times = []
+    for i in range(a.warmup + a.steps):
+        t = time.perf_counter()
+        lib.moe_layer(0, blobs, X, eidx, ewt, D, MI)
+        if i >= a.warmup:
+            times.append(time.perf_counter() - t)
+    ms = 1e3 * float(np.mean(times))
+    v = S / (ms / 1e3)
+    line = {"metric": "moe_layer_tok_per_s", "value": v, "unit": "token-layers/s", "n_gpus": a.gpus,
+            "steps": a.steps, "warmup": a.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "int8", "data": "synthetic", "impl": "reference",
+            "config": {"workload": f"Gemma-4 MoE layer, S={S}, 128 q4_0 experts, top-8 Zipf(1.1); one layer per step",
+                       "l2": "n/a (CPU)"},
+            "cpu_baseline": {"value": v, "unit": "token-layers/s", "cores": cores, "kind": kind,
+                             "sample": f"one layer of S={S} tokens per step"},
+            "e2e": {"value": v, "unit": "token-layers/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+# ----------------------------------------------------------------------------- main
+def main():
+    a = parse()
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if a.impl == "reference":
+        run_reference_arm(a, rank)
+        return
+    import torch
+    if world > 1:
+        from zunzuncito_b200 import ep
+        ep.bench_main(a, rank, world)
+        return
+    import zunzuncito_b200 as zz
+    from zunzuncito_b200 import synth
+
+    torch.cuda.set_device(0)
+    stream = torch.cuda.current_stream()
+    S, L = a.tokens, a.layers
+    banks, host0 = make_stack(zz, torch, L, seed=1234, keep_host_layer0=not a.no_cpu)
+    routes = routing(synth, L, S, seed=99)
+    X = torch.from_numpy(synth.gaussian(7, (S, D))).cuda()
+    eidx = [torch.from_numpy(r[0]).cuda() for r in routes]
+    ewt = [torch.from_numpy(r[1]).cuda() for r in routes]
+    out = torch.empty((S, D), device="cuda")
+    for b in banks:
+        b.workspace(S, K)
+    distinct = [len(np.unique(r[0])) for r in routes]
+
+    def step():
+        for l in range(L):
+            zz.moe_ffn(banks[l], X, eidx[l], ewt[l], zz.ZZ_ACT_GEGLU_TANH, out=out)
+
+    step()
+    torch.cuda.synchronize()
+    with ClockSampler(0) as clk:
+        ms = timed(torch, step, a.steps, a.warmup, stream)
+        # stage split of the same loop, live CUDA events inside the library
+        zz.lib.zz_prof_enable(1)
+        for _ in range(max(1, a.steps // 2)):
+            step()
+        zz.lib.zz_prof_enable(0)
+    import ctypes
+    st = (ctypes.c_float * 3)()
+    calls = ctypes.c_int()
+    zz.lib.zz_prof_collect(st, ctypes.byref(calls))
+    stage_ms = [st[i] / max(1, calls.value) for i in range(3)]   # per layer call
+
+    value = S * L / (ms / 1e3)
+    peaks = {}
+    try:
+        peaks = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
+    except OSError:
+        pass
+    hbm_peak = peaks.get("hbm_gbs", 6650.0)
+    peak_src = "measured" if "hbm_gbs" in peaks else "fallback"
+    # dominant kernel: gate/up GEMM; algorithmic bytes = distinct experts' gate+up planes
+    # (2 * 704 * 88 * 18 B) + the gathered q8_0 rows (2816 + 88*4 B per pair) + hq/hs out
+    gu_bytes = float(np.mean(distinct)) * 2 * MI * (D // 32) * 18 + S * K * (D + 4 * D // 32) + S * K * (MI + 4 * MI // 32)
+    gu_ms = stage_ms[1]
+    achieved = gu_bytes / (gu_ms / 1e3) / 1e9
+    layer_bytes = float(np.mean(distinct)) * EXPERT_BYTES
+    line = {
+        "metric": "moe_layer_tok_per_s", "value": value, "unit": "token-layers/s", "n_gpus": 1,
+        "steps": a.steps, "warmup": a.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "int8", "data": "synthetic",
+        "config": {"workload": f"Gemma-4 batch-union MoE stack: {L} layers x 128 q4_0 experts (12.85 GB resident), "
+                               f"S={S} tokens/step, top-8 Zipf(1.1) routing, GeGLU",
+                   "tokens": S, "layers": L, "experts_per_layer": E, "hidden": D, "inter": MI, "topk": K,
+                   "parallelism": "ep1",
+                   "l2": "no flush: each layer reads ~{:.0f} MB of distinct experts > 126 MB L2".format(layer_bytes / 1e6)},
+        "layer_ms": ms / L,
+        "layer_hbm_gbs": layer_bytes / (ms / L / 1e3) / 1e9,
+        "layer_int8_tops": 2 * S * K * MACS_PER_PAIR / (ms / L / 1e3) / 1e12,
+        "stage_ms_per_layer": {"quant_route": stage_ms[0], "gate_up": stage_ms[1], "down": stage_ms[2]},
+        "roofline": {"kernel": "k_gemm<q4_0,64,EPI_GATEUP> (gate/up GEMM + GeGLU + requant)", "bound": "hbm",
+                     "achieved": achieved, "peak": hbm_peak, "unit": "GB/s", "frac": achieved / hbm_peak,
+                     "peak_source": peak_src, "traffic": None,
+                     "algorithmic_bytes_per_launch": gu_bytes},
+        "clocks": clk.summary(),
+        "gpu_launches": (a.steps) * L * 4,
+    }
+    # ---- e2e: the same stack through the host-buffer plugin path (pinned copies in the timed region)
+    Xh = torch.from_numpy(synth.gaussian(7, (S, D))).pin_memory()
+    eh = [torch.from_numpy(r[0]).pin_memory() for r in routes]
+    wh = [torch.from_numpy(r[1]).pin_memory() for r in routes]
+    oh = torch.empty((L, S, D), dtype=torch.float32).pin_memory()
+    Xd = torch.empty((S, D), device="cuda")
+    ed = torch.empty((S, K), dtype=torch.int32, device="cuda")
+    wd = torch.empty((S, K), device="cuda")
+
+    def step_e2e():
+        for l in range(L):
+            Xd.copy_(Xh, non_blocking=True)
+            ed.copy_(eh[l], non_blocking=True)
+            wd.copy_(wh[l], non_blocking=True)
+            zz.moe_ffn(banks[l], Xd, ed, wd, zz.ZZ_ACT_GEGLU_TANH, out=out)
+            oh[l].copy_(out, non_blocking=True)
+
+    ms_e2e = timed(torch, step_e2e, max(2, a.steps // 2), 2, stream)
+    line["e2e"] = {"value": S * L / (ms_e2e / 1e3), "unit": "token-layers/s",
+                   "h2d_bytes_per_step": L * (S * D * 4 + S * K * 8), "d2h_bytes_per_step": L * S * D * 4}
+    if not a.no_sub:
+        line["sub"] = sub_benchmarks(zz, torch, synth, stream, banks, hbm_peak)
+    del banks
+    if host0 is not None:
+        line["cpu_baseline"] = cpu_baseline_moe(host0, S, seed=11)
+    print(json.dumps(line), flush=True)
+
+
+def sub_benchmarks(zz, torch, synth, stream, banks, hbm_peak):
+    res = {}
+    # config 1: q4_0 2816x2816 GEMV, 64 stacked distinct matrices per launch (285 MB > L2)
+    G = 64
+    w = torch.randn((G * 2816, 2816), device="cuda") * 0.02
+    Wq = zz.quant_rows(zz.GPU_FMT_Q40, w)
+    del w
+    T = zz.QTensorDev(zz.GPU_FMT_Q40, Wq, G * 2816, 2816)
+    del Wq
+    xq, sx, _ = zz.quant_act(torch.randn((1, 2816), device="cuda"))
+    y = torch.empty((1, G * 2816), device="cuda")
+    ms = timed(torch, lambda: zz.matvec(T, xq, sx, y=y), 20, 5, stream)
+    gbs = G * GEMV_BYTES / (ms / 1e3) / 1e9
+    res["q40_gemv_2816"] = {"unit": "GB/s", "value": gbs, "frac_hbm": gbs / hbm_peak, "us_per_launch": ms * 1e3,
+                            "gemvs_per_launch": G, "bytes_per_gemv": GEMV_BYTES}
+    del T
+    # config 2: decode, M=1, 8 routed experts per layer, over the 30 resident layers
+    L = len(banks)
+    r1 = [synth.zipf_routing(300 + l, 1, E, K)[:2] for l in range(L)]
+    x1 = torch.randn((1, D), device="cuda")
+    e1 = [torch.from_numpy(r[0]).cuda() for r in r1]
+    w1 = [torch.from_numpy(r[1]).cuda() for r in r1]
+    o1 = torch.empty((1, D), device="cuda")
+    for b in banks:
+        b.workspace(1, K)
+
+    def dec():
+        for l in range(L):
+            zz.moe_ffn(banks[l], x1, e1[l], w1[l], zz.ZZ_ACT_GEGLU_TANH, out=o1)
+
+    ms = timed(torch, dec, 10, 3, stream)
+    res["decode_8_experts"] = {"unit": "us per layer", "value": ms * 1e3 / L,
+                               "hbm_gbs": 8 * EXPERT_BYTES / (ms / L / 1e3) / 1e9}
+    # S=4096 prefill layer (compute-bound regime)
+    S4 = 4096
+    r4 = [synth.zipf_routing(400 + l, S4, E, K)[:2] for l in range(2)]
+    X4 = torch.randn((S4, D), device="cuda")
+    e4 = [torch.from_numpy(r[0]).cuda() for r in r4]
+    w4 = [torch.from_numpy(r[1]).cuda() for r in r4]
+    o4 = torch.empty((S4, D), device="cuda")
+
+    def pre():
+        for l in range(2):
+            zz.moe_ffn(banks[l], X4, e4[l], w4[l], zz.ZZ_ACT_GEGLU_TANH, out=o4)
+
+    ms = timed(torch, pre, 5, 2, stream) / 2
+    res["prefill_4096_layer"] = {"unit": "int8 TOPS", "value": 2 * S4 * K * MACS_PER_PAIR / (ms / 1e3) / 1e12,
+                                 "ms_per_layer": ms, "tok_per_s": S4 / (ms / 1e3)}
+    for b in banks[:2]:
+        b._ws = None
+    return res
+
+
+if __name__ == "__main__":
+    main()

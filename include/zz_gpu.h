@@ -1,0 +1,170 @@
+/* zz_gpu.h -- C ABI of libzz_cuda.so, the B200 (sm_100a) backend for zunzuncito's
+ * quantized matrix hot path.
+ *
+ * Two layers:
+ *  1. The reference's backend surface, unchanged in name, signature and 1/0 decline
+ *     convention (reference gpu.h:61-84), so an engine built against gpu.h links this
+ *     library in place of metal.o. Activations cross it as host f32 and are quantized
+ *     ON DEVICE exactly like q40_quant_act (q40.h:124-138); the dots are the integer
+ *     q40_dot / q80_dot / tq2_dot (q40.h:188, 374; tq2.h:134), so results match the
+ *     engines' default int8-activation CPU build.
+ *  2. Device-pointer entry points (zz_*) for callers that keep weights, activations and
+ *     outputs resident in HBM: no host copies, explicit caller-provided workspace, an
+ *     explicit stream (a cudaStream_t passed as void*; NULL = legacy default stream).
+ *
+ * Every entry returns 1 on success and 0 to decline; gpu_last_error() then says why.
+ * There is no CPU fallback inside this library: a decline is the caller's to handle,
+ * as the engines already do for gpu.h (gemma4.c:445, 683).
+ * Not re-entrant: one host thread drives the library, like the reference's backend.
+ */
+#ifndef ZZ_GPU_H
+#define ZZ_GPU_H
+
+#include <stdint.h>
+#include <stddef.h>
+
+/* weight formats; values equal the reference's GPU_FMT_* (gpu.h:49-52) */
+#define GPU_FMT_Q40 1
+#define GPU_FMT_Q80 2
+#define GPU_FMT_TQ2 3
+#define GPU_FMT_Q4A 4
+
+/* gated activations of the routed-expert FFN */
+#define ZZ_ACT_GEGLU_TANH 0   /* gelu_tanh(g)*u            gemma4.c:432-434, 637-644 */
+#define ZZ_ACT_SWIGLU 1       /* silu(g)*u                 lfm25.c:677-730, ling.c:797-850 */
+#define ZZ_ACT_SWIGLU_CLAMP 2 /* silu(min(g,c))*clip(u,+-c) maple.c:653-655, 676-678 */
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---------- 1. the reference backend surface (gpu.h:61-84) ---------- */
+
+/* replaces gpu_init (gpu.h:62): 1 if a CUDA device of compute capability 10.x is
+ * present and the kernels load */
+int gpu_init(void);
+/* replaces gpu_shutdown (gpu.h:63): frees every mapped region and cached plane */
+void gpu_shutdown(void);
+/* replaces gpu_ready (gpu.h:64) */
+int gpu_ready(void);
+/* replaces gpu_name (gpu.h:65) */
+const char *gpu_name(void);
+/* replaces gpu_map (gpu.h:70): registers a caller-owned host region holding weights
+ * in the reference formats. The bytes are copied into HBM at once; each tensor inside
+ * is repacked into structure-of-arrays planes the first time a matmul names it. The
+ * region must not change afterwards unless gpu_unmap is called first. */
+int gpu_map(const void *p, size_t n);
+/* added: forget a region registered by gpu_map (the streaming cache rewrites slots,
+ * gemma4.c:2052-2054). No reference counterpart. */
+int gpu_unmap(const void *p);
+/* replaces gpu_q40_matmul (gpu.h:75): y[S,O] = W[O,I] (q4_0) x[S,I]; host y and x */
+int gpu_q40_matmul(float *y, const uint8_t *W, const float *x, int O, int I, int S);
+/* replaces gpu_matmul (gpu.h:84) for GPU_FMT_Q40, Q80 and TQ2 (W is the whole tq2
+ * tensor, alphas first). GPU_FMT_Q4A declines. I % 32 (q4_0/q8_0) or I % 64 (tq2). */
+int gpu_matmul(int fmt, float *y, const uint8_t *W, const float *x, int O, int I, int S);
+/* added: why the last call declined ("" if it did not). */
+const char *gpu_last_error(void);
+
+/* ---------- 2. device-resident entry points ---------- */
+
+/* One weight tensor [O, I] in HBM as structure-of-arrays planes.
+ *   q4_0: codes = O rows of I/2 bytes (the 16 nibble bytes of each block, in block
+ *         order), scale = O x I/32 fp16 block scales
+ *   q8_0: codes = O rows of I int8,  scale = O x I/32 fp16
+ *   tq2 : codes = O rows of I/4 bytes (the reference packing), scale = O f32 alphas
+ * Row strides are exactly those widths; planes start 256-byte aligned. */
+typedef struct zz_qtensor {
+    int fmt, O, I;
+    const uint8_t *codes;
+    const void *scale;
+} zz_qtensor;
+
+/* device bytes zz_repack_dev needs for one tensor (both planes + alignment) */
+size_t zz_qtensor_bytes(int fmt, int O, int I);
+/* repack a reference-format tensor already in device memory (q40.h / tq2.h layout:
+ * q4_0/q8_0 rows of interleaved 18/34-byte blocks, or the tq2 tensor) into planes
+ * inside dst (zz_qtensor_bytes bytes, 256-aligned) and describe them in *out. */
+int zz_repack_dev(int fmt, const uint8_t *src, int O, int I, void *dst, zz_qtensor *out,
+                  void *stream);
+/* inverse of zz_repack_dev, for checks: planes -> reference layout in dst */
+int zz_unpack_dev(const zz_qtensor *t, uint8_t *dst, void *stream);
+
+/* q4_0 / q8_0 weight quantizer on device, bit-exact with q40_quant_row /
+ * q80_quant_row (q40.h:83-110, 332-350): w [O, I] f32 -> dst in the reference row
+ * layout (O * I/32 blocks of 18 or 34 bytes). fmt = GPU_FMT_Q40 or GPU_FMT_Q80. */
+int zz_quant_rows_dev(int fmt, const float *w, int O, int I, uint8_t *dst, void *stream);
+
+/* replaces q40_quant_act (q40.h:124) and tq2_quant_act (tq2.h:98) for S rows:
+ * x [S, I] f32 -> xq [S, I] int8, sx [S, I/32] f32 and, when sxtot != NULL, the
+ * per-row tq2 offset total Sx (double sum in block order, then rounded to f32). */
+int zz_quant_act_dev(const float *x, int S, int I, int8_t *xq, float *sx, float *sxtot,
+                     void *stream);
+
+/* replaces q40_matvec / q80_matvec (q40.h:308, 456) and the tq2 row loop that maple
+ * runs through w_dot (maple.c:387-398): y[S, O] = W . (xq, sx) for S quantized rows.
+ * sxtot is required for tq2 and ignored otherwise. */
+int zz_matvec_dev(const zz_qtensor *W, const int8_t *xq, const float *sx, const float *sxtot,
+                  float *y, int S, void *stream);
+
+/* per-block integer sums for the bit-exact parity check: out[o, b] = <q_w - 8, q_x>
+ * (q4_0), <q_w, q_x> (q8_0), <c, q_x> with unsigned codes (tq2), for one activation
+ * row (q40.h:162-187, 359-372; tq2.h:116-133). out is [O, I/32] int32. */
+int zz_blocksums_dev(const zz_qtensor *W, const int8_t *xq, int32_t *out, void *stream);
+
+/* The routed experts of one MoE layer, packed for the batch-union FFN.
+ *   gu: gate and up stacked per expert as a [2*inter, hidden] tensor whose rows are
+ *       interleaved in groups of 64 (64 gate rows, then the 64 up rows of the same
+ *       features, ...); dn: down [hidden, inter]. Planes as in zz_qtensor, experts
+ *       contiguous. inter % 64 == 0, hidden % 64 == 0. */
+typedef struct zz_expert_bank {
+    int fmt, n_experts, hidden, inter;
+    const uint8_t *gu_codes;
+    const void *gu_scale;
+    const uint8_t *dn_codes;
+    const void *dn_scale;
+} zz_expert_bank;
+
+size_t zz_expert_bank_bytes(int fmt, int n_experts, int hidden, int inter);
+/* Pack experts from reference expert blobs already in device memory. Blob e starts at
+ * blobs + e * blob_stride and holds [gate | up | down] as the engines' expert files do
+ * (gemma4.c:660, maple.c:616-619): q4_0/q8_0 row tensors, or three tq2 tensors. */
+int zz_expert_bank_pack_dev(int fmt, int n_experts, int hidden, int inter, const uint8_t *blobs,
+                            int64_t blob_stride, void *dst, zz_expert_bank *out, void *stream);
+
+/* workspace bytes zz_moe_ffn_dev needs for S tokens with top-K routing */
+size_t zz_moe_workspace_bytes(const zz_expert_bank *bank, int S, int K);
+
+/* Batch-union routed-expert FFN of one layer: the device counterpart of moe_start's
+ * union + moe_apply_chunk + expert_apply (gemma4.c:618-711, 750-790; maple.c:612-692):
+ *   OUT[s] = sum_k ewt[s,k] * down_e( act( gate_e(q8(X[s])), up_e(q8(X[s])) ) requant )
+ * with e = eidx[s,k]. X [S, hidden] f32, eidx/ewt [S, K], OUT [S, hidden] f32
+ * (overwritten). Each distinct expert's weights are streamed once for all of its
+ * tokens. act is a ZZ_ACT_* value, clamp is used by ZZ_ACT_SWIGLU_CLAMP.
+ * eidx values outside [0, n_experts) decline before any work is launched only when
+ * validate != 0 (it costs a device->host sync); otherwise they are skipped. */
+int zz_moe_ffn_dev(const zz_expert_bank *bank, const float *X, const int32_t *eidx,
+                   const float *ewt, float *OUT, int S, int K, int act, float clamp,
+                   void *workspace, size_t workspace_bytes, int validate, void *stream);
+
+/* Diagnostic: byte offset inside the zz_moe_ffn_dev workspace (same bank, S, K) of
+ *   0 pair_src int32[S*K]  routing slot s*K+k held by each pair row, grouped by expert
+ *   1 pair_w   f32[S*K]    its router weight
+ *   2 hq       int8[S*K][inter]      requantized activation per pair row
+ *   3 hs       f32[S*K][inter/32]    its block scales
+ *   4 n_items  int32                 work items of the last call
+ * so tests can check the gate/up stage bit for bit. (size_t)-1 for an unknown id.
+ * No reference counterpart (the engines keep these in Buf: gemma4.c:2123-2127). */
+size_t zz_moe_workspace_offset(const zz_expert_bank *bank, int S, int K, int which);
+
+/* Diagnostic stage timing, no reference counterpart (the engines print wall-clock
+ * phase times to stderr, gemma4.c:3216). While enabled, every zz_moe_ffn_dev call
+ * records CUDA events on its stream at its stage boundaries; zz_prof_collect waits
+ * for them and returns the summed milliseconds of [quantize + route, gate/up GEMM,
+ * down GEMM] and the number of calls, then forgets them. */
+int zz_prof_enable(int on);
+int zz_prof_collect(float *stage_ms, int *calls);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* ZZ_GPU_H */

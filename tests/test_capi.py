@@ -1,0 +1,63 @@
+"""The C-ABI library without a GPU: it loads, exports every entry point that
+include/zz_gpu.h declares, and declines cleanly (0 + a reason) when there is no device."""
+import ctypes
+import os
+import re
+
+import pytest
+import torch
+
+import zunzuncito_b200 as zz
+
+HDR = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "include", "zz_gpu.h")
+
+
+def declared_symbols():
+    txt = open(HDR).read()
+    txt = re.sub(r"/\*.*?\*/", "", txt, flags=re.S)
+    return sorted(set(re.findall(r"\b((?:gpu|zz)_\w+)\s*\(", txt)))
+
+
+def test_header_symbols_exported():
+    lib = ctypes.CDLL(zz.LIB_PATH)
+    syms = declared_symbols()
+    assert len(syms) >= 20
+    missing = [s for s in syms if not hasattr(lib, s)]
+    assert not missing, missing
+
+
+def test_python_prototypes_cover_header():
+    names = {p[0] for p in zz._PROTOS}
+    assert set(declared_symbols()) <= names
+
+
+def test_library_is_sm100a():
+    data = open(zz.LIB_PATH, "rb").read()
+    assert b"sm_100a" in data
+
+
+@pytest.mark.skipif(torch.cuda.is_available(), reason="checks the no-device decline")
+def test_declines_without_device():
+    assert zz.lib.gpu_init() == 0
+    assert zz.lib.gpu_ready() == 0
+    assert len(zz.lib.gpu_last_error()) > 0
+    y = (ctypes.c_float * 4)()
+    assert zz.lib.gpu_matmul(1, y, None, None, 4, 32, 1) == 0
+    assert zz.lib.gpu_name() == b"none"
+
+
+def test_size_queries_host_only():
+    assert zz.lib.zz_qtensor_bytes(zz.GPU_FMT_Q40, 2816, 2816) >= 2816 * 1408 + 2816 * 88 * 2
+    assert zz.lib.zz_qtensor_bytes(zz.GPU_FMT_TQ2, 10, 96) == 0   # tq2 needs I % 64
+    assert zz.lib.zz_qtensor_bytes(zz.GPU_FMT_Q4A, 10, 64) == 0
+    assert zz.lib.zz_expert_bank_bytes(zz.GPU_FMT_Q40, 128, 2816, 704) > 128 * 3345408 * 0.99
+    assert zz.lib.zz_expert_bank_bytes(zz.GPU_FMT_Q40, 128, 2816, 700) == 0  # inter % 64
+    b = zz.ExpertBank(zz.GPU_FMT_Q40, 128, 2816, 704, None, None, None, None)
+    assert zz.lib.zz_moe_workspace_bytes(ctypes.byref(b), 512, 8) > 512 * 8 * 704
+
+
+def test_bad_arguments_decline_before_device_work():
+    t = zz.QTensor(zz.GPU_FMT_Q40, 16, 33, None, None)
+    assert zz.lib.zz_matvec_dev(ctypes.byref(t), None, None, None, None, 1, None) == 0
+    assert b"invalid" in zz.lib.gpu_last_error()
+    assert zz.lib.zz_quant_act_dev(None, 1, 48, None, None, None, None) == 0

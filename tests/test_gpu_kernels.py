@@ -1,0 +1,162 @@
+"""CUDA kernels through the C ABI against the oracle: quantizers and per-block integer
+sums bit-exact, fp32 matvec outputs within 1e-4 of max|y| (the tolerance BASELINE
+states; accumulation order differs), the gpu.h host surface, and declines."""
+import ctypes
+
+import numpy as np
+import pytest
+import torch
+
+import zunzuncito_b200 as zz
+from zunzuncito_b200 import synth
+
+pytestmark = pytest.mark.gpu
+
+TOL = 1e-4  # max |y - y_ref| / max |y_ref|
+
+
+@pytest.fixture(scope="module", autouse=True)
+def _device():
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    torch.cuda.init()
+    yield
+    torch.cuda.synchronize()
+
+
+def dev(a):
+    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+
+
+def rel(a, b):
+    return float(np.max(np.abs(np.asarray(a, np.float64) - b)) / (np.max(np.abs(b)) + 1e-30))
+
+
+def q_weights(orc, fmt, seed, O, I):
+    if fmt == zz.GPU_FMT_TQ2:
+        return synth.tq2_tensor(seed, O, I)
+    w = synth.gaussian(seed, (O, I), 0.02)
+    return (orc.q40_quant_rows(w) if fmt == zz.GPU_FMT_Q40 else orc.q80_quant_rows(w)).reshape(-1)
+
+
+def oracle_matvec(orc, fmt, Wb, O, I, xq, sx, tot):
+    if fmt == zz.GPU_FMT_Q40:
+        return orc.q40_matvec(Wb.reshape(O, -1), xq, sx)
+    if fmt == zz.GPU_FMT_Q80:
+        return orc.q80_matvec(Wb.reshape(O, -1), xq, sx)
+    return orc.tq2_matvec(Wb, O, xq, sx, tot)
+
+
+def test_quant_act_bit_exact(orc):
+    x = synth.gaussian(21, (9, 2816))
+    x[1, :64] = 0.0
+    x[2, 5] = 1e-30
+    x[3, :32] = np.arange(32, dtype=np.float32) - 15.5          # exact .5 ties
+    x[4, :32] = np.float32(3.0) * (np.arange(32) % 3 - 1)
+    xq, sx, tot = zz.quant_act(dev(x), want_sxtot=True)
+    exq, esx, etot = orc.tq2_quant_act(x)
+    assert np.array_equal(xq.cpu().numpy(), exq)
+    assert np.array_equal(sx.cpu().numpy(), esx)
+    assert np.array_equal(tot.cpu().numpy(), etot)
+
+
+@pytest.mark.parametrize("fmt", [zz.GPU_FMT_Q40, zz.GPU_FMT_Q80])
+@pytest.mark.parametrize("scale", [0.02, 1.0, 1e-6])
+def test_quant_rows_bit_exact(orc, fmt, scale):
+    w = synth.gaussian(22, (37, 704), scale)
+    w[0, :32] = 0.0
+    w[1, :32] = 0.5; w[1, 7] = -0.5
+    got = zz.quant_rows(fmt, dev(w)).cpu().numpy().reshape(37, -1)
+    want = orc.q40_quant_rows(w) if fmt == zz.GPU_FMT_Q40 else orc.q80_quant_rows(w)
+    assert np.array_equal(got, want)
+
+
+@pytest.mark.parametrize("fmt,O,I", [(zz.GPU_FMT_Q40, 37, 704), (zz.GPU_FMT_Q80, 19, 96), (zz.GPU_FMT_TQ2, 33, 128)])
+def test_repack_roundtrip(orc, fmt, O, I):
+    Wb = q_weights(orc, fmt, 23, O, I)
+    t = zz.QTensorDev(fmt, dev(Wb), O, I)
+    assert np.array_equal(t.unpack().cpu().numpy(), Wb)
+
+
+@pytest.mark.parametrize("fmt,O,I", [(zz.GPU_FMT_Q40, 64, 2816), (zz.GPU_FMT_Q80, 40, 704), (zz.GPU_FMT_TQ2, 48, 2048)])
+def test_blocksums_bit_exact(orc, fmt, O, I):
+    Wb = q_weights(orc, fmt, 24, O, I)
+    x = synth.gaussian(25, (1, I))
+    xq, sx = orc.quant_act(x)
+    t = zz.QTensorDev(fmt, dev(Wb), O, I)
+    got = zz.blocksums(t, dev(xq[0])).cpu().numpy()
+    Wrows = Wb[4 * O:].reshape(O, -1) if fmt == zz.GPU_FMT_TQ2 else Wb.reshape(O, -1)
+    assert np.array_equal(got, orc.blocksums(fmt, Wrows, xq[0]))
+
+
+@pytest.mark.parametrize("fmt,O,I", [
+    (zz.GPU_FMT_Q40, 2816, 2816),
+    (zz.GPU_FMT_Q40, 1, 32), (zz.GPU_FMT_Q40, 37, 704), (zz.GPU_FMT_Q40, 5, 8192), (zz.GPU_FMT_Q40, 9, 8224),
+    (zz.GPU_FMT_Q80, 2816, 2816), (zz.GPU_FMT_Q80, 3, 96),
+    (zz.GPU_FMT_TQ2, 512, 2048), (zz.GPU_FMT_TQ2, 2048, 512), (zz.GPU_FMT_TQ2, 7, 64), (zz.GPU_FMT_TQ2, 3, 8192 + 64),
+])
+def test_matvec_one_row(orc, fmt, O, I):
+    Wb = q_weights(orc, fmt, 26, O, I)
+    x = synth.gaussian(27, (1, I))
+    xq, sx, tot = orc.tq2_quant_act(x)
+    t = zz.QTensorDev(fmt, dev(Wb), O, I)
+    y = zz.matvec(t, dev(xq), dev(sx), dev(tot)).cpu().numpy()[0]
+    assert rel(y, oracle_matvec(orc, fmt, Wb, O, I, xq[0], sx[0], tot[0])) < TOL
+
+
+@pytest.mark.parametrize("fmt", [zz.GPU_FMT_Q40, zz.GPU_FMT_Q80, zz.GPU_FMT_TQ2])
+@pytest.mark.parametrize("S,O,I", [(2, 128, 256), (3, 200, 704), (17, 2816, 2816), (65, 130, 2048), (130, 64, 512)])
+def test_matvec_many_rows(orc, fmt, S, O, I):
+    Wb = q_weights(orc, fmt, 28, O, I)
+    x = synth.gaussian(29, (S, I))
+    xq, sx, tot = orc.tq2_quant_act(x)
+    t = zz.QTensorDev(fmt, dev(Wb), O, I)
+    y = zz.matvec(t, dev(xq), dev(sx), dev(tot)).cpu().numpy()
+    for s in range(S):
+        assert rel(y[s], oracle_matvec(orc, fmt, Wb, O, I, xq[s], sx[s], tot[s])) < TOL, s
+
+
+def test_gpu_h_surface(orc):
+    """gpu_init / gpu_map / gpu_matmul exactly as an engine calls them (gemma4.c:445)."""
+    L = zz.lib
+    assert L.gpu_init() == 1, L.gpu_last_error()
+    assert L.gpu_ready() == 1
+    assert b"B200" in L.gpu_name() or b"sm_10" in L.gpu_name()
+    O, I = 300, 2816
+    W4 = q_weights(orc, zz.GPU_FMT_Q40, 30, O, I)
+    W8 = q_weights(orc, zz.GPU_FMT_Q80, 31, O, I)
+    T2 = q_weights(orc, zz.GPU_FMT_TQ2, 32, O, 2048)
+    # one page-aligned region holding all three tensors, like the dense blob
+    region = np.zeros(((W4.size + W8.size + T2.size) // 4096 + 2) * 4096, np.uint8)
+    region[:W4.size] = W4
+    region[W4.size:W4.size + W8.size] = W8
+    o2 = W4.size + W8.size
+    region[o2:o2 + T2.size] = T2
+    base = region.ctypes.data
+    assert L.gpu_map(ctypes.c_void_p(base), region.size) == 1, L.gpu_last_error()
+    for S in (1, 3):
+        x = synth.gaussian(33 + S, (S, I))
+        y = np.zeros((S, O), np.float32)
+        assert L.gpu_q40_matmul(y.ctypes.data, ctypes.c_void_p(base), x.ctypes.data, O, I, S) == 1, L.gpu_last_error()
+        xq, sx = orc.quant_act(x)
+        for s in range(S):
+            assert rel(y[s], orc.q40_matvec(W4.reshape(O, -1), xq[s], sx[s])) < TOL
+        y8 = np.zeros((S, O), np.float32)
+        assert L.gpu_matmul(zz.GPU_FMT_Q80, y8.ctypes.data, ctypes.c_void_p(base + W4.size), x.ctypes.data, O, I, S) == 1
+        for s in range(S):
+            assert rel(y8[s], orc.q80_matvec(W8.reshape(O, -1), xq[s], sx[s])) < TOL
+        xt = synth.gaussian(40 + S, (S, 2048))
+        yt = np.zeros((S, O), np.float32)
+        assert L.gpu_matmul(zz.GPU_FMT_TQ2, yt.ctypes.data, ctypes.c_void_p(base + o2), xt.ctypes.data, O, 2048, S) == 1
+        tq, ts, tt = orc.tq2_quant_act(xt)
+        for s in range(S):
+            assert rel(yt[s], orc.tq2_matvec(T2, O, tq[s], ts[s], tt[s])) < TOL
+    # declines: q4a, bad shape, unmapped pointer
+    y = np.zeros(8, np.float32)
+    assert L.gpu_matmul(zz.GPU_FMT_Q4A, y.ctypes.data, ctypes.c_void_p(base), y.ctypes.data, 8, 64, 1) == 0
+    assert L.gpu_matmul(zz.GPU_FMT_Q40, y.ctypes.data, ctypes.c_void_p(base), y.ctypes.data, 8, 48, 1) == 0
+    other = np.zeros(4096, np.uint8)
+    assert L.gpu_q40_matmul(y.ctypes.data, other.ctypes.data, y.ctypes.data, 1, 32, 1) == 0
+    assert b"gpu_map" in L.gpu_last_error()
+    assert L.gpu_unmap(ctypes.c_void_p(base)) == 1
+    assert L.gpu_q40_matmul(y.ctypes.data, ctypes.c_void_p(base), y.ctypes.data, 1, 32, 1) == 0

@@ -1,0 +1,91 @@
+"""zunzuncito_b200 -- B200 (sm_100a) backend for zunzuncito's quantized matrix hot path.
+
+The product is the C-ABI shared library ``libzz_cuda.so`` built from ``csrc/`` (its
+interface is ``include/zz_gpu.h``). This package only loads it and gives Python callers
+(tests, the benchmark, host-side plumbing such as the expert-parallel exchange) typed
+access to it. There is no CPU fallback: if the library is missing, importing the
+package raises.
+"""
+import ctypes
+import os
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "libzz_cuda.so")
+
+GPU_FMT_Q40, GPU_FMT_Q80, GPU_FMT_TQ2, GPU_FMT_Q4A = 1, 2, 3, 4
+ZZ_ACT_GEGLU_TANH, ZZ_ACT_SWIGLU, ZZ_ACT_SWIGLU_CLAMP = 0, 1, 2
+
+c_void_p, c_int, c_size_t, c_float, c_int64 = (ctypes.c_void_p, ctypes.c_int, ctypes.c_size_t,
+                                               ctypes.c_float, ctypes.c_int64)
+
+
+class QTensor(ctypes.Structure):
+    """zz_qtensor: one weight tensor as structure-of-arrays planes in HBM."""
+    _fields_ = [("fmt", c_int), ("O", c_int), ("I", c_int), ("codes", c_void_p), ("scale", c_void_p)]
+
+
+class ExpertBank(ctypes.Structure):
+    """zz_expert_bank: one MoE layer's routed experts, packed for the batch-union FFN."""
+    _fields_ = [("fmt", c_int), ("n_experts", c_int), ("hidden", c_int), ("inter", c_int),
+                ("gu_codes", c_void_p), ("gu_scale", c_void_p), ("dn_codes", c_void_p),
+                ("dn_scale", c_void_p)]
+
+
+# (name, restype, argtypes): every entry point of include/zz_gpu.h
+_PROTOS = [
+    ("gpu_init", c_int, []),
+    ("gpu_shutdown", None, []),
+    ("gpu_ready", c_int, []),
+    ("gpu_name", ctypes.c_char_p, []),
+    ("gpu_map", c_int, [c_void_p, c_size_t]),
+    ("gpu_unmap", c_int, [c_void_p]),
+    ("gpu_q40_matmul", c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int, c_int]),
+    ("gpu_matmul", c_int, [c_int, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int]),
+    ("gpu_last_error", ctypes.c_char_p, []),
+    ("zz_qtensor_bytes", c_size_t, [c_int, c_int, c_int]),
+    ("zz_repack_dev", c_int, [c_int, c_void_p, c_int, c_int, c_void_p, ctypes.POINTER(QTensor), c_void_p]),
+    ("zz_unpack_dev", c_int, [ctypes.POINTER(QTensor), c_void_p, c_void_p]),
+    ("zz_quant_rows_dev", c_int, [c_int, c_void_p, c_int, c_int, c_void_p, c_void_p]),
+    ("zz_quant_act_dev", c_int, [c_void_p, c_int, c_int, c_void_p, c_void_p, c_void_p, c_void_p]),
+    ("zz_matvec_dev", c_int, [ctypes.POINTER(QTensor), c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_void_p]),
+    ("zz_blocksums_dev", c_int, [ctypes.POINTER(QTensor), c_void_p, c_void_p, c_void_p]),
+    ("zz_expert_bank_bytes", c_size_t, [c_int, c_int, c_int, c_int]),
+    ("zz_expert_bank_pack_dev", c_int, [c_int, c_int, c_int, c_int, c_void_p, c_int64, c_void_p,
+                                        ctypes.POINTER(ExpertBank), c_void_p]),
+    ("zz_moe_workspace_bytes", c_size_t, [ctypes.POINTER(ExpertBank), c_int, c_int]),
+    ("zz_moe_workspace_offset", c_size_t, [ctypes.POINTER(ExpertBank), c_int, c_int, c_int]),
+    ("zz_prof_enable", c_int, [c_int]),
+    ("zz_prof_collect", c_int, [ctypes.POINTER(c_float), ctypes.POINTER(c_int)]),
+    ("zz_moe_ffn_dev", c_int, [ctypes.POINTER(ExpertBank), c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int,
+                               c_int, c_float, c_void_p, c_size_t, c_int, c_void_p]),
+]
+
+
+def _load():
+    if not os.path.exists(LIB_PATH):
+        raise ImportError(f"{LIB_PATH} is missing: run `python zunzuncito_b200/build.py` "
+                          "(this package has no CPU fallback)")
+    lib = ctypes.CDLL(LIB_PATH)
+    for name, res, args in _PROTOS:
+        fn = getattr(lib, name)
+        fn.restype = res
+        fn.argtypes = args
+    return lib
+
+
+lib = _load()
+
+
+class ZZError(RuntimeError):
+    pass
+
+
+def check(ok, what=""):
+    """Raise with gpu_last_error() when an entry point declined (returned 0)."""
+    if not ok:
+        msg = lib.gpu_last_error().decode()
+        raise ZZError(f"{what}: {msg}" if what else msg)
+    return ok
+
+
+from .api import *  # noqa: E402,F401,F403

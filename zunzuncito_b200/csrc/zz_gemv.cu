@@ -1,0 +1,267 @@
+// zz_gemv.cu -- decode (one activation row) matvec for q4_0 / q8_0 / tq2 planes, and
+// the per-block integer-sum kernel used for bit-exact parity checks.
+//
+// HBM-bound by construction: 18 (q4_0) / 34 (q8_0) / 8 (tq2) bytes per 32 weights,
+// against 8 dp4a per block. Layout on chip: one warp per weight row; lane l owns the
+// blocks b = l, l+32, l+64, ... of EVERY row, so its slice of the quantized activation
+// is loaded into registers once and reused for all rows the warp visits. Weight codes
+// stream with 16-byte L1-bypassing loads (a warp reads 512 contiguous bytes per step);
+// two rows are in flight per warp to cover HBM latency.
+#include "zz_common.cuh"
+
+namespace zz {
+
+// q4_0 block . q8_0 activation block, <q-8, x> (q40.h:162-187)
+__device__ __forceinline__ int q40_block_dot(uint4 w, const uint32_t x[8]) {
+    int s = 0;
+    s = dp4a_ss((int)nib_to_s8(w.x), (int)x[0], s);
+    s = dp4a_ss((int)nib_to_s8(w.y), (int)x[1], s);
+    s = dp4a_ss((int)nib_to_s8(w.z), (int)x[2], s);
+    s = dp4a_ss((int)nib_to_s8(w.w), (int)x[3], s);
+    s = dp4a_ss((int)nib_to_s8(w.x >> 4), (int)x[4], s);
+    s = dp4a_ss((int)nib_to_s8(w.y >> 4), (int)x[5], s);
+    s = dp4a_ss((int)nib_to_s8(w.z >> 4), (int)x[6], s);
+    s = dp4a_ss((int)nib_to_s8(w.w >> 4), (int)x[7], s);
+    return s;
+}
+// q8_0 block . activation block (q40.h:359-372)
+__device__ __forceinline__ int q80_block_dot(uint4 a, uint4 b, const uint32_t x[8]) {
+    int s = 0;
+    s = dp4a_ss((int)a.x, (int)x[0], s); s = dp4a_ss((int)a.y, (int)x[1], s);
+    s = dp4a_ss((int)a.z, (int)x[2], s); s = dp4a_ss((int)a.w, (int)x[3], s);
+    s = dp4a_ss((int)b.x, (int)x[4], s); s = dp4a_ss((int)b.y, (int)x[5], s);
+    s = dp4a_ss((int)b.z, (int)x[6], s); s = dp4a_ss((int)b.w, (int)x[7], s);
+    return s;
+}
+// tq2 64-weight group . two activation blocks: unsigned codes, <c, x> per block
+// (tq2.h:116-133); x holds 16 words (blocks 2g, 2g+1)
+__device__ __forceinline__ void tq2_group_dot(uint4 c, const uint32_t x[16], int &s0, int &s1) {
+    const uint32_t m = 0x03030303u;
+    s0 = 0; s1 = 0;
+    s0 = dp4a_ss((int)(c.x & m), (int)x[0], s0);  s0 = dp4a_ss((int)(c.y & m), (int)x[1], s0);
+    s0 = dp4a_ss((int)(c.z & m), (int)x[2], s0);  s0 = dp4a_ss((int)(c.w & m), (int)x[3], s0);
+    s0 = dp4a_ss((int)((c.x >> 2) & m), (int)x[4], s0);  s0 = dp4a_ss((int)((c.y >> 2) & m), (int)x[5], s0);
+    s0 = dp4a_ss((int)((c.z >> 2) & m), (int)x[6], s0);  s0 = dp4a_ss((int)((c.w >> 2) & m), (int)x[7], s0);
+    s1 = dp4a_ss((int)((c.x >> 4) & m), (int)x[8], s1);  s1 = dp4a_ss((int)((c.y >> 4) & m), (int)x[9], s1);
+    s1 = dp4a_ss((int)((c.z >> 4) & m), (int)x[10], s1); s1 = dp4a_ss((int)((c.w >> 4) & m), (int)x[11], s1);
+    s1 = dp4a_ss((int)((c.x >> 6) & m), (int)x[12], s1); s1 = dp4a_ss((int)((c.y >> 6) & m), (int)x[13], s1);
+    s1 = dp4a_ss((int)((c.z >> 6) & m), (int)x[14], s1); s1 = dp4a_ss((int)((c.w >> 6) & m), (int)x[15], s1);
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+// q4_0 / q8_0 decode matvec. NBL = blocks per lane (ceil(nb/32)).
+template <int FMT, int NBL>
+__global__ void __launch_bounds__(256) k_gemv_q(const uint8_t *__restrict__ codes, const __half *__restrict__ scale,
+                                                int O, int I, const int8_t *__restrict__ xq,
+                                                const float *__restrict__ sx, float *__restrict__ y) {
+    const int lane = threadIdx.x & 31;
+    const int nb = I / ZZ_BLK, nbp = (nb + 7) & ~7;
+    const int CB = FMT == GPU_FMT_Q40 ? 16 : 32;
+    uint32_t xr[NBL][8];
+    float xs[NBL];
+#pragma unroll
+    for (int i = 0; i < NBL; i++) {
+        int b = lane + 32 * i;
+        if (b < nb) {
+            const uint4 *p = reinterpret_cast<const uint4 *>(xq + (size_t)b * ZZ_BLK);
+            uint4 lo = p[0], hi = p[1];
+            xr[i][0] = lo.x; xr[i][1] = lo.y; xr[i][2] = lo.z; xr[i][3] = lo.w;
+            xr[i][4] = hi.x; xr[i][5] = hi.y; xr[i][6] = hi.z; xr[i][7] = hi.w;
+            xs[i] = sx[b];
+        } else {
+#pragma unroll
+            for (int k = 0; k < 8; k++) xr[i][k] = 0;
+            xs[i] = 0.f;
+        }
+    }
+    const int warps = (gridDim.x * blockDim.x) >> 5;
+    const int w0 = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const size_t rowb = (size_t)nb * CB;
+    for (int o = w0 * 2; o < O; o += warps * 2) {
+        const bool two = o + 1 < O;
+        uint4 wa[NBL], wb[NBL], wa2[NBL], wb2[NBL];
+        float da[NBL], db[NBL];
+#pragma unroll
+        for (int i = 0; i < NBL; i++) {
+            int b = lane + 32 * i;
+            if (b < nb) {
+                const uint8_t *pa = codes + (size_t)o * rowb + (size_t)b * CB;
+                wa[i] = ldg_stream(pa);
+                if (FMT == GPU_FMT_Q80) wa2[i] = ldg_stream(pa + 16);
+                da[i] = __half2float(scale[(size_t)o * nbp + b]);
+                if (two) {
+                    wb[i] = ldg_stream(pa + rowb);
+                    if (FMT == GPU_FMT_Q80) wb2[i] = ldg_stream(pa + rowb + 16);
+                    db[i] = __half2float(scale[(size_t)(o + 1) * nbp + b]);
+                }
+            }
+        }
+        float acc_a = 0.f, acc_b = 0.f;
+#pragma unroll
+        for (int i = 0; i < NBL; i++) {
+            int b = lane + 32 * i;
+            if (b < nb) {
+                int sa = FMT == GPU_FMT_Q40 ? q40_block_dot(wa[i], xr[i]) : q80_block_dot(wa[i], wa2[i], xr[i]);
+                acc_a = fmaf(da[i] * xs[i], (float)sa, acc_a);
+                if (two) {
+                    int sb = FMT == GPU_FMT_Q40 ? q40_block_dot(wb[i], xr[i]) : q80_block_dot(wb[i], wb2[i], xr[i]);
+                    acc_b = fmaf(db[i] * xs[i], (float)sb, acc_b);
+                }
+            }
+        }
+        acc_a = warp_sum(acc_a);
+        acc_b = warp_sum(acc_b);
+        if (lane == 0) {
+            y[o] = acc_a;
+            if (two) y[o + 1] = acc_b;
+        }
+    }
+}
+
+// tq2 decode matvec: lane owns 64-weight groups g = lane + 32 i; y = alpha*(acc - Sx)
+template <int NGL>
+__global__ void __launch_bounds__(256) k_gemv_tq2(const uint8_t *__restrict__ codes, const float *__restrict__ alpha,
+                                                  int O, int I, const int8_t *__restrict__ xq,
+                                                  const float *__restrict__ sx, const float *__restrict__ sxtot,
+                                                  float *__restrict__ y) {
+    const int lane = threadIdx.x & 31;
+    const int ng = I / 64;
+    uint32_t xr[NGL][16];
+    float xs0[NGL], xs1[NGL];
+#pragma unroll
+    for (int i = 0; i < NGL; i++) {
+        int g = lane + 32 * i;
+        if (g < ng) {
+            const uint4 *p = reinterpret_cast<const uint4 *>(xq + (size_t)g * 64);
+#pragma unroll
+            for (int k = 0; k < 4; k++) {
+                uint4 v = p[k];
+                xr[i][4 * k] = v.x; xr[i][4 * k + 1] = v.y; xr[i][4 * k + 2] = v.z; xr[i][4 * k + 3] = v.w;
+            }
+            xs0[i] = sx[2 * g]; xs1[i] = sx[2 * g + 1];
+        } else {
+#pragma unroll
+            for (int k = 0; k < 16; k++) xr[i][k] = 0;
+            xs0[i] = xs1[i] = 0.f;
+        }
+    }
+    const float tot = sxtot[0];
+    const int warps = (gridDim.x * blockDim.x) >> 5;
+    const int w0 = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const size_t rowb = (size_t)I / 4;
+    for (int o = w0 * 2; o < O; o += warps * 2) {
+        const bool two = o + 1 < O;
+        uint4 ca[NGL], cb[NGL];
+#pragma unroll
+        for (int i = 0; i < NGL; i++) {
+            int g = lane + 32 * i;
+            if (g < ng) {
+                ca[i] = ldg_stream(codes + (size_t)o * rowb + (size_t)g * 16);
+                if (two) cb[i] = ldg_stream(codes + (size_t)(o + 1) * rowb + (size_t)g * 16);
+            }
+        }
+        float acc_a = 0.f, acc_b = 0.f;
+#pragma unroll
+        for (int i = 0; i < NGL; i++) {
+            int g = lane + 32 * i;
+            if (g < ng) {
+                int s0, s1;
+                tq2_group_dot(ca[i], xr[i], s0, s1);
+                acc_a = fmaf(xs0[i], (float)s0, acc_a);
+                acc_a = fmaf(xs1[i], (float)s1, acc_a);
+                if (two) {
+                    tq2_group_dot(cb[i], xr[i], s0, s1);
+                    acc_b = fmaf(xs0[i], (float)s0, acc_b);
+                    acc_b = fmaf(xs1[i], (float)s1, acc_b);
+                }
+            }
+        }
+        acc_a = warp_sum(acc_a);
+        acc_b = warp_sum(acc_b);
+        if (lane == 0) {
+            y[o] = alpha[o] * (acc_a - tot);
+            if (two) y[o + 1] = alpha[o + 1] * (acc_b - tot);
+        }
+    }
+}
+
+// per-block integer sums, one thread per (row, block): the bit-exact parity quantity
+template <int FMT>
+__global__ void k_blocksums(const uint8_t *__restrict__ codes, int O, int I, const int8_t *__restrict__ xq,
+                            int32_t *__restrict__ out) {
+    const int nb = I / ZZ_BLK;
+    long t = (long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (t >= (long)O * nb) return;
+    int o = (int)(t / nb), b = (int)(t % nb);
+    const int8_t *x = xq + (size_t)b * ZZ_BLK;
+    int s = 0;
+    if (FMT == GPU_FMT_Q40) {
+        const uint8_t *c = codes + (size_t)o * (I / 2) + (size_t)b * 16;
+        for (int j = 0; j < 16; j++) s += ((c[j] & 15) - 8) * x[j] + ((c[j] >> 4) - 8) * x[j + 16];
+    } else if (FMT == GPU_FMT_Q80) {
+        const int8_t *c = reinterpret_cast<const int8_t *>(codes) + (size_t)o * I + (size_t)b * 32;
+        for (int j = 0; j < 32; j++) s += c[j] * x[j];
+    } else {
+        const uint8_t *c = codes + (size_t)o * (I / 4) + (size_t)(b / 2) * 16;
+        int sh = (b & 1) * 4;
+        for (int k = 0; k < 16; k++)
+            s += ((c[k] >> sh) & 3) * x[k] + ((c[k] >> (sh + 2)) & 3) * x[k + 16];
+    }
+    out[t] = s;
+}
+
+static int gemv_grid(int O) {
+    int g = (O + 15) / 16;  // 8 warps x 2 rows
+    int cap = 148 * 8;
+    return g < cap ? g : cap;
+}
+
+// one activation row; returns 0 if the shape has no fast-path instantiation
+int launch_gemv1(const zz_qtensor *W, const int8_t *xq, const float *sx, const float *sxtot, float *y,
+                 cudaStream_t st) {
+    const int O = W->O, I = W->I, grid = gemv_grid(O);
+    if (W->fmt == GPU_FMT_TQ2) {
+        int ngl = (I / 64 + 31) / 32;
+        switch (ngl) {
+#define ZZ_T(N) case N: k_gemv_tq2<N><<<grid, 256, 0, st>>>(W->codes, (const float *)W->scale, O, I, xq, sx, sxtot, y); break;
+            ZZ_T(1) ZZ_T(2) ZZ_T(3) ZZ_T(4)
+#undef ZZ_T
+            default: return 0;
+        }
+    } else {
+        int nbl = (I / 32 + 31) / 32;
+        const __half *sc = (const __half *)W->scale;
+        if (W->fmt == GPU_FMT_Q40) {
+            switch (nbl) {
+#define ZZ_Q(N) case N: k_gemv_q<GPU_FMT_Q40, N><<<grid, 256, 0, st>>>(W->codes, sc, O, I, xq, sx, y); break;
+                ZZ_Q(1) ZZ_Q(2) ZZ_Q(3) ZZ_Q(4) ZZ_Q(5) ZZ_Q(6) ZZ_Q(7) ZZ_Q(8)
+#undef ZZ_Q
+                default: return 0;
+            }
+        } else {
+            switch (nbl) {
+#define ZZ_Q(N) case N: k_gemv_q<GPU_FMT_Q80, N><<<grid, 256, 0, st>>>(W->codes, sc, O, I, xq, sx, y); break;
+                ZZ_Q(1) ZZ_Q(2) ZZ_Q(3) ZZ_Q(4) ZZ_Q(5) ZZ_Q(6) ZZ_Q(7) ZZ_Q(8)
+#undef ZZ_Q
+                default: return 0;
+            }
+        }
+    }
+    return check_cuda(cudaGetLastError(), "gemv launch") ? 1 : -1;
+}
+
+int launch_blocksums(const zz_qtensor *W, const int8_t *xq, int32_t *out, cudaStream_t st) {
+    long n = (long)W->O * (W->I / ZZ_BLK);
+    unsigned grid = (unsigned)((n + 255) / 256);
+    if (W->fmt == GPU_FMT_Q40) k_blocksums<GPU_FMT_Q40><<<grid, 256, 0, st>>>(W->codes, W->O, W->I, xq, out);
+    else if (W->fmt == GPU_FMT_Q80) k_blocksums<GPU_FMT_Q80><<<grid, 256, 0, st>>>(W->codes, W->O, W->I, xq, out);
+    else k_blocksums<GPU_FMT_TQ2><<<grid, 256, 0, st>>>(W->codes, W->O, W->I, xq, out);
+    return check_cuda(cudaGetLastError(), "blocksums launch");
+}
+
+}  // namespace zz

@@ -1,0 +1,310 @@
+// zz_moe.cu -- dense matvec dispatch, expert-bank packing and the batch-union
+// routed-expert FFN (device counterpart of gemma4.c:618-711 + 750-790 and
+// maple.c:612-692, 738-790).
+//
+// Layer pipeline on one stream, no host round trip:
+//   1. quantize X once per token (the engines re-quantize per (token, expert); the
+//      bytes are identical, gemma4.c:642)
+//   2. route: histogram of expert ids -> offsets -> pair slots grouped by expert, and
+//      the work list of (expert, <=BN pairs) items  -- replaces moe_start's O(S*K*nu)
+//      union scan and moe_apply_chunk's gather (gemma4.c:756-761, 781-783)
+//   3. gate/up GEMM over the interleaved [2*inter, hidden] stack, fused activation and
+//      q8_0 requant of h (gemma4.c:637-644)
+//   4. down GEMM with the router weight and the scatter-add into OUT fused into its
+//      epilogue (gemma4.c:647-651)
+// Each distinct expert's weights cross HBM once per item; items of one expert are
+// adjacent in the grid so repeated reads of the same expert hit L2.
+#include <vector>
+#include "zz_gemm.cuh"
+
+namespace zz {
+
+size_t code_row_bytes(int fmt, int I);
+size_t scale_row_bytes(int fmt, int I);
+size_t ref_tensor_bytes(int fmt, int O, int I);
+size_t codes_bytes(int fmt, int O, int I);
+size_t scales_bytes(int fmt, int O, int I);
+int launch_repack(int fmt, const uint8_t *src, long src_expert_stride, int rows, int I, RowMap map,
+                  uint8_t *codes, void *scale, long dce, long dse, int n_experts, cudaStream_t st);
+int launch_gemv1(const zz_qtensor *W, const int8_t *xq, const float *sx, const float *sxtot, float *y,
+                 cudaStream_t st);
+int launch_blocksums(const zz_qtensor *W, const int8_t *xq, int32_t *out, cudaStream_t st);
+
+constexpr int MOE_BN = 64;
+constexpr int DENSE_BN = 64;
+
+static inline size_t a256(size_t n) { return (n + 255) & ~(size_t)255; }
+
+template <int FMT, int BN, int EPI>
+static int launch_gemm_t(const GemmArgs &a, dim3 grid, cudaStream_t st) {
+    constexpr int smem = GemmSmem<FMT, BN>::TOTAL;
+    static bool attr_set = false;  // per process; the library drives one device
+    if (!attr_set) {
+        if (!check_cuda(cudaFuncSetAttribute(k_gemm<FMT, BN, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem),
+                        "gemm smem attribute"))
+            return 0;
+        attr_set = true;
+    }
+    k_gemm<FMT, BN, EPI><<<grid, G_THREADS, smem, st>>>(a);
+    return check_cuda(cudaGetLastError(), "gemm launch");
+}
+
+template <int EPI, int BN>
+static int launch_gemm(int fmt, const GemmArgs &a, dim3 grid, cudaStream_t st) {
+    if (fmt == GPU_FMT_Q40) return launch_gemm_t<GPU_FMT_Q40, BN, EPI>(a, grid, st);
+    if (fmt == GPU_FMT_Q80) return launch_gemm_t<GPU_FMT_Q80, BN, EPI>(a, grid, st);
+    return launch_gemm_t<GPU_FMT_TQ2, BN, EPI>(a, grid, st);
+}
+
+// ---------------------------------------------------------------- routing
+// One CTA. Pairs p = s*K + k with a valid expert go to slot off[e] + rank; the rank
+// order inside an expert is arbitrary (each pair's result is independent of its slot).
+__global__ void __launch_bounds__(1024) k_route(const int32_t *__restrict__ eidx, const float *__restrict__ ewt,
+                                                int P, int E, int BN, int *__restrict__ pair_src,
+                                                float *__restrict__ pair_w, WorkItem *__restrict__ items,
+                                                int *__restrict__ n_items) {
+    extern __shared__ int sh[];
+    int *cnt = sh, *off = sh + E, *ioff = sh + 2 * E, *cur = sh + 3 * E;
+    for (int e = threadIdx.x; e < E; e += blockDim.x) { cnt[e] = 0; cur[e] = 0; }
+    __syncthreads();
+    for (int p = threadIdx.x; p < P; p += blockDim.x) {
+        int e = eidx[p];
+        if (e >= 0 && e < E) atomicAdd(&cnt[e], 1);
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        int o = 0, io = 0;
+        for (int e = 0; e < E; e++) {
+            off[e] = o; ioff[e] = io;
+            o += cnt[e];
+            io += (cnt[e] + BN - 1) / BN;
+        }
+        *n_items = io;
+    }
+    __syncthreads();
+    for (int p = threadIdx.x; p < P; p += blockDim.x) {
+        int e = eidx[p];
+        if (e >= 0 && e < E) {
+            int pos = off[e] + atomicAdd(&cur[e], 1);
+            pair_src[pos] = p;
+            pair_w[pos] = ewt[p];
+        }
+    }
+    for (int e = threadIdx.x; e < E; e += blockDim.x) {
+        int c = cnt[e], ni = (c + BN - 1) / BN;
+        for (int i = 0; i < ni; i++) items[ioff[e] + i] = WorkItem{e, off[e] + i * BN, min(BN, c - i * BN), 0};
+    }
+}
+
+__global__ void k_count_bad(const int32_t *eidx, int P, int E, int *bad) {
+    int p = blockIdx.x * blockDim.x + threadIdx.x;
+    if (p < P && (eidx[p] < 0 || eidx[p] >= E)) atomicAdd(bad, 1);
+}
+
+struct MoeWs {
+    int8_t *xq; float *xs, *xsx;
+    int *pair_src; float *pair_w;
+    WorkItem *items; int *n_items;
+    int8_t *hq; float *hs; int *hblk;
+    int *bad;
+    size_t total;
+};
+
+static MoeWs moe_layout(const zz_expert_bank *b, int S, int K, uint8_t *base) {
+    MoeWs w{};
+    const int D = b->hidden, MI = b->inter, E = b->n_experts;
+    const size_t P = (size_t)S * K, maxit = P / MOE_BN + E + 1;
+    size_t o = 0;
+    auto take = [&](size_t n) { size_t r = o; o += a256(n); return base ? base + r : nullptr; };
+    w.xq = (int8_t *)take((size_t)S * D);
+    w.xs = (float *)take((size_t)S * (D / 32) * 4);
+    w.xsx = (float *)take((size_t)S * 4);
+    w.pair_src = (int *)take(P * 4);
+    w.pair_w = (float *)take(P * 4);
+    w.items = (WorkItem *)take(maxit * sizeof(WorkItem));
+    w.n_items = (int *)take(4);
+    w.hq = (int8_t *)take(P * MI);
+    w.hs = (float *)take(P * (MI / 32) * 4);
+    w.hblk = (int *)take(P * (MI / 32) * 4);
+    w.bad = (int *)take(4);
+    w.total = o;
+    return w;
+}
+
+// ---- optional stage timing (diagnostic): events at the stage boundaries of every
+// zz_moe_ffn_dev call while enabled; summed on collection.
+struct StageProf {
+    bool on = false;
+    std::vector<cudaEvent_t> ev;  // 4 per call: start, after route, after gate/up, after down
+};
+static StageProf g_prof;
+
+static void prof_mark(cudaStream_t st) {
+    if (!g_prof.on) return;
+    cudaEvent_t e;
+    if (cudaEventCreate(&e) != cudaSuccess) return;
+    cudaEventRecord(e, st);
+    g_prof.ev.push_back(e);
+}
+
+}  // namespace zz
+
+using namespace zz;
+
+extern "C" int zz_prof_enable(int on) {
+    g_prof.on = on != 0;
+    return 1;
+}
+
+extern "C" int zz_prof_collect(float *stage_ms, int *calls) {
+    if (!stage_ms || !calls) return fail("zz_prof_collect: null pointer");
+    stage_ms[0] = stage_ms[1] = stage_ms[2] = 0.f;
+    *calls = 0;
+    size_t n = g_prof.ev.size() / 4 * 4;
+    if (n && !check_cuda(cudaEventSynchronize(g_prof.ev[n - 1]), "prof sync")) return 0;
+    for (size_t i = 0; i < n; i += 4) {
+        for (int k = 0; k < 3; k++) {
+            float ms = 0.f;
+            cudaEventElapsedTime(&ms, g_prof.ev[i + k], g_prof.ev[i + k + 1]);
+            stage_ms[k] += ms;
+        }
+        (*calls)++;
+    }
+    for (cudaEvent_t e : g_prof.ev) cudaEventDestroy(e);
+    g_prof.ev.clear();
+    return 1;
+}
+
+static bool bank_ok(const zz_expert_bank *b) {
+    if (!b) return false;
+    if (b->fmt != GPU_FMT_Q40 && b->fmt != GPU_FMT_Q80 && b->fmt != GPU_FMT_TQ2) return false;
+    return b->n_experts > 0 && b->n_experts <= 2048 && b->hidden > 0 && b->inter > 0 && b->hidden % 128 == 0 &&
+           b->inter % 64 == 0;
+}
+
+extern "C" size_t zz_expert_bank_bytes(int fmt, int E, int D, int MI) {
+    zz_expert_bank b{fmt, E, D, MI, nullptr, nullptr, nullptr, nullptr};
+    if (!bank_ok(&b)) return 0;
+    return (size_t)E * (codes_bytes(fmt, 2 * MI, D) + scales_bytes(fmt, 2 * MI, D) + codes_bytes(fmt, D, MI) +
+                        scales_bytes(fmt, D, MI));
+}
+
+extern "C" int zz_expert_bank_pack_dev(int fmt, int E, int D, int MI, const uint8_t *blobs, int64_t blob_stride,
+                                       void *dst, zz_expert_bank *out, void *stream) {
+    zz_expert_bank b{fmt, E, D, MI, nullptr, nullptr, nullptr, nullptr};
+    if (!bank_ok(&b)) return fail("zz_expert_bank_pack_dev: unsupported fmt %d / shape E=%d D=%d MI=%d", fmt, E, D, MI);
+    if (!blobs || !dst || !out) return fail("zz_expert_bank_pack_dev: null pointer");
+    if ((uintptr_t)dst & 255) return fail("zz_expert_bank_pack_dev: dst must be 256-byte aligned");
+    if ((uintptr_t)blobs & 3 || blob_stride & 3) return fail("zz_expert_bank_pack_dev: blobs must be 4-byte aligned");
+    cudaStream_t st = (cudaStream_t)stream;
+    const size_t gc = codes_bytes(fmt, 2 * MI, D), gs = scales_bytes(fmt, 2 * MI, D);
+    const size_t dc = codes_bytes(fmt, D, MI), ds = scales_bytes(fmt, D, MI);
+    uint8_t *p = (uint8_t *)dst;
+    uint8_t *gu_codes = p, *gu_scale = p + (size_t)E * gc;
+    uint8_t *dn_codes = gu_scale + (size_t)E * gs, *dn_scale = dn_codes + (size_t)E * dc;
+    if (!check_cuda(cudaMemsetAsync(gu_scale, 0, (size_t)E * gs, st), "bank memset")) return 0;
+    if (!check_cuda(cudaMemsetAsync(dn_scale, 0, (size_t)E * ds, st), "bank memset")) return 0;
+    const size_t gate_b = ref_tensor_bytes(fmt, MI, D);
+    RowMap gu{1, MI, (long)gate_b};
+    if (!launch_repack(fmt, blobs, blob_stride, 2 * MI, D, gu, gu_codes, gu_scale, (long)gc, (long)gs, E, st)) return 0;
+    RowMap dn{0, 0, 0};
+    if (!launch_repack(fmt, blobs + 2 * gate_b, blob_stride, D, MI, dn, dn_codes, dn_scale, (long)dc, (long)ds, E, st))
+        return 0;
+    *out = zz_expert_bank{fmt, E, D, MI, gu_codes, gu_scale, dn_codes, dn_scale};
+    return 1;
+}
+
+extern "C" size_t zz_moe_workspace_bytes(const zz_expert_bank *b, int S, int K) {
+    if (!bank_ok(b) || S < 0 || K <= 0) return 0;
+    return moe_layout(b, S, K, nullptr).total;
+}
+
+extern "C" size_t zz_moe_workspace_offset(const zz_expert_bank *b, int S, int K, int which) {
+    if (!bank_ok(b) || S <= 0 || K <= 0) return (size_t)-1;
+    uint8_t *base = reinterpret_cast<uint8_t *>((uintptr_t)4096);  // offsets only; never dereferenced
+    MoeWs w = moe_layout(b, S, K, base);
+    const void *p = which == 0 ? (const void *)w.pair_src : which == 1 ? (const void *)w.pair_w
+                  : which == 2 ? (const void *)w.hq : which == 3 ? (const void *)w.hs
+                  : which == 4 ? (const void *)w.n_items : nullptr;
+    if (!p) return (size_t)-1;
+    return (size_t)((const uint8_t *)p - base);
+}
+
+extern "C" int zz_moe_ffn_dev(const zz_expert_bank *b, const float *X, const int32_t *eidx, const float *ewt,
+                              float *OUT, int S, int K, int act, float clamp, void *workspace, size_t ws_bytes,
+                              int validate, void *stream) {
+    if (!bank_ok(b)) return fail("zz_moe_ffn_dev: invalid expert bank");
+    if (S < 0 || K <= 0 || K > 64) return fail("zz_moe_ffn_dev: bad S=%d or K=%d", S, K);
+    if (act < ZZ_ACT_GEGLU_TANH || act > ZZ_ACT_SWIGLU_CLAMP) return fail("zz_moe_ffn_dev: bad act %d", act);
+    if ((long)S * K > (1L << 26)) return fail("zz_moe_ffn_dev: S*K too large");
+    if (S == 0) return 1;
+    if (!X || !eidx || !ewt || !OUT || !workspace) return fail("zz_moe_ffn_dev: null pointer");
+    if ((uintptr_t)workspace & 255) return fail("zz_moe_ffn_dev: workspace must be 256-byte aligned");
+    MoeWs need = moe_layout(b, S, K, nullptr);
+    if (ws_bytes < need.total) return fail("zz_moe_ffn_dev: workspace %zu < %zu bytes", ws_bytes, need.total);
+    MoeWs w = moe_layout(b, S, K, (uint8_t *)workspace);
+    cudaStream_t st = (cudaStream_t)stream;
+    const int fmt = b->fmt, D = b->hidden, MI = b->inter, E = b->n_experts, P = S * K;
+    const int maxit = P / MOE_BN + E + 1;
+
+    if (validate) {
+        int bad = 0;
+        if (!check_cuda(cudaMemsetAsync(w.bad, 0, 4, st), "memset")) return 0;
+        k_count_bad<<<(P + 255) / 256, 256, 0, st>>>(eidx, P, E, w.bad);
+        if (!check_cuda(cudaMemcpyAsync(&bad, w.bad, 4, cudaMemcpyDeviceToHost, st), "copy") ||
+            !check_cuda(cudaStreamSynchronize(st), "sync"))
+            return 0;
+        if (bad) return fail("zz_moe_ffn_dev: %d expert ids outside [0, %d)", bad, E);
+    }
+    prof_mark(st);
+    if (!check_cuda(cudaMemsetAsync(OUT, 0, (size_t)S * D * 4, st), "memset OUT")) return 0;
+    if (!zz_quant_act_dev(X, S, D, w.xq, w.xs, fmt == GPU_FMT_TQ2 ? w.xsx : nullptr, stream)) return 0;
+    k_route<<<1, 1024, 4 * E * sizeof(int), st>>>(eidx, ewt, P, E, MOE_BN, w.pair_src, w.pair_w, w.items, w.n_items);
+    if (!check_cuda(cudaGetLastError(), "route launch")) return 0;
+
+    GemmArgs g{};
+    g.codes = b->gu_codes; g.scale = b->gu_scale;
+    g.codes_gstride = (long)codes_bytes(fmt, 2 * MI, D);
+    g.scale_gstride = (long)scales_bytes(fmt, 2 * MI, D);
+    g.O = 2 * MI; g.I = D;
+    g.xq = w.xq; g.xs = w.xs; g.xsx = w.xsx; g.xblk = nullptr; g.gather = w.pair_src; g.gather_div = K;
+    g.items = w.items; g.n_items = w.n_items;
+    g.act = act; g.clamp = clamp;
+    g.hq = w.hq; g.hs = w.hs; g.hblk = w.hblk;
+    prof_mark(st);
+    if (!launch_gemm<EPI_GATEUP, MOE_BN>(fmt, g, dim3((2 * MI) / G_BM, maxit), st)) return 0;
+    prof_mark(st);
+
+    GemmArgs d{};
+    d.codes = b->dn_codes; d.scale = b->dn_scale;
+    d.codes_gstride = (long)codes_bytes(fmt, D, MI);
+    d.scale_gstride = (long)scales_bytes(fmt, D, MI);
+    d.O = D; d.I = MI;
+    d.xq = w.hq; d.xs = w.hs; d.xsx = nullptr; d.xblk = fmt == GPU_FMT_TQ2 ? w.hblk : nullptr; d.gather = nullptr;
+    d.items = w.items; d.n_items = w.n_items;
+    d.out = OUT; d.pair_w = w.pair_w; d.pair_src = w.pair_src; d.K = K;
+    int ok = launch_gemm<EPI_DOWN, MOE_BN>(fmt, d, dim3((D + G_BM - 1) / G_BM, maxit), st);
+    prof_mark(st);
+    return ok;
+}
+
+// ---------------------------------------------------------------- dense
+namespace zz {
+// y[S, O] for S quantized rows; S == 1 takes the register-resident GEMV, larger S the
+// tensor-core GEMM with work items derived from the grid (no device scratch).
+int matvec_impl(const zz_qtensor *W, const int8_t *xq, const float *sx, const float *sxtot, float *y, int S,
+                cudaStream_t st) {
+    if (S == 1) {
+        int r = launch_gemv1(W, xq, sx, sxtot, y, st);
+        if (r != 0) return r > 0;
+    }
+    int n = (S + DENSE_BN - 1) / DENSE_BN;
+    GemmArgs g{};
+    g.codes = W->codes; g.scale = W->scale;
+    g.O = W->O; g.I = W->I;
+    g.xq = xq; g.xs = sx; g.xsx = sxtot;
+    g.items = nullptr; g.n_items = nullptr; g.rows_total = S;
+    g.y = y;
+    return launch_gemm<EPI_STORE, DENSE_BN>(W->fmt, g, dim3((W->O + G_BM - 1) / G_BM, n), st);
+}
+}  // namespace zz
