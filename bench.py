@@ -16,7 +16,6 @@ routed q8_0 activations move with an NCCL all-to-all; see zunzuncito_b200/ep.py.
 import argparse
 import json
 import os
-import subprocess
 import sys
 import threading
 import time
@@ -48,44 +47,49 @@ def parse():
 
 # ----------------------------------------------------------------------------- clocks
 class ClockSampler:
-    """nvidia-smi samples during the timed region (clocks + throttle reasons)."""
-    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    """NVML samples (read-only) of SM clock and throttle reasons during the timed region."""
+    REASONS = {"hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20, "hw_thermal_slowdown": 0x40, "sw_power_cap": 0x4}
 
-    def __init__(self, index):
-        self.index, self.rows, self.proc = index, [], None
+    def __init__(self, index, period=0.1):
+        self.index, self.period, self.rows, self.stop = index, period, [], threading.Event()
 
     def __enter__(self):
         try:
-            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}",
-                                          "--format=csv,noheader,nounits", "-lms", "100"],
-                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-            self.t = threading.Thread(target=self._read, daemon=True)
+            import pynvml
+            pynvml.nvmlInit()
+            self.nv = pynvml
+            self.h = pynvml.nvmlDeviceGetHandleByIndex(self.index)
+            self.max_sm = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+            self.t = threading.Thread(target=self._run, daemon=True)
             self.t.start()
-        except OSError:
-            self.proc = None
+        except Exception as e:  # noqa: BLE001
+            self.nv, self.err = None, str(e)
         return self
 
-    def _read(self):
-        for line in self.proc.stdout:
-            self.rows.append([c.strip() for c in line.split(",")])
+    def _run(self):
+        nv = self.nv
+        while not self.stop.is_set():
+            try:
+                sm = nv.nvmlDeviceGetClockInfo(self.h, nv.NVML_CLOCK_SM)
+                rs = nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+                pw = nv.nvmlDeviceGetPowerUsage(self.h) / 1000.0
+                self.rows.append((sm, rs, pw))
+            except Exception:  # noqa: BLE001
+                pass
+            self.stop.wait(self.period)
 
     def __exit__(self, *a):
-        if self.proc:
-            self.proc.terminate()
-            self.proc.wait()
+        self.stop.set()
+        if self.nv:
             self.t.join(timeout=2)
 
     def summary(self):
         if not self.rows:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
-        sm = [float(r[1]) for r in self.rows if r[1].replace(".", "").isdigit()]
-        mx = [float(r[2]) for r in self.rows if r[2].replace(".", "").isdigit()]
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({n for r in self.rows for n, v in zip(names, r[5:9]) if v.lower() == "active"})
-        return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": max(mx) if mx else None,
-                "reasons": reasons, "samples": len(self.rows)}
+        sm = [r[0] for r in self.rows]
+        reasons = sorted({n for r in self.rows for n, bit in self.REASONS.items() if r[1] & bit})
+        return {"sm_mhz": float(np.median(sm)), "sm_max_mhz": self.max_sm, "reasons": reasons,
+                "samples": len(self.rows), "power_w_max": max(r[2] for r in self.rows)}
 
 
 # ----------------------------------------------------------------------------- data

@@ -140,11 +140,20 @@ size_t zz_moe_workspace_bytes(const zz_expert_bank *bank, int S, int K);
  * with e = eidx[s,k]. X [S, hidden] f32, eidx/ewt [S, K], OUT [S, hidden] f32
  * (overwritten). Each distinct expert's weights are streamed once for all of its
  * tokens. act is a ZZ_ACT_* value, clamp is used by ZZ_ACT_SWIGLU_CLAMP.
- * eidx values outside [0, n_experts) decline before any work is launched only when
- * validate != 0 (it costs a device->host sync); otherwise they are skipped. */
+ * With validate != 0, eidx values outside [0, n_experts) decline before any work is
+ * launched (it costs a device->host sync); otherwise such entries are skipped. */
 int zz_moe_ffn_dev(const zz_expert_bank *bank, const float *X, const int32_t *eidx,
                    const float *ewt, float *OUT, int S, int K, int act, float clamp,
                    void *workspace, size_t workspace_bytes, int validate, void *stream);
+
+/* Same layer for rows that arrive already quantized to q8_0 (xq [S, hidden] int8,
+ * xs [S, hidden/32] f32), e.g. received from another GPU by the expert-parallel
+ * dispatch. eidx entries outside [0, n_experts) are skipped, so a row can carry fewer
+ * than K local experts (pad with -1). Output and workspace as zz_moe_ffn_dev. */
+int zz_moe_ffn_q8_dev(const zz_expert_bank *bank, const int8_t *xq, const float *xs,
+                      const int32_t *eidx, const float *ewt, float *OUT, int S, int K, int act,
+                      float clamp, void *workspace, size_t workspace_bytes, int validate,
+                      void *stream);
 
 /* Diagnostic: byte offset inside the zz_moe_ffn_dev workspace (same bank, S, K) of
  *   0 pair_src int32[S*K]  routing slot s*K+k held by each pair row, grouped by expert

@@ -98,8 +98,8 @@ def check_pairs(orc, kind, blobs, X, eidx, ewt, out_gpu, bank, pairs=None):
             assert np.max(np.abs(diff)) <= 1, (r, np.max(np.abs(diff)))
             n_flip += int(np.count_nonzero(diff))
             flipped_tok.add(s)
-        # scales: identical unless the block max itself moved by an ulp
-        assert np.allclose(hs[r], es[0], rtol=3e-7, atol=0), r
+        # scales: amax/127 of h; h itself carries fp32 accumulation-order noise
+        assert np.allclose(hs[r], es[0], rtol=1e-5, atol=0), r
     total = len(rows) * MI
     assert n_flip <= max(3, total // 500), (n_flip, total)
     if pairs is None:

@@ -10,7 +10,7 @@ import torch
 from . import (GPU_FMT_Q40, GPU_FMT_Q80, GPU_FMT_TQ2, ExpertBank, QTensor, check, lib)
 
 __all__ = ["ref_row_bytes", "ref_tensor_bytes", "expert_blob_bytes", "quant_act", "quant_rows",
-           "QTensorDev", "matvec", "blocksums", "ExpertBankDev", "moe_ffn", "alloc_aligned"]
+           "QTensorDev", "matvec", "blocksums", "ExpertBankDev", "moe_ffn", "moe_ffn_q8", "alloc_aligned"]
 
 
 def _stream():
@@ -131,4 +131,18 @@ def moe_ffn(bank, X, eidx, ewt, act, clamp=0.0, out=None, validate=False):
     ws = bank.workspace(S, K)
     check(lib.zz_moe_ffn_dev(ctypes.byref(bank.b), _p(X), _p(eidx), _p(ewt), _p(out), S, K, act, float(clamp),
                              _p(ws), ws.numel(), int(validate), _stream()), "zz_moe_ffn_dev")
+    return out
+
+
+def moe_ffn_q8(bank, xq, xs, eidx, ewt, act, clamp=0.0, out=None, validate=False):
+    """The same layer for q8_0 rows (zz_moe_ffn_q8_dev); eidx entries of -1 are skipped."""
+    S, D = xq.shape
+    K = eidx.shape[1]
+    if out is None:
+        out = torch.empty((S, D), dtype=torch.float32, device=xq.device)
+    if S == 0:
+        return out
+    ws = bank.workspace(S, K)
+    check(lib.zz_moe_ffn_q8_dev(ctypes.byref(bank.b), _p(xq), _p(xs), _p(eidx), _p(ewt), _p(out), S, K, act,
+                                float(clamp), _p(ws), ws.numel(), int(validate), _stream()), "zz_moe_ffn_q8_dev")
     return out

@@ -230,18 +230,39 @@ extern "C" size_t zz_moe_workspace_offset(const zz_expert_bank *b, int S, int K,
     return (size_t)((const uint8_t *)p - base);
 }
 
-extern "C" int zz_moe_ffn_dev(const zz_expert_bank *b, const float *X, const int32_t *eidx, const float *ewt,
-                              float *OUT, int S, int K, int act, float clamp, void *workspace, size_t ws_bytes,
-                              int validate, void *stream) {
-    if (!bank_ok(b)) return fail("zz_moe_ffn_dev: invalid expert bank");
-    if (S < 0 || K <= 0 || K > 64) return fail("zz_moe_ffn_dev: bad S=%d or K=%d", S, K);
-    if (act < ZZ_ACT_GEGLU_TANH || act > ZZ_ACT_SWIGLU_CLAMP) return fail("zz_moe_ffn_dev: bad act %d", act);
-    if ((long)S * K > (1L << 26)) return fail("zz_moe_ffn_dev: S*K too large");
+// Sx of q8_0 rows (tq2 offset total, tq2.h:103-107), one thread per row
+__global__ void k_rows_sx(const int8_t *__restrict__ xq, const float *__restrict__ xs, int S, int I,
+                          float *__restrict__ xsx) {
+    int r = blockIdx.x * blockDim.x + threadIdx.x;
+    if (r >= S) return;
+    const int nb = I / 32;
+    double tot = 0;
+    for (int b = 0; b < nb; b++) {
+        const char4 *q = reinterpret_cast<const char4 *>(xq + (size_t)r * I + (size_t)b * 32);
+        int s = 0;
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+            char4 c = q[i];
+            s += c.x + c.y + c.z + c.w;
+        }
+        tot += (double)xs[(size_t)r * nb + b] * (double)s;
+    }
+    xsx[r] = (float)tot;
+}
+
+// X != NULL: f32 rows quantized here; else xq/xs are q8_0 rows given by the caller.
+static int moe_impl(const zz_expert_bank *b, const float *X, const int8_t *xq_in, const float *xs_in,
+                    const int32_t *eidx, const float *ewt, float *OUT, int S, int K, int act, float clamp,
+                    void *workspace, size_t ws_bytes, int validate, void *stream) {
+    if (!bank_ok(b)) return fail("zz_moe_ffn: invalid expert bank");
+    if (S < 0 || K <= 0 || K > 64) return fail("zz_moe_ffn: bad S=%d or K=%d", S, K);
+    if (act < ZZ_ACT_GEGLU_TANH || act > ZZ_ACT_SWIGLU_CLAMP) return fail("zz_moe_ffn: bad act %d", act);
+    if ((long)S * K > (1L << 26)) return fail("zz_moe_ffn: S*K too large");
     if (S == 0) return 1;
-    if (!X || !eidx || !ewt || !OUT || !workspace) return fail("zz_moe_ffn_dev: null pointer");
-    if ((uintptr_t)workspace & 255) return fail("zz_moe_ffn_dev: workspace must be 256-byte aligned");
+    if ((!X && (!xq_in || !xs_in)) || !eidx || !ewt || !OUT || !workspace) return fail("zz_moe_ffn: null pointer");
+    if ((uintptr_t)workspace & 255) return fail("zz_moe_ffn: workspace must be 256-byte aligned");
     MoeWs need = moe_layout(b, S, K, nullptr);
-    if (ws_bytes < need.total) return fail("zz_moe_ffn_dev: workspace %zu < %zu bytes", ws_bytes, need.total);
+    if (ws_bytes < need.total) return fail("zz_moe_ffn: workspace %zu < %zu bytes", ws_bytes, need.total);
     MoeWs w = moe_layout(b, S, K, (uint8_t *)workspace);
     cudaStream_t st = (cudaStream_t)stream;
     const int fmt = b->fmt, D = b->hidden, MI = b->inter, E = b->n_experts, P = S * K;
@@ -254,11 +275,19 @@ extern "C" int zz_moe_ffn_dev(const zz_expert_bank *b, const float *X, const int
         if (!check_cuda(cudaMemcpyAsync(&bad, w.bad, 4, cudaMemcpyDeviceToHost, st), "copy") ||
             !check_cuda(cudaStreamSynchronize(st), "sync"))
             return 0;
-        if (bad) return fail("zz_moe_ffn_dev: %d expert ids outside [0, %d)", bad, E);
+        if (bad) return fail("zz_moe_ffn: %d expert ids outside [0, %d)", bad, E);
     }
     prof_mark(st);
     if (!check_cuda(cudaMemsetAsync(OUT, 0, (size_t)S * D * 4, st), "memset OUT")) return 0;
-    if (!zz_quant_act_dev(X, S, D, w.xq, w.xs, fmt == GPU_FMT_TQ2 ? w.xsx : nullptr, stream)) return 0;
+    const int8_t *xq = xq_in;
+    const float *xs = xs_in;
+    if (X) {
+        if (!zz_quant_act_dev(X, S, D, w.xq, w.xs, fmt == GPU_FMT_TQ2 ? w.xsx : nullptr, stream)) return 0;
+        xq = w.xq;
+        xs = w.xs;
+    } else if (fmt == GPU_FMT_TQ2) {
+        k_rows_sx<<<(S + 127) / 128, 128, 0, st>>>(xq, xs, S, D, w.xsx);
+    }
     k_route<<<1, 1024, 4 * E * sizeof(int), st>>>(eidx, ewt, P, E, MOE_BN, w.pair_src, w.pair_w, w.items, w.n_items);
     if (!check_cuda(cudaGetLastError(), "route launch")) return 0;
 
@@ -267,7 +296,7 @@ extern "C" int zz_moe_ffn_dev(const zz_expert_bank *b, const float *X, const int
     g.codes_gstride = (long)codes_bytes(fmt, 2 * MI, D);
     g.scale_gstride = (long)scales_bytes(fmt, 2 * MI, D);
     g.O = 2 * MI; g.I = D;
-    g.xq = w.xq; g.xs = w.xs; g.xsx = w.xsx; g.xblk = nullptr; g.gather = w.pair_src; g.gather_div = K;
+    g.xq = xq; g.xs = xs; g.xsx = w.xsx; g.xblk = nullptr; g.gather = w.pair_src; g.gather_div = K;
     g.items = w.items; g.n_items = w.n_items;
     g.act = act; g.clamp = clamp;
     g.hq = w.hq; g.hs = w.hs; g.hblk = w.hblk;
@@ -286,6 +315,20 @@ extern "C" int zz_moe_ffn_dev(const zz_expert_bank *b, const float *X, const int
     int ok = launch_gemm<EPI_DOWN, MOE_BN>(fmt, d, dim3((D + G_BM - 1) / G_BM, maxit), st);
     prof_mark(st);
     return ok;
+}
+
+extern "C" int zz_moe_ffn_dev(const zz_expert_bank *b, const float *X, const int32_t *eidx, const float *ewt,
+                              float *OUT, int S, int K, int act, float clamp, void *workspace, size_t ws_bytes,
+                              int validate, void *stream) {
+    if (!X && S > 0) return fail("zz_moe_ffn_dev: null X");
+    return moe_impl(b, X, nullptr, nullptr, eidx, ewt, OUT, S, K, act, clamp, workspace, ws_bytes, validate, stream);
+}
+
+extern "C" int zz_moe_ffn_q8_dev(const zz_expert_bank *b, const int8_t *xq, const float *xs, const int32_t *eidx,
+                                 const float *ewt, float *OUT, int S, int K, int act, float clamp, void *workspace,
+                                 size_t ws_bytes, int validate, void *stream) {
+    if ((!xq || !xs) && S > 0) return fail("zz_moe_ffn_q8_dev: null activation");
+    return moe_impl(b, nullptr, xq, xs, eidx, ewt, OUT, S, K, act, clamp, workspace, ws_bytes, validate, stream);
 }
 
 // ---------------------------------------------------------------- dense
