@@ -172,6 +172,21 @@ class Oracle(_Lib):
         return out
 
 
+    def moe_layer_q8(self, kind, blobs, XQ, XS, eidx, ewt, D, MI, clamp=7.0):
+        """the layer on pre-quantized rows; eidx entries outside [0, E) are skipped"""
+        S, K = eidx.shape
+        E = blobs.shape[0]
+        out = np.zeros((S, D), np.float32)
+        if S == 0:
+            return out
+        ptrs = (_P * max(E, 1))(*[blobs[e].ctypes.data for e in range(E)])
+        f = self.fn("moe_layer_q8", None, [_I, _P, _I, _P, _P, _P, _I, _I, _P, _P, _I, _I, _F])
+        f(kind, ptrs, E, _ptr(np.ascontiguousarray(XQ, np.int8)), _ptr(np.ascontiguousarray(XS, np.float32)),
+          _ptr(out), S, K, _ptr(np.ascontiguousarray(eidx, np.int32)), _ptr(np.ascontiguousarray(ewt, np.float32)),
+          D, MI, float(clamp))
+        return out
+
+
 class Reference(_Lib):
     """The reference's own kernels and engine routines (oracle/_ref/libzzref.so)."""
 

@@ -346,3 +346,68 @@ void orc_act_vec(int act, const float *g, const float *u, float *h, int n, float
         h[i] = orc_silu(gv) * uv;
     }
 }
+
+/* The batch-union layer for rows that arrive already quantized (xq [S, D] int8,
+ * sx [S, D/32]): what an expert-parallel receiver computes for the rows routed to its
+ * experts. Expert ids outside [0, E) are skipped (padding). Sums per row over the K
+ * slots in slot order; OUT zeroed first. Same expert math as orc_moe_layer. */
+void orc_moe_layer_q8(int kind, const uint8_t *const *blobs, int E, const int8_t *XQ, const float *XS,
+                      float *OUT, int S, int K, const int *eidx, const float *ewt, int D, int MI, float CL) {
+    int nbD = D / ORC_BLK;
+    float *X = malloc(sizeof(float) * (size_t)D);
+    int8_t *xq = malloc((size_t)D);
+    float *sx = malloc(sizeof(float) * nbD);
+    memset(OUT, 0, sizeof(float) * (size_t)S * D);
+    for (int s = 0; s < S; s++) {
+        /* the expert routines quantize their input row; hand them a row whose
+         * quantization is exactly (xq, sx): only the GEMV inputs matter, so run the
+         * expert math directly on the given codes */
+        for (int k = 0; k < K; k++) {
+            int e = eidx[s * K + k];
+            if (e < 0 || e >= E) continue;
+            const uint8_t *blob = blobs[e];
+            float w = ewt[s * K + k];
+            const int8_t *q = XQ + (size_t)s * D;
+            const float *qs = XS + (size_t)s * nbD;
+            float *out = OUT + (size_t)s * D;
+            float *h = malloc(sizeof(float) * (size_t)MI);
+            int8_t *hq = malloc((size_t)MI);
+            float *hs = malloc(sizeof(float) * (MI / ORC_BLK));
+            if (kind == 3) {
+                size_t gate_b = (size_t)MI * 4 + (size_t)MI * (D / 4);
+                const uint8_t *G = blob, *U = blob + gate_b, *Dn = blob + 2 * gate_b;
+                double tot = 0;
+                for (int b = 0; b < nbD; b++) {
+                    int32_t t = 0;
+                    for (int j = 0; j < ORC_BLK; j++) t += q[b * ORC_BLK + j];
+                    tot += (double)qs[b] * (double)t;
+                }
+                float tx = (float)tot;
+                for (int o = 0; o < MI; o++) {
+                    float g = orc_tq2_dot(G + MI * 4 + (size_t)o * (D / 4), ((const float *)G)[o], q, qs, tx, D);
+                    float u = orc_tq2_dot(U + MI * 4 + (size_t)o * (D / 4), ((const float *)U)[o], q, qs, tx, D);
+                    if (g > CL) g = CL;
+                    u = u < -CL ? -CL : (u > CL ? CL : u);
+                    h[o] = orc_silu(g) * u;
+                }
+                float th = orc_tq2_quant_act(h, hq, hs, MI);
+                for (int o = 0; o < D; o++)
+                    out[o] += w * orc_tq2_dot(Dn + D * 4 + (size_t)o * (MI / 4), ((const float *)Dn)[o], hq, hs, th, MI);
+            } else {
+                int fmt = kind == 2 ? 2 : 1, bb = fmt == 2 ? ORC_Q80_BB : ORC_Q40_BB;
+                size_t grb = (size_t)nbD * bb, drb = (size_t)(MI / ORC_BLK) * bb, gate_b = grb * MI;
+                const uint8_t *G = blob, *U = blob + gate_b, *Dn = blob + 2 * gate_b;
+                for (int o = 0; o < MI; o++) {
+                    float g = fmt == 2 ? orc_q80_dot(G + o * grb, q, qs, D) : orc_q40_dot(G + o * grb, q, qs, D);
+                    float u = fmt == 2 ? orc_q80_dot(U + o * grb, q, qs, D) : orc_q40_dot(U + o * grb, q, qs, D);
+                    h[o] = kind == 0 ? orc_gelu_tanh(g) * u : orc_silu(g) * u;
+                }
+                orc_quant_act(h, hq, hs, MI);
+                for (int o = 0; o < D; o++)
+                    out[o] += w * (fmt == 2 ? orc_q80_dot(Dn + o * drb, hq, hs, MI) : orc_q40_dot(Dn + o * drb, hq, hs, MI));
+            }
+            free(h); free(hq); free(hs);
+        }
+    }
+    free(X); free(xq); free(sx);
+}

@@ -4,14 +4,24 @@
 //
 // The per-block scales vary along both o and n, so int32 partials cannot be carried
 // across 32-wide K blocks: every block's integer product is converted and scaled into
-// fp32 accumulators before the next block (the decomposition of q40.h:20-31). One
-// tensor-core MMA of K=32 therefore matches exactly one q4_0 block.
+// fp32 accumulators before the next block (the decomposition of q40.h:20-31).
+//
+// The tensor cores see the codes and activations as fp16 values that are exactly the
+// integers the reference multiplies (q-8 in [-8,7], q8 codes and activations in
+// [-127,127], tq2 codes {0,1,2}); each product and each 32-term block sum (|s| <
+// 2^15) is exact in the f32 accumulator, so the MMA result of one block IS the
+// reference's per-block integer, already in floating point. That removes the
+// int->float conversion per (row, column, block) that an s8 MMA would need (a
+// quarter-rate instruction that otherwise bounds the whole kernel); what remains per
+// element and block is one packed fma.rn.f32x2 and one packed multiply.
 //
 // CTA tile: 128 weight rows x BN activation rows, 8 warps of 16 rows each. K moves in
-// chunks of 4 blocks (128 weights) through a 4-stage cp.async pipeline; nibble / 2-bit
-// codes are widened to int8 in registers straight into the MMA fragment (the q4_0
-// byte layout -- low nibble k, high nibble k+16 -- is exactly the m16n8k32 A-fragment
-// split, so one 32-bit shared load feeds two fragment registers).
+// chunks of 4 blocks (128 weights) through a cp.async pipeline. The weight codes stay
+// packed in shared memory and are widened to fp16 in registers straight into the
+// m16n8k16 A fragment (q4_0: low nibbles of bytes j are k = j, high nibbles k = j+16,
+// so one 16-bit load feeds both k16 steps of a block). Activations are fp16 in
+// shared memory (ldmatrix.x4 fetches a whole block's B fragment) or int8 widened in
+// registers for callers that hold only int8 rows.
 //
 // Work items (grid.y) name a group (expert) and a contiguous range of <= BN activation
 // rows; grid.x walks 128-row weight tiles. Epilogues:
@@ -26,7 +36,7 @@ namespace zz {
 
 enum { EPI_STORE = 0, EPI_GATEUP = 1, EPI_DOWN = 2 };
 
-constexpr int G_BM = 128, G_BKB = 4, G_STAGES = 4, G_THREADS = 256;
+constexpr int G_BM = 128, G_BKB = 4, G_STAGES = 3, G_THREADS = 256;
 
 template <int FMT>
 struct FmtTraits {
@@ -49,7 +59,7 @@ struct GemmArgs {
     long codes_gstride, scale_gstride;  // bytes
     int O, I;                // rows per group, K
     // activations: row r of the item -> X row xrow(r) (gather), scales likewise
-    const int8_t *xq;
+    const void *xq;          // int8 rows [*, I] (B_HALF = false) or fp16 rows (B_HALF = true)
     const float *xs;
     const float *xsx;        // tq2 per-row Sx (EPI_STORE / EPI_GATEUP, indexed by X row)
     const int *xblk;         // tq2 down: per-block int sums of X rows; Sx is summed here
@@ -65,6 +75,7 @@ struct GemmArgs {
     int act;
     float clamp;
     int8_t *hq;              // [pair][O/2]
+    __half *hh;              // [pair][O/2] the same values as fp16 (the down GEMM's B)
     float *hs;               // [pair][O/64]
     int *hblk;               // [pair][O/64] (tq2 only)
     // EPI_DOWN
@@ -74,20 +85,41 @@ struct GemmArgs {
     int K;
 };
 
-__device__ __forceinline__ void mma_s8(int c[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
-                                       uint32_t b1) {
+__device__ __forceinline__ void mma_f16(float d[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                        uint32_t b0, uint32_t b1, float c0, float c1, float c2, float c3) {
     asm volatile(
-        "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
         "{%10,%11,%12,%13};"
-        : "=r"(c[0]), "=r"(c[1]), "=r"(c[2]), "=r"(c[3])
-        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(0), "r"(0), "r"(0), "r"(0));
+        : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "f"(c0), "f"(c1), "f"(c2), "f"(c3));
+}
+__device__ __forceinline__ void ldsm_x4(uint32_t &r0, uint32_t &r1, uint32_t &r2, uint32_t &r3, const void *p) {
+    uint32_t s = (uint32_t)__cvta_generic_to_shared(p);
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3) : "r"(s));
+}
+// packed fp32 pair ops (sm_100): d = a*b + c and d = a*b on two lanes at once
+__device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
+    float2 d;
+    asm("{.reg .b64 ra, rb, rc, rd;\n\t"
+        "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\tmov.b64 rc, {%6, %7};\n\t"
+        "fma.rn.f32x2 rd, ra, rb, rc;\n\tmov.b64 {%0, %1}, rd;}"
+        : "=f"(d.x), "=f"(d.y) : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+    return d;
+}
+__device__ __forceinline__ float2 fmul2(float2 a, float2 b) {
+    float2 d;
+    asm("{.reg .b64 ra, rb, rd;\n\t"
+        "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+        "mul.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;}"
+        : "=f"(d.x), "=f"(d.y) : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+    return d;
 }
 __device__ __forceinline__ void cp_async4_zfill(void *smem, const void *gmem, bool valid) {
     uint32_t s = (uint32_t)__cvta_generic_to_shared(smem);
     int n = valid ? 4 : 0;
     asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(s), "l"(gmem), "r"(n));
 }
-
 __device__ __forceinline__ void cp_async8_zfill(void *smem, const void *gmem, bool valid) {
     uint32_t s = (uint32_t)__cvta_generic_to_shared(smem);
     int n = valid ? 8 : 0;
@@ -98,6 +130,7 @@ __device__ __forceinline__ float gelu_tanh_dev(float x) {
     return 0.5f * x * (1.0f + tanhf(0.7978845608028654f * (x + 0.044715f * x * x * x)));
 }
 __device__ __forceinline__ float silu_dev(float x) { return x / (1.0f + expf(-x)); }
+// gated activations of the expert FFN (gemma4.c:432-434, 637-644; maple.c:653-655)
 __device__ __forceinline__ float gated_act(int act, float g, float u, float cl) {
     if (act == ZZ_ACT_GEGLU_TANH) return gelu_tanh_dev(g) * u;
     if (act == ZZ_ACT_SWIGLU_CLAMP) {
@@ -107,10 +140,33 @@ __device__ __forceinline__ float gated_act(int act, float g, float u, float cl) 
     return silu_dev(g) * u;
 }
 
-template <int FMT, int BN>
+// --- widening two packed codes (bytes b0, b1 of a 16-bit value) to an fp16 pair ---
+__device__ __forceinline__ uint32_t spread2(uint32_t v) { return __byte_perm(v, 0u, 0x4140u); }  // 00 b1 00 b0
+__device__ __forceinline__ uint32_t h2sub(uint32_t a, uint32_t b) {
+    __half2 r = __hsub2(*reinterpret_cast<__half2 *>(&a), *reinterpret_cast<__half2 *>(&b));
+    return *reinterpret_cast<uint32_t *>(&r);
+}
+__device__ __forceinline__ uint32_t h2fma(uint32_t a, uint32_t b, uint32_t c) {
+    __half2 r = __hfma2(*reinterpret_cast<__half2 *>(&a), *reinterpret_cast<__half2 *>(&b),
+                        *reinterpret_cast<__half2 *>(&c));
+    return *reinterpret_cast<uint32_t *>(&r);
+}
+// 0x6400 is fp16 1024.0; OR-ing a small integer into its mantissa makes 1024 + v exactly
+constexpr uint32_t H1024 = 0x64006400u, H1032 = 0x64086408u, H1152 = 0x64806480u;
+constexpr uint32_t H_1_16 = 0x2C002C00u, H_NEG72 = 0xD480D480u;  // 1/16, -72
+// q4_0 low nibbles -> q-8
+__device__ __forceinline__ uint32_t q4lo_h2(uint32_t p) { return h2sub((p & 0x000F000Fu) | H1024, H1032); }
+// q4_0 high nibbles: 1024 + 16q, times 1/16 minus 72 -> q-8
+__device__ __forceinline__ uint32_t q4hi_h2(uint32_t p) { return h2fma((p & 0x00F000F0u) | H1024, H_1_16, H_NEG72); }
+// signed int8 -> fp16: (x ^ 0x80) = x + 128 in [0, 255]; 1024 + x + 128 - 1152 = x
+__device__ __forceinline__ uint32_t s8_h2(uint32_t p) { return h2sub((p ^ 0x00800080u) | H1024, H1152); }
+// tq2 2-bit codes at bit offset sh -> c
+__device__ __forceinline__ uint32_t c2_h2(uint32_t p, int sh) { return h2sub(((p >> sh) & 0x00030003u) | H1024, H1024); }
+
+template <int FMT, int BN, bool B_HALF>
 struct GemmSmem {
     using T = FmtTraits<FMT>;
-    static constexpr int B_STRIDE = 32 * G_BKB + 16;
+    static constexpr int B_STRIDE = B_HALF ? (32 * G_BKB * 2 + 16) : (32 * G_BKB + 16);  // bytes per row
     static constexpr int A_BYTES = G_BM * T::A_STRIDE;
     static constexpr int AS_BYTES = T::HAS_WSCALE ? G_BM * G_BKB * 2 : 0;
     static constexpr int B_BYTES = BN * B_STRIDE;
@@ -121,10 +177,10 @@ struct GemmSmem {
     static constexpr int TOTAL = (PIPE > EPI ? PIPE : EPI) + BN * 16;  // + per-column info
 };
 
-template <int FMT, int BN, int EPI>
+template <int FMT, int BN, int EPI, bool B_HALF>
 __global__ void __launch_bounds__(G_THREADS) k_gemm(GemmArgs a) {
     using T = FmtTraits<FMT>;
-    using L = GemmSmem<FMT, BN>;
+    using L = GemmSmem<FMT, BN, B_HALF>;
     extern __shared__ __align__(128) uint8_t smem[];
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, t = lane & 3;
 
@@ -146,8 +202,10 @@ __global__ void __launch_bounds__(G_THREADS) k_gemm(GemmArgs a) {
 
     const uint8_t *codes = a.codes + (long)it.group * a.codes_gstride;
     const size_t code_row = (size_t)nb * T::CB;
+    const size_t xrow_bytes = (size_t)a.I * (B_HALF ? 2 : 1);
+    const uint8_t *xbase = reinterpret_cast<const uint8_t *>(a.xq);
 
-    // per-column info: X row index (after gather)
+    // per-column info: X row index (after gather) and the tq2 offset total
     int *col_xrow = reinterpret_cast<int *>(smem + L::TOTAL - BN * 16);
     float *col_sx = reinterpret_cast<float *>(smem + L::TOTAL - BN * 12);
     for (int n = tid; n < BN; n += G_THREADS) {
@@ -183,8 +241,7 @@ __global__ void __launch_bounds__(G_THREADS) k_gemm(GemmArgs a) {
         for (int i = tid; i < G_BM * APR; i += G_THREADS) {
             int r = i / APR, p = i % APR;
             int row = m0 + r;
-            // a 16 B piece covers 16/CB blocks (1 for q4, half for q8, 2 for tq2)
-            int blk_in = (p * 16) / T::CB;
+            int blk_in = (p * 16) / T::CB;  // a piece covers 16/CB blocks
             bool ok = row < a.O && blk_in < nbk;
             const uint8_t *src = codes + (size_t)(ok ? row : 0) * code_row + (size_t)b0 * T::CB + p * 16;
             cp_async16_zfill(sa + r * T::A_STRIDE + p * 16, ok ? src : codes, ok);
@@ -201,27 +258,28 @@ __global__ void __launch_bounds__(G_THREADS) k_gemm(GemmArgs a) {
                 cp_async8_zfill(sas + r * 8, src, ok);
             }
         }
-        // B: BN activation rows x 128 bytes (8 pieces), gathered
-        for (int i = tid; i < BN * 8; i += G_THREADS) {
-            int n = i >> 3, p = i & 7;
-            bool ok = n < ncols && (p >> 1) < nbk;
-            const int8_t *src = a.xq + (size_t)col_xrow[n] * a.I + (size_t)b0 * 32 + p * 16;
-            cp_async16_zfill(sb + n * L::B_STRIDE + p * 16, ok ? (const void *)src : (const void *)a.xq, ok);
+        // B: BN activation rows x 4 blocks, gathered, in 16 B pieces
+        constexpr int BPR = B_HALF ? 16 : 8;
+        constexpr int PPB = BPR / G_BKB;  // pieces per block
+        for (int i = tid; i < BN * BPR; i += G_THREADS) {
+            int n = i / BPR, p = i % BPR;
+            bool ok = n < ncols && (p / PPB) < nbk;
+            const uint8_t *src = xbase + (size_t)col_xrow[n] * xrow_bytes + (size_t)b0 * (B_HALF ? 64 : 32) + p * 16;
+            cp_async16_zfill(sb + n * L::B_STRIDE + p * 16, ok ? (const void *)src : (const void *)xbase, ok);
         }
+        // activation scales, stored [block][column] so a column pair is one 8-byte load
         for (int i = tid; i < BN * G_BKB; i += G_THREADS) {
             int n = i / G_BKB, k = i % G_BKB;
             bool ok = n < ncols && k < nbk;
             const float *src = a.xs + (size_t)col_xrow[n] * nb + b0 + k;
-            cp_async4_zfill(sbs + (n * G_BKB + k) * 4, ok ? (const void *)src : (const void *)a.xs, ok);
+            cp_async4_zfill(sbs + (k * BN + n) * 4, ok ? (const void *)src : (const void *)a.xs, ok);
         }
     };
 
     constexpr int NT = BN / 8;
-    float acc[NT][4];
+    float2 acc[NT][2];  // [n8 tile][row g | row g+8] x column pair (2t, 2t+1)
 #pragma unroll
-    for (int j = 0; j < NT; j++)
-#pragma unroll
-        for (int e = 0; e < 4; e++) acc[j][e] = 0.f;
+    for (int j = 0; j < NT; j++) acc[j][0] = acc[j][1] = make_float2(0.f, 0.f);
     const int jv = (ncols + 7) >> 3;  // n8 tiles holding valid columns (warp-uniform)
 
 #pragma unroll
@@ -244,50 +302,72 @@ __global__ void __launch_bounds__(G_THREADS) k_gemm(GemmArgs a) {
         const float *sbs = reinterpret_cast<const float *>(sb + L::B_BYTES);
         const int nbk = nb - c * G_BKB < G_BKB ? nb - c * G_BKB : G_BKB;
         for (int kb = 0; kb < nbk; kb++) {
-            uint32_t a0, a1, a2, a3;
-            if (FMT == GPU_FMT_Q40) {
-                uint32_t w0 = *reinterpret_cast<const uint32_t *>(sa + rA * T::A_STRIDE + kb * 16 + 4 * t);
-                uint32_t w1 = *reinterpret_cast<const uint32_t *>(sa + (rA + 8) * T::A_STRIDE + kb * 16 + 4 * t);
-                a0 = nib_to_s8(w0); a2 = nib_to_s8(w0 >> 4);
-                a1 = nib_to_s8(w1); a3 = nib_to_s8(w1 >> 4);
-            } else if (FMT == GPU_FMT_Q80) {
-                const uint8_t *p0 = sa + rA * T::A_STRIDE + kb * 32 + 4 * t;
-                const uint8_t *p1 = p0 + 8 * T::A_STRIDE;
-                a0 = *reinterpret_cast<const uint32_t *>(p0); a2 = *reinterpret_cast<const uint32_t *>(p0 + 16);
-                a1 = *reinterpret_cast<const uint32_t *>(p1); a3 = *reinterpret_cast<const uint32_t *>(p1 + 16);
-            } else {
-                const int sh = (kb & 1) * 4;
-                uint32_t w0 = *reinterpret_cast<const uint32_t *>(sa + rA * T::A_STRIDE + (kb >> 1) * 16 + 4 * t);
-                uint32_t w1 = *reinterpret_cast<const uint32_t *>(sa + (rA + 8) * T::A_STRIDE + (kb >> 1) * 16 + 4 * t);
-                a0 = (w0 >> sh) & 0x03030303u; a2 = (w0 >> (sh + 2)) & 0x03030303u;
-                a1 = (w1 >> sh) & 0x03030303u; a3 = (w1 >> (sh + 2)) & 0x03030303u;
+            // A fragments of the two k16 steps of this block: s0 = k 0..15, s1 = k 16..31
+            uint32_t a0[4], a1[4];  // {row g k 2t.., row g+8 k 2t.., row g k 2t+8.., row g+8 k 2t+8..}
+            {
+                const uint8_t *r0 = sa + rA * T::A_STRIDE, *r1 = r0 + 8 * T::A_STRIDE;
+                if (FMT == GPU_FMT_Q40) {
+                    const int o = kb * 16 + 2 * t;
+                    uint32_t p00 = spread2(*reinterpret_cast<const uint16_t *>(r0 + o));
+                    uint32_t p10 = spread2(*reinterpret_cast<const uint16_t *>(r1 + o));
+                    uint32_t p01 = spread2(*reinterpret_cast<const uint16_t *>(r0 + o + 8));
+                    uint32_t p11 = spread2(*reinterpret_cast<const uint16_t *>(r1 + o + 8));
+                    a0[0] = q4lo_h2(p00); a0[1] = q4lo_h2(p10); a0[2] = q4lo_h2(p01); a0[3] = q4lo_h2(p11);
+                    a1[0] = q4hi_h2(p00); a1[1] = q4hi_h2(p10); a1[2] = q4hi_h2(p01); a1[3] = q4hi_h2(p11);
+                } else if (FMT == GPU_FMT_Q80) {
+                    const int o = kb * 32 + 2 * t;
+                    a0[0] = s8_h2(spread2(*reinterpret_cast<const uint16_t *>(r0 + o)));
+                    a0[1] = s8_h2(spread2(*reinterpret_cast<const uint16_t *>(r1 + o)));
+                    a0[2] = s8_h2(spread2(*reinterpret_cast<const uint16_t *>(r0 + o + 8)));
+                    a0[3] = s8_h2(spread2(*reinterpret_cast<const uint16_t *>(r1 + o + 8)));
+                    a1[0] = s8_h2(spread2(*reinterpret_cast<const uint16_t *>(r0 + o + 16)));
+                    a1[1] = s8_h2(spread2(*reinterpret_cast<const uint16_t *>(r1 + o + 16)));
+                    a1[2] = s8_h2(spread2(*reinterpret_cast<const uint16_t *>(r0 + o + 24)));
+                    a1[3] = s8_h2(spread2(*reinterpret_cast<const uint16_t *>(r1 + o + 24)));
+                } else {
+                    const int o = (kb >> 1) * 16 + 2 * t, sh = (kb & 1) * 4;
+                    uint32_t p00 = spread2(*reinterpret_cast<const uint16_t *>(r0 + o));
+                    uint32_t p10 = spread2(*reinterpret_cast<const uint16_t *>(r1 + o));
+                    uint32_t p01 = spread2(*reinterpret_cast<const uint16_t *>(r0 + o + 8));
+                    uint32_t p11 = spread2(*reinterpret_cast<const uint16_t *>(r1 + o + 8));
+                    a0[0] = c2_h2(p00, sh); a0[1] = c2_h2(p10, sh); a0[2] = c2_h2(p01, sh); a0[3] = c2_h2(p11, sh);
+                    a1[0] = c2_h2(p00, sh + 2); a1[1] = c2_h2(p10, sh + 2);
+                    a1[2] = c2_h2(p01, sh + 2); a1[3] = c2_h2(p11, sh + 2);
+                }
             }
-            float dw0 = 1.f, dw1 = 1.f;
+            float2 dw0 = make_float2(1.f, 1.f), dw1 = make_float2(1.f, 1.f);
             if (T::HAS_WSCALE) {
                 const __half *hs = reinterpret_cast<const __half *>(sas);
-                dw0 = __half2float(hs[rA * G_BKB + kb]);
-                dw1 = __half2float(hs[(rA + 8) * G_BKB + kb]);
+                float w0 = __half2float(hs[rA * G_BKB + kb]), w1 = __half2float(hs[(rA + 8) * G_BKB + kb]);
+                dw0 = make_float2(w0, w0);
+                dw1 = make_float2(w1, w1);
             }
 #pragma unroll
             for (int j = 0; j < NT; j++) {
                 if (j < jv) {
-                    const uint8_t *pb = sb + (j * 8 + g) * L::B_STRIDE + kb * 32 + 4 * t;
-                    uint32_t b0 = *reinterpret_cast<const uint32_t *>(pb);
-                    uint32_t b1 = *reinterpret_cast<const uint32_t *>(pb + 16);
-                    int cc[4];
-                    mma_s8(cc, a0, a1, a2, a3, b0, b1);
-                    float dx0 = sbs[(j * 8 + 2 * t) * G_BKB + kb];
-                    float dx1 = sbs[(j * 8 + 2 * t + 1) * G_BKB + kb];
-                    if (T::HAS_WSCALE) {
-                        acc[j][0] = fmaf(dw0 * dx0, (float)cc[0], acc[j][0]);
-                        acc[j][1] = fmaf(dw0 * dx1, (float)cc[1], acc[j][1]);
-                        acc[j][2] = fmaf(dw1 * dx0, (float)cc[2], acc[j][2]);
-                        acc[j][3] = fmaf(dw1 * dx1, (float)cc[3], acc[j][3]);
+                    uint32_t b00, b01, b10, b11;  // step 0: k 2t.., k 2t+8..; step 1: +16
+                    if (B_HALF) {
+                        // lanes 0-7 address k 0-7 of rows n, 8-15 k 8-15, 16-23 k 16-23, 24-31 k 24-31
+                        const uint8_t *pb = sb + (j * 8 + (lane & 7)) * L::B_STRIDE + kb * 64 + (lane >> 3) * 16;
+                        ldsm_x4(b00, b01, b10, b11, pb);
                     } else {
-                        acc[j][0] = fmaf(dx0, (float)cc[0], acc[j][0]);
-                        acc[j][1] = fmaf(dx1, (float)cc[1], acc[j][1]);
-                        acc[j][2] = fmaf(dx0, (float)cc[2], acc[j][2]);
-                        acc[j][3] = fmaf(dx1, (float)cc[3], acc[j][3]);
+                        const uint8_t *pb = sb + (j * 8 + g) * L::B_STRIDE + kb * 32 + 2 * t;
+                        b00 = s8_h2(spread2(*reinterpret_cast<const uint16_t *>(pb)));
+                        b01 = s8_h2(spread2(*reinterpret_cast<const uint16_t *>(pb + 8)));
+                        b10 = s8_h2(spread2(*reinterpret_cast<const uint16_t *>(pb + 16)));
+                        b11 = s8_h2(spread2(*reinterpret_cast<const uint16_t *>(pb + 24)));
+                    }
+                    float d[4];
+                    mma_f16(d, a0[0], a0[1], a0[2], a0[3], b00, b01, 0.f, 0.f, 0.f, 0.f);
+                    mma_f16(d, a1[0], a1[1], a1[2], a1[3], b10, b11, d[0], d[1], d[2], d[3]);
+                    // d = this block's exact integer sums; scale by dw*dx and accumulate
+                    const float2 dx = *reinterpret_cast<const float2 *>(sbs + kb * BN + j * 8 + 2 * t);
+                    if (T::HAS_WSCALE) {
+                        acc[j][0] = ffma2(fmul2(dw0, dx), make_float2(d[0], d[1]), acc[j][0]);
+                        acc[j][1] = ffma2(fmul2(dw1, dx), make_float2(d[2], d[3]), acc[j][1]);
+                    } else {
+                        acc[j][0] = ffma2(dx, make_float2(d[0], d[1]), acc[j][0]);
+                        acc[j][1] = ffma2(dx, make_float2(d[2], d[3]), acc[j][1]);
                     }
                 }
             }
@@ -301,10 +381,8 @@ __global__ void __launch_bounds__(G_THREADS) k_gemm(GemmArgs a) {
     constexpr int CS = BN + 4;
 #pragma unroll
     for (int j = 0; j < NT; j++) {
-        ct[rA * CS + j * 8 + 2 * t] = acc[j][0];
-        ct[rA * CS + j * 8 + 2 * t + 1] = acc[j][1];
-        ct[(rA + 8) * CS + j * 8 + 2 * t] = acc[j][2];
-        ct[(rA + 8) * CS + j * 8 + 2 * t + 1] = acc[j][3];
+        *reinterpret_cast<float2 *>(ct + rA * CS + j * 8 + 2 * t) = acc[j][0];
+        *reinterpret_cast<float2 *>(ct + (rA + 8) * CS + j * 8 + 2 * t) = acc[j][1];
     }
     __syncthreads();
 
@@ -343,6 +421,7 @@ __global__ void __launch_bounds__(G_THREADS) k_gemm(GemmArgs a) {
             int8_t q = quant_lane(h, d);
             const size_t pr = (size_t)(it.row0 + n);
             a.hq[pr * MI + f0 + f] = q;
+            a.hh[pr * MI + f0 + f] = __int2half_rn(q);
             if (lane == 0) a.hs[pr * nbh + f0 / 32 + hb] = d;
             if (FMT == GPU_FMT_TQ2) {
                 int s = q;

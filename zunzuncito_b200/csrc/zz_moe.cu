@@ -29,31 +29,35 @@ int launch_repack(int fmt, const uint8_t *src, long src_expert_stride, int rows,
 int launch_gemv1(const zz_qtensor *W, const int8_t *xq, const float *sx, const float *sxtot, float *y,
                  cudaStream_t st);
 int launch_blocksums(const zz_qtensor *W, const int8_t *xq, int32_t *out, cudaStream_t st);
+int launch_quant_act(const float *x, int S, int I, int8_t *xq, float *sx, float *sxtot, __half *xh,
+                     cudaStream_t st);
+int launch_s8_to_h(const int8_t *q, __half *h, long n, cudaStream_t st);
 
 constexpr int MOE_BN = 64;
 constexpr int DENSE_BN = 64;
 
 static inline size_t a256(size_t n) { return (n + 255) & ~(size_t)255; }
 
-template <int FMT, int BN, int EPI>
+template <int FMT, int BN, int EPI, bool BH>
 static int launch_gemm_t(const GemmArgs &a, dim3 grid, cudaStream_t st) {
-    constexpr int smem = GemmSmem<FMT, BN>::TOTAL;
+    constexpr int smem = GemmSmem<FMT, BN, BH>::TOTAL;
     static bool attr_set = false;  // per process; the library drives one device
     if (!attr_set) {
-        if (!check_cuda(cudaFuncSetAttribute(k_gemm<FMT, BN, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem),
+        if (!check_cuda(cudaFuncSetAttribute(k_gemm<FMT, BN, EPI, BH>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             smem),
                         "gemm smem attribute"))
             return 0;
         attr_set = true;
     }
-    k_gemm<FMT, BN, EPI><<<grid, G_THREADS, smem, st>>>(a);
+    k_gemm<FMT, BN, EPI, BH><<<grid, G_THREADS, smem, st>>>(a);
     return check_cuda(cudaGetLastError(), "gemm launch");
 }
 
-template <int EPI, int BN>
+template <int EPI, int BN, bool BH>
 static int launch_gemm(int fmt, const GemmArgs &a, dim3 grid, cudaStream_t st) {
-    if (fmt == GPU_FMT_Q40) return launch_gemm_t<GPU_FMT_Q40, BN, EPI>(a, grid, st);
-    if (fmt == GPU_FMT_Q80) return launch_gemm_t<GPU_FMT_Q80, BN, EPI>(a, grid, st);
-    return launch_gemm_t<GPU_FMT_TQ2, BN, EPI>(a, grid, st);
+    if (fmt == GPU_FMT_Q40) return launch_gemm_t<GPU_FMT_Q40, BN, EPI, BH>(a, grid, st);
+    if (fmt == GPU_FMT_Q80) return launch_gemm_t<GPU_FMT_Q80, BN, EPI, BH>(a, grid, st);
+    return launch_gemm_t<GPU_FMT_TQ2, BN, EPI, BH>(a, grid, st);
 }
 
 // ---------------------------------------------------------------- routing
@@ -102,10 +106,10 @@ __global__ void k_count_bad(const int32_t *eidx, int P, int E, int *bad) {
 }
 
 struct MoeWs {
-    int8_t *xq; float *xs, *xsx;
+    int8_t *xq; float *xs, *xsx; __half *xh;
     int *pair_src; float *pair_w;
     WorkItem *items; int *n_items;
-    int8_t *hq; float *hs; int *hblk;
+    int8_t *hq; float *hs; int *hblk; __half *hh;
     int *bad;
     size_t total;
 };
@@ -119,6 +123,7 @@ static MoeWs moe_layout(const zz_expert_bank *b, int S, int K, uint8_t *base) {
     w.xq = (int8_t *)take((size_t)S * D);
     w.xs = (float *)take((size_t)S * (D / 32) * 4);
     w.xsx = (float *)take((size_t)S * 4);
+    w.xh = (__half *)take((size_t)S * D * 2);
     w.pair_src = (int *)take(P * 4);
     w.pair_w = (float *)take(P * 4);
     w.items = (WorkItem *)take(maxit * sizeof(WorkItem));
@@ -126,6 +131,7 @@ static MoeWs moe_layout(const zz_expert_bank *b, int S, int K, uint8_t *base) {
     w.hq = (int8_t *)take(P * MI);
     w.hs = (float *)take(P * (MI / 32) * 4);
     w.hblk = (int *)take(P * (MI / 32) * 4);
+    w.hh = (__half *)take(P * MI * 2);
     w.bad = (int *)take(4);
     w.total = o;
     return w;
@@ -282,11 +288,12 @@ static int moe_impl(const zz_expert_bank *b, const float *X, const int8_t *xq_in
     const int8_t *xq = xq_in;
     const float *xs = xs_in;
     if (X) {
-        if (!zz_quant_act_dev(X, S, D, w.xq, w.xs, fmt == GPU_FMT_TQ2 ? w.xsx : nullptr, stream)) return 0;
+        if (!launch_quant_act(X, S, D, w.xq, w.xs, fmt == GPU_FMT_TQ2 ? w.xsx : nullptr, w.xh, st)) return 0;
         xq = w.xq;
         xs = w.xs;
-    } else if (fmt == GPU_FMT_TQ2) {
-        k_rows_sx<<<(S + 127) / 128, 128, 0, st>>>(xq, xs, S, D, w.xsx);
+    } else {
+        if (fmt == GPU_FMT_TQ2) k_rows_sx<<<(S + 127) / 128, 128, 0, st>>>(xq, xs, S, D, w.xsx);
+        if (!launch_s8_to_h(xq, w.xh, (long)S * D, st)) return 0;
     }
     k_route<<<1, 1024, 4 * E * sizeof(int), st>>>(eidx, ewt, P, E, MOE_BN, w.pair_src, w.pair_w, w.items, w.n_items);
     if (!check_cuda(cudaGetLastError(), "route launch")) return 0;
@@ -296,12 +303,12 @@ static int moe_impl(const zz_expert_bank *b, const float *X, const int8_t *xq_in
     g.codes_gstride = (long)codes_bytes(fmt, 2 * MI, D);
     g.scale_gstride = (long)scales_bytes(fmt, 2 * MI, D);
     g.O = 2 * MI; g.I = D;
-    g.xq = xq; g.xs = xs; g.xsx = w.xsx; g.xblk = nullptr; g.gather = w.pair_src; g.gather_div = K;
+    g.xq = w.xh; g.xs = xs; g.xsx = w.xsx; g.xblk = nullptr; g.gather = w.pair_src; g.gather_div = K;
     g.items = w.items; g.n_items = w.n_items;
     g.act = act; g.clamp = clamp;
-    g.hq = w.hq; g.hs = w.hs; g.hblk = w.hblk;
+    g.hq = w.hq; g.hs = w.hs; g.hblk = w.hblk; g.hh = w.hh;
     prof_mark(st);
-    if (!launch_gemm<EPI_GATEUP, MOE_BN>(fmt, g, dim3((2 * MI) / G_BM, maxit), st)) return 0;
+    if (!launch_gemm<EPI_GATEUP, MOE_BN, true>(fmt, g, dim3((2 * MI) / G_BM, maxit), st)) return 0;
     prof_mark(st);
 
     GemmArgs d{};
@@ -309,10 +316,10 @@ static int moe_impl(const zz_expert_bank *b, const float *X, const int8_t *xq_in
     d.codes_gstride = (long)codes_bytes(fmt, D, MI);
     d.scale_gstride = (long)scales_bytes(fmt, D, MI);
     d.O = D; d.I = MI;
-    d.xq = w.hq; d.xs = w.hs; d.xsx = nullptr; d.xblk = fmt == GPU_FMT_TQ2 ? w.hblk : nullptr; d.gather = nullptr;
+    d.xq = w.hh; d.xs = w.hs; d.xsx = nullptr; d.xblk = fmt == GPU_FMT_TQ2 ? w.hblk : nullptr; d.gather = nullptr;
     d.items = w.items; d.n_items = w.n_items;
     d.out = OUT; d.pair_w = w.pair_w; d.pair_src = w.pair_src; d.K = K;
-    int ok = launch_gemm<EPI_DOWN, MOE_BN>(fmt, d, dim3((D + G_BM - 1) / G_BM, maxit), st);
+    int ok = launch_gemm<EPI_DOWN, MOE_BN, true>(fmt, d, dim3((D + G_BM - 1) / G_BM, maxit), st);
     prof_mark(st);
     return ok;
 }
@@ -348,6 +355,6 @@ int matvec_impl(const zz_qtensor *W, const int8_t *xq, const float *sx, const fl
     g.xq = xq; g.xs = sx; g.xsx = sxtot;
     g.items = nullptr; g.n_items = nullptr; g.rows_total = S;
     g.y = y;
-    return launch_gemm<EPI_STORE, DENSE_BN>(W->fmt, g, dim3((W->O + G_BM - 1) / G_BM, n), st);
+    return launch_gemm<EPI_STORE, DENSE_BN, false>(W->fmt, g, dim3((W->O + G_BM - 1) / G_BM, n), st);
 }
 }  // namespace zz

@@ -33,7 +33,7 @@ size_t scales_bytes(int fmt, int O, int I) { return align256((size_t)O * scale_r
 // q40_quant_act (q40.h:124-138); with sxtot, the tq2 total of tq2_quant_act
 // (tq2.h:98-108) summed serially in double in block order, then rounded to f32.
 __global__ void k_quant_act(const float *__restrict__ x, int I, int8_t *__restrict__ xq,
-                            float *__restrict__ sx, float *__restrict__ sxtot) {
+                            float *__restrict__ sx, float *__restrict__ sxtot, __half *__restrict__ xh) {
     extern __shared__ int blk_sum[];
     const int row = blockIdx.x, nb = I / ZZ_BLK;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
@@ -42,6 +42,7 @@ __global__ void k_quant_act(const float *__restrict__ x, int I, int8_t *__restri
         float v = xr[b * ZZ_BLK + lane], d;
         int8_t q = quant_lane(v, d);
         xq[(size_t)row * I + b * ZZ_BLK + lane] = q;
+        if (xh) xh[(size_t)row * I + b * ZZ_BLK + lane] = __int2half_rn(q);
         if (lane == 0) sx[(size_t)row * nb + b] = d;
         if (sxtot) {
             int s = q;
@@ -252,13 +253,31 @@ extern "C" int zz_quant_rows_dev(int fmt, const float *w, int O, int I, uint8_t 
     return check_cuda(cudaGetLastError(), "quant_rows launch");
 }
 
+// int8 rows -> the same values as fp16 (activations that arrive already quantized)
+__global__ void k_s8_to_h(const int8_t *__restrict__ q, __half *__restrict__ h, long n) {
+    long i = (long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n) h[i] = __int2half_rn(q[i]);
+}
+namespace zz {
+int launch_s8_to_h(const int8_t *q, __half *h, long n, cudaStream_t st) {
+    if (n <= 0) return 1;
+    k_s8_to_h<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(q, h, n);
+    return check_cuda(cudaGetLastError(), "s8_to_h launch");
+}
+// quantize rows; xh (optional) receives the int8 codes as fp16 for the GEMM's B operand
+int launch_quant_act(const float *x, int S, int I, int8_t *xq, float *sx, float *sxtot, __half *xh,
+                     cudaStream_t st) {
+    size_t smem = sxtot ? (size_t)(I / ZZ_BLK) * sizeof(int) : 0;
+    if (smem > 48 * 1024) return fail("quant_act: I=%d too large for the Sx reduction", I);
+    k_quant_act<<<S, 256, smem, st>>>(x, I, xq, sx, sxtot, xh);
+    return check_cuda(cudaGetLastError(), "quant_act launch");
+}
+}  // namespace zz
+
 extern "C" int zz_quant_act_dev(const float *x, int S, int I, int8_t *xq, float *sx, float *sxtot,
                                 void *stream) {
     if (S < 0 || I <= 0 || I % 32) return fail("zz_quant_act_dev: I=%d must be a positive multiple of 32", I);
     if (S == 0) return 1;
     if (!x || !xq || !sx) return fail("zz_quant_act_dev: null pointer");
-    size_t smem = sxtot ? (size_t)(I / ZZ_BLK) * sizeof(int) : 0;
-    if (smem > 48 * 1024) return fail("zz_quant_act_dev: I=%d too large for the Sx reduction", I);
-    k_quant_act<<<S, 256, smem, (cudaStream_t)stream>>>(x, I, xq, sx, sxtot);
-    return check_cuda(cudaGetLastError(), "quant_act launch");
+    return launch_quant_act(x, S, I, xq, sx, sxtot, nullptr, (cudaStream_t)stream);
 }

@@ -1,0 +1,149 @@
+"""Expert parallelism for the batch-union MoE layer across the GPUs of one node.
+
+The reference is single-process (OpenMP over rows, no collectives). On a B200 node the
+routed experts of a layer are sharded contiguously, rank r holding experts
+[r*E/G, (r+1)*E/G), and tokens stay data-parallel: each rank owns its own S tokens.
+One layer is then
+
+  1. quantize the rank's tokens to q8_0 once (3168 B per row at D=2816 instead of
+     11264 B of f32)
+  2. dispatch: one row per (token, destination rank) that holds at least one of the
+     token's top-K experts, carrying the q8_0 row and the token's routing restricted to
+     that rank (local expert ids, -1 elsewhere) -- an NCCL all-to-all
+  3. the destination runs the batch-union FFN over everything it received
+     (zz_moe_ffn_q8_dev), which already sums that rank's experts per row
+  4. combine: the f32 partial rows go back with the reverse all-to-all and are added
+     into the token's output.
+
+The exchange is the only collective; dense weights are replicated. ``ep_moe_layer``
+takes the local FFN as a callable so the exchange logic runs unchanged on CPU ranks
+over gloo (tests) and on GPU ranks over NCCL (bench).
+"""
+import os
+
+import numpy as np
+import torch
+import torch.distributed as dist
+
+
+def _a2a_counts(send_counts, group):
+    recv = torch.empty_like(send_counts)
+    dist.all_to_all_single(recv, send_counts, group=group)
+    return recv
+
+
+def ep_moe_layer(xq, xs, eidx, ewt, n_experts, local_ffn, group=None):
+    """One expert-parallel MoE layer on this rank's tokens.
+
+    xq [S, D] int8, xs [S, D/32] f32: this rank's quantized tokens; eidx [S, K] int32
+    global expert ids, ewt [S, K] f32. local_ffn(xq_r, xs_r, eidx_r, ewt_r) -> [R, D]
+    f32 runs this rank's experts (local ids, -1 = skip) over the R received rows.
+    Returns out [S, D] f32 = sum_k ewt[s,k] * FFN_{eidx[s,k]}(x_s)."""
+    world = dist.get_world_size(group)
+    rank = dist.get_rank(group)
+    dev = xq.device
+    S, D = xq.shape
+    K = eidx.shape[1]
+    nb = xs.shape[1]
+    per = n_experts // world
+    dst = (eidx // per).long()                                            # [S, K]
+    onehot = torch.zeros((S, world), dtype=torch.bool, device=dev)
+    onehot.scatter_(1, dst, True)
+    # rows grouped by destination, tokens ascending within a destination
+    d_idx, s_idx = onehot.t().nonzero(as_tuple=True)
+    send_counts = onehot.sum(0).to(torch.int64)
+    # routing restricted to the destination, as local ids (or -1)
+    loc = eidx[s_idx].long() - d_idx[:, None] * per
+    mine = (loc >= 0) & (loc < per)
+    loc_e = torch.where(mine, loc, torch.full_like(loc, -1)).to(torch.int32)
+    loc_w = torch.where(mine, ewt[s_idx], torch.zeros_like(ewt[s_idx]))
+    # one byte row per dispatched (token, destination): q8 codes | scales | ids | weights
+    payload = torch.cat([xq[s_idx].view(torch.uint8), xs[s_idx].contiguous().view(torch.uint8),
+                         loc_e.contiguous().view(torch.uint8), loc_w.contiguous().view(torch.uint8)], dim=1)
+    row_bytes = D + 4 * nb + 8 * K
+    recv_counts = _a2a_counts(send_counts, group)
+    sc, rc = send_counts.tolist(), recv_counts.tolist()
+    recv = torch.empty((sum(rc), row_bytes), dtype=torch.uint8, device=dev)
+    dist.all_to_all_single(recv, payload, output_split_sizes=rc, input_split_sizes=sc, group=group)
+    R = recv.shape[0]
+    r_xq = recv[:, :D].contiguous().view(torch.int8)
+    r_xs = recv[:, D:D + 4 * nb].contiguous().view(torch.float32)
+    r_e = recv[:, D + 4 * nb:D + 4 * nb + 4 * K].contiguous().view(torch.int32)
+    r_w = recv[:, D + 4 * nb + 4 * K:].contiguous().view(torch.float32)
+    part = local_ffn(r_xq, r_xs, r_e, r_w) if R else torch.zeros((0, D), dtype=torch.float32, device=dev)
+    back = torch.empty((len(s_idx), D), dtype=torch.float32, device=dev)
+    dist.all_to_all_single(back, part.contiguous(), output_split_sizes=sc, input_split_sizes=rc, group=group)
+    out = torch.zeros((S, D), dtype=torch.float32, device=dev)
+    out.index_add_(0, s_idx, back)
+    return out
+
+
+# ----------------------------------------------------------------------------- bench
+def bench_main(a, rank, world):
+    """bench.py under torchrun: weak scaling, each rank S tokens and E/G experts per
+    layer of the 30-layer Gemma-4 stack; time = max over ranks of the device time."""
+    import json
+    import time
+
+    import zunzuncito_b200 as zz
+    from zunzuncito_b200 import synth
+
+    local = int(os.environ.get("LOCAL_RANK", rank))
+    torch.cuda.set_device(local)
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    import datetime
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=torch.device("cuda", local))
+    D, MI, E, K = synth.GEMMA_D, synth.GEMMA_MI, synth.GEMMA_E, synth.GEMMA_K
+    per = E // world
+    S, L = a.tokens, a.layers
+    stride = zz.expert_blob_bytes(zz.GPU_FMT_Q40, D, MI)
+    gb = zz.ref_tensor_bytes(zz.GPU_FMT_Q40, MI, D)
+    g = torch.Generator(device="cuda").manual_seed(1234 + rank)
+    banks = []
+    for _ in range(L):
+        blobs = torch.empty((per, stride), dtype=torch.uint8, device="cuda")
+        for i, (O, I) in enumerate([(MI, D), (MI, D), (D, MI)]):
+            w = torch.randn((per * O, I), generator=g, device="cuda") * 0.02
+            q = zz.quant_rows(zz.GPU_FMT_Q40, w).view(per, -1)
+            blobs[:, i * gb:i * gb + q.shape[1]] = q
+            del w, q
+        banks.append(zz.ExpertBankDev(zz.GPU_FMT_Q40, blobs, D, MI))
+        del blobs
+    routes = [synth.zipf_routing(99 + 17 * l + 100003 * rank, S, E, K)[:2] for l in range(L)]
+    X = torch.from_numpy(synth.gaussian(7 + rank, (S, D))).cuda()
+    eidx = [torch.from_numpy(r[0]).cuda() for r in routes]
+    ewt = [torch.from_numpy(r[1]).cuda() for r in routes]
+
+    def step():
+        for l in range(L):
+            xq, xs, _ = zz.quant_act(X)
+            ffn = lambda q, s, e, w, b=banks[l]: zz.moe_ffn_q8(b, q, s, e, w, zz.ZZ_ACT_GEGLU_TANH)
+            ep_moe_layer(xq, xs, eidx[l], ewt[l], E, ffn)
+
+    for _ in range(a.warmup):
+        step()
+    torch.cuda.synchronize()
+    dist.barrier()
+    torch.cuda.synchronize()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record()
+    for _ in range(a.steps):
+        step()
+    t1.record()
+    torch.cuda.synchronize()
+    ms = torch.tensor([t0.elapsed_time(t1) / a.steps], device="cuda")
+    dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+    dist.barrier()
+    ms = float(ms.item())
+    if rank == 0:
+        value = S * world * L / (ms / 1e3)
+        line = {"metric": "moe_layer_tok_per_s", "value": value, "unit": "token-layers/s", "n_gpus": world,
+                "steps": a.steps, "warmup": a.warmup, "ms_per_step": ms, "higher_is_better": True,
+                "scaling": "weak", "vs_baseline": None, "dtype": "int8", "data": "synthetic",
+                "config": {"workload": f"Gemma-4 batch-union MoE stack, {L} layers x 128 q4_0 experts sharded "
+                                       f"{per}/GPU, S={S} tokens per GPU per step, top-8 Zipf(1.1), NCCL all-to-all "
+                                       "of q8_0 rows", "tokens_per_gpu": S, "layers": L, "parallelism": f"ep{world}",
+                           "l2": "no flush: per-layer expert reads exceed L2"},
+                "gpu_launches": a.steps * L * 5}
+        print(json.dumps(line), flush=True)
+    dist.destroy_process_group()
