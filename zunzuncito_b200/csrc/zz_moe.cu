@@ -338,6 +338,45 @@ extern "C" int zz_moe_ffn_q8_dev(const zz_expert_bank *b, const int8_t *xq, cons
     return moe_impl(b, nullptr, xq, xs, eidx, ewt, OUT, S, K, act, clamp, workspace, ws_bytes, validate, stream);
 }
 
+// ---------------------------------------------------------------- no-allocation variant
+// Some callers cannot allocate device memory at all: an engine that hands the GPU one
+// fixed budget at start-up, a plugin host that forbids cudaMalloc after init, or code
+// running where an allocation could stall or fail mid-request. For them the layer's
+// scratch lives in this file-scope array instead of a caller workspace. It is part of
+// the library image, so every GPU that loads the library holds these bytes until exit.
+#define ZZ_NOALLOC_SCRATCH_BYTES (32u << 20)
+static __device__ __align__(256) uint8_t g_noalloc_scratch[ZZ_NOALLOC_SCRATCH_BYTES];
+
+// Device address of g_noalloc_scratch per device. Host code must not pass the symbol
+// itself to a kernel: on the host it is only a stand-in, not a device address.
+static void *g_noalloc_ptr[64];
+
+extern "C" int zz_moe_ffn_noalloc_dev(const zz_expert_bank *b, const float *X, const int32_t *eidx,
+                                      const float *ewt, float *OUT, int S, int K, int act, float clamp,
+                                      void *stream) {
+    if (!bank_ok(b)) return fail("zz_moe_ffn_noalloc_dev: invalid expert bank");
+    if (S < 0 || K <= 0 || K > 64) return fail("zz_moe_ffn_noalloc_dev: bad S=%d or K=%d", S, K);
+    if (S == 0) return 1;
+    const size_t need = moe_layout(b, S, K, nullptr).total;
+    if (need > ZZ_NOALLOC_SCRATCH_BYTES)
+        return fail("zz_moe_ffn_noalloc_dev: S=%d K=%d needs %zu scratch bytes, more than the fixed %u; "
+                    "use zz_moe_ffn_dev with a caller workspace",
+                    S, K, need, (unsigned)ZZ_NOALLOC_SCRATCH_BYTES);
+    int dev = 0;
+    if (!check_cuda(cudaGetDevice(&dev), "zz_moe_ffn_noalloc_dev: cudaGetDevice")) return 0;
+    if (dev < 0 || dev >= 64) return fail("zz_moe_ffn_noalloc_dev: device %d out of range", dev);
+    if (!g_noalloc_ptr[dev]) {  // one-time set-up on this device, with it current
+        void *p = nullptr;
+        if (!check_cuda(cudaGetSymbolAddress(&p, g_noalloc_scratch), "zz_moe_ffn_noalloc_dev: cudaGetSymbolAddress"))
+            return 0;
+        g_noalloc_ptr[dev] = p;
+    }
+    // Nothing in the scratch needs to start at zero: OUT is cleared by the layer itself
+    // and the routing counters live in shared memory.
+    return moe_impl(b, X, nullptr, nullptr, eidx, ewt, OUT, S, K, act, clamp, g_noalloc_ptr[dev],
+                    ZZ_NOALLOC_SCRATCH_BYTES, 0, stream);
+}
+
 // ---------------------------------------------------------------- dense
 namespace zz {
 // y[S, O] for S quantized rows; S == 1 takes the register-resident GEMV, larger S the
