@@ -58,6 +58,8 @@ def ws_views(bank, S, K):
     src = ws[off(0):off(0) + 4 * P].view(torch.int32).cpu().numpy()
     hq = ws[off(2):off(2) + P * MI].view(torch.int8).cpu().numpy().reshape(P, MI)
     hs = ws[off(3):off(3) + P * (MI // 32) * 4].view(torch.float32).cpu().numpy().reshape(P, MI // 32)
+    err = int(ws[off(5):off(5) + 4].view(torch.int32).cpu().numpy()[0])
+    assert err == 0, f"tensor-core pipeline wait {err} ran out"
     return src, hq, hs
 
 

@@ -14,6 +14,8 @@
 //      epilogue (gemma4.c:647-651)
 // Each distinct expert's weights cross HBM once per item; items of one expert are
 // adjacent in the grid so repeated reads of the same expert hit L2.
+#include <cstdlib>
+#include <cstring>
 #include <vector>
 #include "zz_gemm.cuh"
 
@@ -32,6 +34,14 @@ int launch_blocksums(const zz_qtensor *W, const int8_t *xq, int32_t *out, cudaSt
 int launch_quant_act(const float *x, int S, int I, int8_t *xq, float *sx, float *sxtot, __half *xh,
                      cudaStream_t st);
 int launch_s8_to_h(const int8_t *q, __half *h, long n, cudaStream_t st);
+int launch_moe_tc(int fmt, int epi, const GemmArgs &a, int n_groups, int *err, cudaStream_t st);
+
+// tcgen05 path unless ZZ_MOE_KERNEL=mma asks for the mma.sync one (for comparisons)
+static bool use_tc() {
+    const char *e = getenv("ZZ_MOE_KERNEL");
+    return !(e && !strcmp(e, "mma"));
+}
+constexpr int TC_BN = 128;
 
 constexpr int MOE_BN = 64;
 constexpr int DENSE_BN = 64;
@@ -111,6 +121,7 @@ struct MoeWs {
     WorkItem *items; int *n_items;
     int8_t *hq; float *hs; int *hblk; __half *hh;
     int *bad;
+    int *tcerr;
     size_t total;
 };
 
@@ -133,6 +144,7 @@ static MoeWs moe_layout(const zz_expert_bank *b, int S, int K, uint8_t *base) {
     w.hblk = (int *)take(P * (MI / 32) * 4);
     w.hh = (__half *)take(P * MI * 2);
     w.bad = (int *)take(4);
+    w.tcerr = (int *)take(4);
     w.total = o;
     return w;
 }
@@ -231,7 +243,7 @@ extern "C" size_t zz_moe_workspace_offset(const zz_expert_bank *b, int S, int K,
     MoeWs w = moe_layout(b, S, K, base);
     const void *p = which == 0 ? (const void *)w.pair_src : which == 1 ? (const void *)w.pair_w
                   : which == 2 ? (const void *)w.hq : which == 3 ? (const void *)w.hs
-                  : which == 4 ? (const void *)w.n_items : nullptr;
+                  : which == 4 ? (const void *)w.n_items : which == 5 ? (const void *)w.tcerr : nullptr;
     if (!p) return (size_t)-1;
     return (size_t)((const uint8_t *)p - base);
 }
@@ -295,7 +307,9 @@ static int moe_impl(const zz_expert_bank *b, const float *X, const int8_t *xq_in
         if (fmt == GPU_FMT_TQ2) k_rows_sx<<<(S + 127) / 128, 128, 0, st>>>(xq, xs, S, D, w.xsx);
         if (!launch_s8_to_h(xq, w.xh, (long)S * D, st)) return 0;
     }
-    k_route<<<1, 1024, 4 * E * sizeof(int), st>>>(eidx, ewt, P, E, MOE_BN, w.pair_src, w.pair_w, w.items, w.n_items);
+    const bool tcp = use_tc();
+    k_route<<<1, 1024, 4 * E * sizeof(int), st>>>(eidx, ewt, P, E, tcp ? TC_BN : MOE_BN, w.pair_src, w.pair_w, w.items,
+                                                  w.n_items);
     if (!check_cuda(cudaGetLastError(), "route launch")) return 0;
 
     GemmArgs g{};
@@ -308,7 +322,12 @@ static int moe_impl(const zz_expert_bank *b, const float *X, const int8_t *xq_in
     g.act = act; g.clamp = clamp;
     g.hq = w.hq; g.hs = w.hs; g.hblk = w.hblk; g.hh = w.hh;
     prof_mark(st);
-    if (!launch_gemm<EPI_GATEUP, MOE_BN, true>(fmt, g, dim3((2 * MI) / G_BM, maxit), st)) return 0;
+    if (tcp) {
+        if (!check_cuda(cudaMemsetAsync(w.tcerr, 0, 4, st), "memset")) return 0;
+        if (!launch_moe_tc(fmt, EPI_GATEUP, g, E, w.tcerr, st)) return 0;
+    } else if (!launch_gemm<EPI_GATEUP, MOE_BN, true>(fmt, g, dim3((2 * MI) / G_BM, maxit), st)) {
+        return 0;
+    }
     prof_mark(st);
 
     GemmArgs d{};
@@ -319,7 +338,8 @@ static int moe_impl(const zz_expert_bank *b, const float *X, const int8_t *xq_in
     d.xq = w.hh; d.xs = w.hs; d.xsx = nullptr; d.xblk = fmt == GPU_FMT_TQ2 ? w.hblk : nullptr; d.gather = nullptr;
     d.items = w.items; d.n_items = w.n_items;
     d.out = OUT; d.pair_w = w.pair_w; d.pair_src = w.pair_src; d.K = K;
-    int ok = launch_gemm<EPI_DOWN, MOE_BN, true>(fmt, d, dim3((D + G_BM - 1) / G_BM, maxit), st);
+    int ok = tcp ? launch_moe_tc(fmt, EPI_DOWN, d, E, w.tcerr, st)
+                 : launch_gemm<EPI_DOWN, MOE_BN, true>(fmt, d, dim3((D + G_BM - 1) / G_BM, maxit), st);
     prof_mark(st);
     return ok;
 }
