@@ -176,6 +176,9 @@ int zz_moe_ffn_noalloc_dev(const zz_expert_bank *bank, const float *X, const int
  *   4 n_items  int32                 work items of the last call
  *   5 tc_error int32                 0, or the id of a tensor-core pipeline wait that
  *                                    ran out (the call's results are then invalid)
+ * Pair rows are grouped by expert with each expert's rows starting on a 16-row
+ * boundary; padding rows hold pair_src = -1. which = 6 returns the number of pair
+ * rows (capacity incl. padding) instead of an offset.
  * so tests can check the gate/up stage bit for bit. (size_t)-1 for an unknown id.
  * No reference counterpart (the engines keep these in Buf: gemma4.c:2123-2127). */
 size_t zz_moe_workspace_offset(const zz_expert_bank *bank, int S, int K, int which);

@@ -19,6 +19,7 @@ from zunzuncito_b200 import synth
 
 pytestmark = pytest.mark.gpu
 
+ENGINES = ("mma", "tc")
 KINDS = {0: (zz.GPU_FMT_Q40, zz.ZZ_ACT_GEGLU_TANH), 1: (zz.GPU_FMT_Q40, zz.ZZ_ACT_SWIGLU),
          2: (zz.GPU_FMT_Q80, zz.ZZ_ACT_SWIGLU), 3: (zz.GPU_FMT_TQ2, zz.ZZ_ACT_SWIGLU_CLAMP)}
 CLAMP = 7.0
@@ -52,15 +53,19 @@ def split_blob(fmt, blob, D, MI):
 
 
 def ws_views(bank, S, K):
+    """pair rows of the last call (padding rows, src < 0, dropped), their hq / hs"""
     ws = bank._ws
-    P, MI = S * K, bank.MI
+    MI = bank.MI
     off = lambda w: zz.lib.zz_moe_workspace_offset(ctypes.byref(bank.b), S, K, w)
+    P = off(6)  # pair-row capacity incl. per-expert alignment padding
     src = ws[off(0):off(0) + 4 * P].view(torch.int32).cpu().numpy()
     hq = ws[off(2):off(2) + P * MI].view(torch.int8).cpu().numpy().reshape(P, MI)
     hs = ws[off(3):off(3) + P * (MI // 32) * 4].view(torch.float32).cpu().numpy().reshape(P, MI // 32)
     err = int(ws[off(5):off(5) + 4].view(torch.int32).cpu().numpy()[0])
     assert err == 0, f"tensor-core pipeline wait {err} ran out"
-    return src, hq, hs
+    keep = src >= 0
+    assert keep.sum() == S * K
+    return src[keep], hq[keep], hs[keep]
 
 
 def matvec(orc, fmt, T, O, xq, sx, tot):
@@ -118,9 +123,17 @@ def check_pairs(orc, kind, blobs, X, eidx, ewt, out_gpu, bank, pairs=None):
     return flipped_tok
 
 
+@pytest.fixture(params=["auto", "mma", "tc", "dec"])
+def engine(request, monkeypatch):
+    """every expert engine: auto (GEMV for small S*K, else mma.sync), mma.sync, tcgen05,
+    and the small-batch GEMV kernels forced (ZZ_MOE_KERNEL)"""
+    monkeypatch.setenv("ZZ_MOE_KERNEL", request.param)
+    return request.param
+
+
 @pytest.mark.parametrize("kind", [0, 1, 2, 3])
 @pytest.mark.parametrize("S", [1, 7, 100])
-def test_moe_small(orc, kind, S):
+def test_moe_small(orc, kind, S, engine):
     fmt, act = KINDS[kind]
     E, D, MI, K = 8, 256, 128, 2 if S > 1 else 4
     blobs = make_blobs(orc, kind, 300 + kind, E, D, MI)
@@ -139,7 +152,7 @@ def test_moe_small(orc, kind, S):
 
 
 @pytest.mark.parametrize("key,kind", [("g4", 0), ("mp", 3)])
-def test_moe_golden(orc, key, kind):
+def test_moe_golden(orc, key, kind, engine):
     import os
     G = np.load(os.path.join(os.path.dirname(__file__), "golden", "golden.npz"))
     E, D, MI, K, S = (int(v) for v in G["dims"])
@@ -183,7 +196,7 @@ def _full_layer(seed, S):
     return blobs, X, eidx, ewt
 
 
-def test_moe_full_layer_config3(orc):
+def test_moe_full_layer_config3(orc, engine):
     S = 512
     blobs, X, eidx, ewt = _full_layer(600, S)
     D, MI = synth.GEMMA_D, synth.GEMMA_MI

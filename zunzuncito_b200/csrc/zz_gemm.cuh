@@ -83,6 +83,11 @@ struct GemmArgs {
     const float *pair_w;     // [pair]
     const int *pair_src;     // [pair] routing slot s*K+k of the pair
     int K;
+    // tensor-core path: B rows in pair order and transposed block scales
+    const __half *xg;        // [rows_cap][I] fp16
+    const float *xsT;        // [I/32][ldT]
+    int ldT, rows_cap;
+    float *hsT;              // gate/up: transposed hidden scales [O/64][ldT]
 };
 
 __device__ __forceinline__ void mma_f16(float d[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,

@@ -35,15 +35,25 @@ int launch_quant_act(const float *x, int S, int I, int8_t *xq, float *sx, float 
                      cudaStream_t st);
 int launch_s8_to_h(const int8_t *q, __half *h, long n, cudaStream_t st);
 int launch_moe_tc(int fmt, int epi, const GemmArgs &a, int n_groups, int *err, cudaStream_t st);
+int launch_moe_dec(int fmt, const GemmArgs &gu, const GemmArgs &dn, int max_items, float *hbuf, cudaStream_t st);
 
-// tcgen05 path unless ZZ_MOE_KERNEL=mma asks for the mma.sync one (for comparisons)
-static bool use_tc() {
+// Expert engine. Default ("auto"): the small-batch GEMV kernels (zz_moe_dec.cu) when
+// S*K <= DEC_MAX_PAIRS, else the mma.sync GEMM (k_gemm). ZZ_MOE_KERNEL=dec|mma|tc forces
+// one (tc = the tcgen05 kernel, k_moe_tc). All are exact per block.
+enum { ENG_DEC = 0, ENG_MMA = 1, ENG_TC = 2 };
+constexpr int DEC_MAX_PAIRS = 64;
+static int moe_engine(int P) {
     const char *e = getenv("ZZ_MOE_KERNEL");
-    return !(e && !strcmp(e, "mma"));
+    if (e && !strcmp(e, "tc")) return ENG_TC;
+    if (e && !strcmp(e, "mma")) return ENG_MMA;
+    if (e && !strcmp(e, "dec")) return ENG_DEC;
+    return P <= DEC_MAX_PAIRS ? ENG_DEC : ENG_MMA;
 }
-constexpr int TC_BN = 128;
+constexpr int TC_BN = 64;
 
 constexpr int MOE_BN = 64;
+constexpr int ROW_ALIGN = 16;
+constexpr int DEC_BN = 2;      // rows per work item of the small-batch kernels (DEC_C)  // pair rows of each expert start on a 16-row boundary
 constexpr int DENSE_BN = 64;
 
 static inline size_t a256(size_t n) { return (n + 255) & ~(size_t)255; }
@@ -90,7 +100,7 @@ __global__ void __launch_bounds__(1024) k_route(const int32_t *__restrict__ eidx
         int o = 0, io = 0;
         for (int e = 0; e < E; e++) {
             off[e] = o; ioff[e] = io;
-            o += cnt[e];
+            o += (cnt[e] + ROW_ALIGN - 1) / ROW_ALIGN * ROW_ALIGN;  // segments start 16-row aligned
             io += (cnt[e] + BN - 1) / BN;
         }
         *n_items = io;
@@ -115,11 +125,30 @@ __global__ void k_count_bad(const int32_t *eidx, int P, int E, int *bad) {
     if (p < P && (eidx[p] < 0 || eidx[p] >= E)) atomicAdd(bad, 1);
 }
 
+// pair rows incl. alignment padding; a multiple of ROW_ALIGN
+static inline size_t pair_cap(size_t P, int E) { return (P + (size_t)ROW_ALIGN * E + 15) / 16 * 16; }
+
+// routed rows in pair order: xg[r] = xh[token(r)] (fp16) and the block scales
+// transposed, xsT[b][r] = xs[token(r)][b], for the tensor-core path's bulk copies
+__global__ void k_gather_rows(const int *__restrict__ pair_src, int K, int cap, const __half *__restrict__ xh,
+                              const float *__restrict__ xs, int D, __half *__restrict__ xg, float *__restrict__ xsT,
+                              int ldT) {
+    const int r = blockIdx.x;
+    const int src = pair_src[r];
+    if (src < 0) return;
+    const int tok = src / K, nb = D / 32;
+    const uint4 *a = reinterpret_cast<const uint4 *>(xh + (size_t)tok * D);
+    uint4 *b = reinterpret_cast<uint4 *>(xg + (size_t)r * D);
+    for (int i = threadIdx.x; i < D / 8; i += blockDim.x) b[i] = a[i];
+    for (int i = threadIdx.x; i < nb; i += blockDim.x) xsT[(size_t)i * ldT + r] = xs[(size_t)tok * nb + i];
+}
+
 struct MoeWs {
     int8_t *xq; float *xs, *xsx; __half *xh;
     int *pair_src; float *pair_w;
+    __half *xg; float *xsT, *hsT; size_t cap, ldT;
     WorkItem *items; int *n_items;
-    int8_t *hq; float *hs; int *hblk; __half *hh;
+    int8_t *hq; float *hs; int *hblk; __half *hh; float *hf;
     int *bad;
     int *tcerr;
     size_t total;
@@ -128,21 +157,29 @@ struct MoeWs {
 static MoeWs moe_layout(const zz_expert_bank *b, int S, int K, uint8_t *base) {
     MoeWs w{};
     const int D = b->hidden, MI = b->inter, E = b->n_experts;
-    const size_t P = (size_t)S * K, maxit = P / MOE_BN + E + 1;
+    // items: at most P / (smallest item size) + one partial item per expert
+    const size_t P = (size_t)S * K, maxit = P / DEC_BN + E + 1;
+    const size_t cap = pair_cap(P, E), ldT = cap + 128;
+    w.cap = cap;
+    w.ldT = ldT;
     size_t o = 0;
     auto take = [&](size_t n) { size_t r = o; o += a256(n); return base ? base + r : nullptr; };
     w.xq = (int8_t *)take((size_t)S * D);
     w.xs = (float *)take((size_t)S * (D / 32) * 4);
     w.xsx = (float *)take((size_t)S * 4);
     w.xh = (__half *)take((size_t)S * D * 2);
-    w.pair_src = (int *)take(P * 4);
-    w.pair_w = (float *)take(P * 4);
+    w.pair_src = (int *)take(cap * 4);
+    w.pair_w = (float *)take(cap * 4);
+    w.xg = (__half *)take(cap * D * 2);
+    w.xsT = (float *)take((size_t)(D / 32) * ldT * 4);
+    w.hsT = (float *)take((size_t)(MI / 32) * ldT * 4);
     w.items = (WorkItem *)take(maxit * sizeof(WorkItem));
     w.n_items = (int *)take(4);
-    w.hq = (int8_t *)take(P * MI);
-    w.hs = (float *)take(P * (MI / 32) * 4);
-    w.hblk = (int *)take(P * (MI / 32) * 4);
-    w.hh = (__half *)take(P * MI * 2);
+    w.hq = (int8_t *)take(cap * MI);
+    w.hs = (float *)take(cap * (MI / 32) * 4);
+    w.hblk = (int *)take(cap * (MI / 32) * 4);
+    w.hh = (__half *)take(cap * MI * 2);
+    w.hf = (float *)take(cap * MI * 4);
     w.bad = (int *)take(4);
     w.tcerr = (int *)take(4);
     w.total = o;
@@ -244,6 +281,7 @@ extern "C" size_t zz_moe_workspace_offset(const zz_expert_bank *b, int S, int K,
     const void *p = which == 0 ? (const void *)w.pair_src : which == 1 ? (const void *)w.pair_w
                   : which == 2 ? (const void *)w.hq : which == 3 ? (const void *)w.hs
                   : which == 4 ? (const void *)w.n_items : which == 5 ? (const void *)w.tcerr : nullptr;
+    if (which == 6) return w.cap;
     if (!p) return (size_t)-1;
     return (size_t)((const uint8_t *)p - base);
 }
@@ -307,11 +345,41 @@ static int moe_impl(const zz_expert_bank *b, const float *X, const int8_t *xq_in
         if (fmt == GPU_FMT_TQ2) k_rows_sx<<<(S + 127) / 128, 128, 0, st>>>(xq, xs, S, D, w.xsx);
         if (!launch_s8_to_h(xq, w.xh, (long)S * D, st)) return 0;
     }
-    const bool tcp = use_tc();
-    k_route<<<1, 1024, 4 * E * sizeof(int), st>>>(eidx, ewt, P, E, tcp ? TC_BN : MOE_BN, w.pair_src, w.pair_w, w.items,
+    const int eng = moe_engine(P);
+    const bool tcp = eng == ENG_TC;
+    if (!check_cuda(cudaMemsetAsync(w.pair_src, 0xFF, w.cap * 4, st), "memset pair_src")) return 0;
+    if (!check_cuda(cudaMemsetAsync(w.tcerr, 0, 4, st), "memset tc error")) return 0;
+    k_route<<<1, 1024, 4 * E * sizeof(int), st>>>(eidx, ewt, P, E, tcp ? TC_BN : eng == ENG_DEC ? DEC_BN : MOE_BN,
+                                                  w.pair_src, w.pair_w, w.items,
                                                   w.n_items);
     if (!check_cuda(cudaGetLastError(), "route launch")) return 0;
+    if (tcp) {
+        k_gather_rows<<<(unsigned)w.cap, 128, 0, st>>>(w.pair_src, K, (int)w.cap, w.xh, xs, D, w.xg, w.xsT, (int)w.ldT);
+        if (!check_cuda(cudaGetLastError(), "gather launch")) return 0;
+    }
 
+    if (eng == ENG_DEC) {
+        GemmArgs gu{}, dn{};
+        gu.codes = b->gu_codes; gu.scale = b->gu_scale;
+        gu.codes_gstride = (long)codes_bytes(fmt, 2 * MI, D);
+        gu.scale_gstride = (long)scales_bytes(fmt, 2 * MI, D);
+        gu.O = 2 * MI; gu.I = D;
+        gu.xq = xq; gu.xs = xs; gu.xsx = w.xsx;
+        gu.items = w.items; gu.n_items = w.n_items; gu.pair_src = w.pair_src; gu.K = K;
+        gu.act = act; gu.clamp = clamp;
+        dn.codes = b->dn_codes; dn.scale = b->dn_scale;
+        dn.codes_gstride = (long)codes_bytes(fmt, D, MI);
+        dn.scale_gstride = (long)scales_bytes(fmt, D, MI);
+        dn.O = D; dn.I = MI;
+        dn.items = w.items; dn.n_items = w.n_items; dn.pair_src = w.pair_src; dn.pair_w = w.pair_w; dn.K = K;
+        dn.out = OUT; dn.hq = w.hq; dn.hs = w.hs;
+        prof_mark(st);
+        // items of <= DEC_BN rows: at most P items (plus one empty tail)
+        int ok = launch_moe_dec(fmt, gu, dn, P, w.hf, st);
+        prof_mark(st);
+        prof_mark(st);
+        return ok;
+    }
     GemmArgs g{};
     g.codes = b->gu_codes; g.scale = b->gu_scale;
     g.codes_gstride = (long)codes_bytes(fmt, 2 * MI, D);
@@ -321,9 +389,9 @@ static int moe_impl(const zz_expert_bank *b, const float *X, const int8_t *xq_in
     g.items = w.items; g.n_items = w.n_items;
     g.act = act; g.clamp = clamp;
     g.hq = w.hq; g.hs = w.hs; g.hblk = w.hblk; g.hh = w.hh;
+    g.xg = w.xg; g.xsT = w.xsT; g.ldT = (int)w.ldT; g.hsT = w.hsT; g.rows_cap = (int)w.cap;
     prof_mark(st);
     if (tcp) {
-        if (!check_cuda(cudaMemsetAsync(w.tcerr, 0, 4, st), "memset")) return 0;
         if (!launch_moe_tc(fmt, EPI_GATEUP, g, E, w.tcerr, st)) return 0;
     } else if (!launch_gemm<EPI_GATEUP, MOE_BN, true>(fmt, g, dim3((2 * MI) / G_BM, maxit), st)) {
         return 0;
@@ -338,6 +406,7 @@ static int moe_impl(const zz_expert_bank *b, const float *X, const int8_t *xq_in
     d.xq = w.hh; d.xs = w.hs; d.xsx = nullptr; d.xblk = fmt == GPU_FMT_TQ2 ? w.hblk : nullptr; d.gather = nullptr;
     d.items = w.items; d.n_items = w.n_items;
     d.out = OUT; d.pair_w = w.pair_w; d.pair_src = w.pair_src; d.K = K;
+    d.xg = w.hh; d.xsT = w.hsT; d.ldT = (int)w.ldT; d.rows_cap = (int)w.cap;
     int ok = tcp ? launch_moe_tc(fmt, EPI_DOWN, d, E, w.tcerr, st)
                  : launch_gemm<EPI_DOWN, MOE_BN, true>(fmt, d, dim3((D + G_BM - 1) / G_BM, maxit), st);
     prof_mark(st);

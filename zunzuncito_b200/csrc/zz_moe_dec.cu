@@ -1,0 +1,241 @@
+// zz_moe_dec.cu -- the batch-union expert FFN for small batches (decode): every
+// expert item carries at most DEC_C tokens, so the layer is a pair of weight-streaming
+// GEMVs rather than GEMMs (one token, 8 experts, 26.8 MB of weights).
+//
+//   k_dec_gateup  one warp per hidden feature f of an expert item: the gate row and the
+//                 up row of f (rows of the interleaved stack) are streamed once with
+//                 16-byte loads and dotted (dp4a) against the item's q8_0 token rows held
+//                 in registers; lane 0 applies the activation and writes h (fp32).
+//   k_dec_down    each CTA first requantizes the item's h rows to q8_0 in shared memory
+//                 (bit-exact with q40_quant_act, q40.h:124-138), then one warp per 4
+//                 output rows streams the down rows and adds w * y into OUT.
+// The per-block integer sums and the fp32 scale order per block are those of the
+// decode matvec (zz_gemv.cu), i.e. q40_dot's decomposition (q40.h:162-187).
+#include "zz_dot.cuh"
+#include "zz_gemm.cuh"
+
+namespace zz {
+
+constexpr int DEC_C = 2;    // max tokens per expert item on this path
+constexpr int DEC_NBL = 4;  // max 32-blocks per lane (K <= 4096)
+
+// one 32-weight block of a weight row, loaded once and dotted against several tokens
+struct WBlock {
+    uint4 w0, w1;
+    float scale;
+    int sh;
+};
+template <int FMT>
+__device__ __forceinline__ WBlock load_block(const uint8_t *row, int b, const __half *srow) {
+    WBlock k;
+    if (FMT == GPU_FMT_Q40) {
+        k.w0 = ldg_stream(row + (size_t)b * 16);
+        k.scale = __half2float(srow[b]);
+    } else if (FMT == GPU_FMT_Q80) {
+        k.w0 = ldg_stream(row + (size_t)b * 32);
+        k.w1 = ldg_stream(row + (size_t)b * 32 + 16);
+        k.scale = __half2float(srow[b]);
+    } else {
+        k.w0 = ldg_stream(row + (size_t)(b >> 1) * 16);
+        k.scale = 1.f;
+        k.sh = (b & 1) * 4;
+    }
+    return k;
+}
+template <int FMT>
+__device__ __forceinline__ int block_dot(const WBlock &k, const uint32_t x[8]) {
+    if (FMT == GPU_FMT_Q40) return q40_block_dot(k.w0, x);
+    if (FMT == GPU_FMT_Q80) return q80_block_dot(k.w0, k.w1, x);
+    return tq2_block_dot(k.w0, k.sh, x);
+}
+
+__device__ __forceinline__ void load_x8(const int8_t *p, uint32_t x[8]) {
+    const uint4 *q = reinterpret_cast<const uint4 *>(p);
+    uint4 lo = q[0], hi = q[1];
+    x[0] = lo.x; x[1] = lo.y; x[2] = lo.z; x[3] = lo.w;
+    x[4] = hi.x; x[5] = hi.y; x[6] = hi.z; x[7] = hi.w;
+}
+
+template <int FMT>
+__global__ void __launch_bounds__(256) k_dec_gateup(GemmArgs a, float *__restrict__ hbuf) {
+    const int item = blockIdx.y;
+    if (item >= *a.n_items) return;
+    const WorkItem it = a.items[item];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int MI = a.O / 2, D = a.I, nb = D / ZZ_BLK, nbp = (nb + 7) & ~7;
+    const int f = blockIdx.x * 8 + warp;
+    if (f >= MI) return;
+    const int nc = it.count;
+    // the item's token rows, this lane's blocks b = lane + 32 i, in registers
+    uint32_t xr[DEC_C][DEC_NBL][8];
+    float xsc[DEC_C][DEC_NBL], tot[DEC_C];
+#pragma unroll
+    for (int c = 0; c < DEC_C; c++) {
+        const int tok = c < nc ? a.pair_src[it.row0 + c] / a.K : 0;
+        tot[c] = FMT == GPU_FMT_TQ2 ? a.xsx[tok] : 0.f;
+#pragma unroll
+        for (int i = 0; i < DEC_NBL; i++) {
+            const int b = lane + 32 * i;
+            if (c < nc && b < nb) {
+                load_x8(reinterpret_cast<const int8_t *>(a.xq) + (size_t)tok * D + (size_t)b * 32, xr[c][i]);
+                xsc[c][i] = a.xs[(size_t)tok * nb + b];
+            } else {
+#pragma unroll
+                for (int k = 0; k < 8; k++) xr[c][i][k] = 0;
+                xsc[c][i] = 0.f;
+            }
+        }
+    }
+    const int grp = f / 64, fi = f % 64;
+    const int rg = grp * 128 + fi, ru = rg + 64;  // rows of the interleaved gate/up stack
+    const int CB = FMT == GPU_FMT_Q40 ? 16 : FMT == GPU_FMT_Q80 ? 32 : 8;
+    const uint8_t *codes = a.codes + (long)it.group * a.codes_gstride;
+    const uint8_t *grow = codes + (size_t)rg * nb * CB, *urow = codes + (size_t)ru * nb * CB;
+    const __half *sc = reinterpret_cast<const __half *>(reinterpret_cast<const uint8_t *>(a.scale) +
+                                                        (long)it.group * a.scale_gstride);
+    const __half *gs = FMT == GPU_FMT_TQ2 ? nullptr : sc + (size_t)rg * nbp;
+    const __half *us = FMT == GPU_FMT_TQ2 ? nullptr : sc + (size_t)ru * nbp;
+    float ag[DEC_C], au[DEC_C];
+#pragma unroll
+    for (int c = 0; c < DEC_C; c++) ag[c] = au[c] = 0.f;
+#pragma unroll
+    for (int i = 0; i < DEC_NBL; i++) {
+        const int b = lane + 32 * i;
+        if (b < nb) {
+            // both rows' codes are loaded before any dot, so the loads overlap
+            const WBlock kg = load_block<FMT>(grow, b, gs), ku = load_block<FMT>(urow, b, us);
+#pragma unroll
+            for (int c = 0; c < DEC_C; c++) {
+                ag[c] = fmaf(kg.scale * xsc[c][i], (float)block_dot<FMT>(kg, xr[c][i]), ag[c]);
+                au[c] = fmaf(ku.scale * xsc[c][i], (float)block_dot<FMT>(ku, xr[c][i]), au[c]);
+            }
+        }
+    }
+#pragma unroll
+    for (int c = 0; c < DEC_C; c++) {
+        float g = warp_sum(ag[c]), u = warp_sum(au[c]);
+        if (lane == 0 && c < nc) {
+            if (FMT == GPU_FMT_TQ2) {
+                const float *alpha = reinterpret_cast<const float *>(sc);
+                g = alpha[rg] * (g - tot[c]);
+                u = alpha[ru] * (u - tot[c]);
+            }
+            hbuf[(size_t)(it.row0 + c) * MI + f] = gated_act(a.act, g, u, a.clamp);
+        }
+    }
+}
+
+template <int FMT>
+__global__ void __launch_bounds__(256) k_dec_down(GemmArgs a, const float *__restrict__ hbuf) {
+    const int item = blockIdx.y;
+    if (item >= *a.n_items) return;
+    const WorkItem it = a.items[item];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int D = a.O, MI = a.I, nb = MI / ZZ_BLK, nbp = (nb + 7) & ~7;
+    const int nc = it.count;
+    __shared__ __align__(16) int8_t hq_s[DEC_C][DEC_NBL * 32 * 32];
+    __shared__ float hs_s[DEC_C][DEC_NBL * 32];
+    __shared__ int hb_s[DEC_C][DEC_NBL * 32];
+    __shared__ float tot_s[DEC_C];
+    // requantize the item's hidden rows (one warp per 32-block); CTA 0 also records
+    // hq / hs / hblk of the pair rows in the workspace, as the GEMM path does
+    for (int w = warp; w < DEC_C * nb; w += 8) {
+        const int c = w / nb, b = w % nb;
+        if (c >= nc) continue;
+        const size_t pr = (size_t)(it.row0 + c);
+        float d;
+        int8_t q = quant_lane(hbuf[pr * MI + b * 32 + lane], d);
+        hq_s[c][b * 32 + lane] = q;
+        int s = q;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+        if (lane == 0) { hs_s[c][b] = d; hb_s[c][b] = s; }
+        if (blockIdx.x == 0) {
+            a.hq[pr * MI + b * 32 + lane] = q;
+            if (lane == 0) a.hs[pr * nb + b] = d;
+        }
+    }
+    __syncthreads();
+    if (FMT == GPU_FMT_TQ2 && threadIdx.x < DEC_C) {
+        const int c = threadIdx.x;
+        double t = 0;
+        for (int b = 0; b < nb && c < nc; b++) t += (double)hs_s[c][b] * (double)hb_s[c][b];
+        tot_s[c] = (float)t;
+    }
+    __syncthreads();
+    uint32_t xr[DEC_C][DEC_NBL][8];
+    float xsc[DEC_C][DEC_NBL];
+#pragma unroll
+    for (int c = 0; c < DEC_C; c++)
+#pragma unroll
+        for (int i = 0; i < DEC_NBL; i++) {
+            const int b = lane + 32 * i;
+            if (c < nc && b < nb) {
+                load_x8(&hq_s[c][b * 32], xr[c][i]);
+                xsc[c][i] = hs_s[c][b];
+            } else {
+#pragma unroll
+                for (int k = 0; k < 8; k++) xr[c][i][k] = 0;
+                xsc[c][i] = 0.f;
+            }
+        }
+    float wt[DEC_C];
+    int tok[DEC_C];
+#pragma unroll
+    for (int c = 0; c < DEC_C; c++) {
+        wt[c] = c < nc ? a.pair_w[it.row0 + c] : 0.f;
+        tok[c] = c < nc ? a.pair_src[it.row0 + c] / a.K : 0;
+    }
+    const int CB = FMT == GPU_FMT_Q40 ? 16 : FMT == GPU_FMT_Q80 ? 32 : 8;
+    const uint8_t *codes = a.codes + (long)it.group * a.codes_gstride;
+    const __half *sc = reinterpret_cast<const __half *>(reinterpret_cast<const uint8_t *>(a.scale) +
+                                                        (long)it.group * a.scale_gstride);
+    const int o0 = blockIdx.x * 32 + warp * 4;
+#pragma unroll
+    for (int r = 0; r < 4; r++) {
+        const int o = o0 + r;
+        if (o >= D) break;
+        const uint8_t *row = codes + (size_t)o * nb * CB;
+        const __half *srow = FMT == GPU_FMT_TQ2 ? nullptr : sc + (size_t)o * nbp;
+        float acc[DEC_C];
+#pragma unroll
+        for (int c = 0; c < DEC_C; c++) acc[c] = 0.f;
+#pragma unroll
+        for (int i = 0; i < DEC_NBL; i++) {
+            const int b = lane + 32 * i;
+            if (b < nb) {
+                const WBlock k = load_block<FMT>(row, b, srow);
+#pragma unroll
+                for (int c = 0; c < DEC_C; c++) acc[c] = fmaf(k.scale * xsc[c][i], (float)block_dot<FMT>(k, xr[c][i]), acc[c]);
+            }
+        }
+#pragma unroll
+        for (int c = 0; c < DEC_C; c++) {
+            float y = warp_sum(acc[c]);
+            if (lane == 0 && c < nc) {
+                if (FMT == GPU_FMT_TQ2) y = reinterpret_cast<const float *>(sc)[o] * (y - tot_s[c]);
+                atomicAdd(a.out + (size_t)tok[c] * D + o, wt[c] * y);
+            }
+        }
+    }
+}
+
+// gate/up then down for items of <= DEC_C tokens; hbuf: [pair rows][inter] fp32
+int launch_moe_dec(int fmt, const GemmArgs &gu, const GemmArgs &dn, int max_items, float *hbuf, cudaStream_t st) {
+    const int MI = gu.O / 2, D = dn.O;
+    if (gu.I / 32 > DEC_NBL * 32 || dn.I / 32 > DEC_NBL * 32) return fail("dec: K too large for the decode path");
+    dim3 g1((MI + 7) / 8, max_items), g2((D + 31) / 32, max_items);
+    if (fmt == GPU_FMT_Q40) {
+        k_dec_gateup<GPU_FMT_Q40><<<g1, 256, 0, st>>>(gu, hbuf);
+        k_dec_down<GPU_FMT_Q40><<<g2, 256, 0, st>>>(dn, hbuf);
+    } else if (fmt == GPU_FMT_Q80) {
+        k_dec_gateup<GPU_FMT_Q80><<<g1, 256, 0, st>>>(gu, hbuf);
+        k_dec_down<GPU_FMT_Q80><<<g2, 256, 0, st>>>(dn, hbuf);
+    } else {
+        k_dec_gateup<GPU_FMT_TQ2><<<g1, 256, 0, st>>>(gu, hbuf);
+        k_dec_down<GPU_FMT_TQ2><<<g2, 256, 0, st>>>(dn, hbuf);
+    }
+    return check_cuda(cudaGetLastError(), "dec launch");
+}
+
+}  // namespace zz

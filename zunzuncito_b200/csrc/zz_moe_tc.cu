@@ -26,31 +26,27 @@
 namespace zz {
 
 namespace tcm {
-constexpr int NTHREADS = 448;
-constexpr int BN = 128;           // max activation rows per tile
-#ifndef ZZ_TC_NACC
-#define ZZ_TC_NACC 4
-#endif
-#ifndef ZZ_TC_LB
-#define ZZ_TC_LB 3
-#endif
-constexpr int NACC = ZZ_TC_NACC;  // TMEM accumulators (NACC * BN <= 512 columns)
-constexpr int RC = 6;             // weight-code ring slots
-constexpr int SLOT = 128 * 64;    // one TMA box: 128 rows x 64 bytes
-constexpr int NS = 6;             // A/B stages
-constexpr int LB = ZZ_TC_LB;      // activation blocks loaded ahead
-constexpr int A_BYTES = 128 * 64;  // 128 rows x 32 fp16
-constexpr int B_BYTES = BN * 64;
+constexpr int NTHREADS = 512;
+constexpr int BN = 64;            // max activation rows per tile
+constexpr int NACC = 8;           // TMEM accumulators (NACC * BN = 512 columns)
+constexpr int RC = 4;             // weight-code ring slots (4 blocks each for q4_0)
+constexpr int SLOT = 128 * 64;    // one code box: 128 rows x 64 bytes
+constexpr int NS = 4;             // widened-weight (A) stages
+constexpr int RB = 24;            // activation (B) ring slots
+constexpr int A_BYTES = 128 * 64;  // 128 rows x 32 fp16, K-major core matrices
+constexpr int B_BYTES = BN * 64;   // up to 64 rows x 32 fp16, 64-byte swizzle
 constexpr int DX_BYTES = BN * 4;
-constexpr int STAGE = A_BYTES + B_BYTES + DX_BYTES;
+constexpr int NDX = 16;           // activation-scale ring (freed by the epilogue)
 constexpr int CS = BN + 4;        // padded row of the fp32 result tile
-constexpr int OFF_RING = 0;
-constexpr int OFF_STAGE = OFF_RING + RC * SLOT;
-constexpr int OFF_CT = OFF_STAGE + NS * STAGE;
+constexpr int OFF_B = 0;          // 1024-aligned (swizzled TMA destination)
+constexpr int OFF_RING = OFF_B + RB * B_BYTES;
+constexpr int OFF_A = OFF_RING + RC * SLOT;
+constexpr int OFF_DX = OFF_A + NS * A_BYTES;
+constexpr int OFF_CT = OFF_DX + NDX * DX_BYTES;
 constexpr int OFF_INFO = OFF_CT + 128 * CS * 4;
 constexpr int OFF_BAR = OFF_INFO + BN * 12;
-constexpr int NBAR = 2 * RC + 2 * NS + 2 * NACC;
-constexpr int SMEM = OFF_BAR + NBAR * 8 + 16;
+constexpr int NBAR = 2 * RC + 2 * NS + 2 * RB + 2 * NACC + 2 * NDX;
+constexpr int SMEM = OFF_BAR + NBAR * 8 + 16 + 1024;  // + slack to align the base to 1 KB
 }  // namespace tcm
 
 // offset of block j's codes inside one weight row, and the bytes it spans
@@ -93,6 +89,10 @@ __device__ __forceinline__ void widen_row(const uint8_t *src, int j, uint4 out[4
     }
 }
 
+struct BMaps {
+    CUtensorMap m[3];  // activation boxes of 16, 32 and 64 rows
+};
+
 struct TcTile {
     WorkItem it;
     int m0;
@@ -106,17 +106,22 @@ __device__ __forceinline__ TcTile tc_tile(const GemmArgs &a, int t, int MT) {
 
 template <int FMT, int EPI>
 __global__ void __launch_bounds__(tcm::NTHREADS, 1)
-    k_moe_tc(const GemmArgs a, const __grid_constant__ CUtensorMap codes_map, int *err) {
+    k_moe_tc(const GemmArgs a, const __grid_constant__ CUtensorMap codes_map, const __grid_constant__ BMaps bmaps,
+             int *err) {
     using namespace tcm;
-    extern __shared__ __align__(128) uint8_t smem[];
+    extern __shared__ __align__(128) uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
     uint8_t *ring = smem + OFF_RING;
-    uint8_t *stages = smem + OFF_STAGE;
+    uint8_t *stages = smem + OFF_A;
+    uint8_t *bring = smem + OFF_B;
     float *ct = reinterpret_cast<float *>(smem + OFF_CT);
     int *col_xrow = reinterpret_cast<int *>(smem + OFF_INFO);
     float *col_sx = reinterpret_cast<float *>(smem + OFF_INFO + BN * 4);
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem + OFF_BAR);
     uint64_t *cfull = bars, *cempty = bars + RC, *sfull = bars + 2 * RC, *sempty = bars + 2 * RC + NS;
     uint64_t *tfull = bars + 2 * RC + 2 * NS, *tempty = bars + 2 * RC + 2 * NS + NACC;
+    uint64_t *dfull = tempty + NACC, *dempty = dfull + NDX, *bfull = dempty + NDX, *bempty = bfull + RB;
+    uint8_t *dxring = smem + OFF_DX;
     uint32_t *tmem_base_smem = reinterpret_cast<uint32_t *>(smem + OFF_BAR + NBAR * 8);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + OFF_BAR + NBAR * 8 + 4);
 
@@ -129,7 +134,9 @@ __global__ void __launch_bounds__(tcm::NTHREADS, 1)
 
     if (tid == 0) {
         for (int i = 0; i < RC; i++) { tc::mbar_init(&cfull[i], 1); tc::mbar_init(&cempty[i], 128); }
-        for (int i = 0; i < NS; i++) { tc::mbar_init(&sfull[i], 128); tc::mbar_init(&sempty[i], 8); }
+        for (int i = 0; i < NS; i++) { tc::mbar_init(&sfull[i], 128); tc::mbar_init(&sempty[i], 1); }
+        for (int i = 0; i < NDX; i++) { tc::mbar_init(&dfull[i], 1); tc::mbar_init(&dempty[i], 8); }
+        for (int i = 0; i < RB; i++) { tc::mbar_init(&bfull[i], 1); tc::mbar_init(&bempty[i], 1); }
         for (int i = 0; i < NACC; i++) { tc::mbar_init(&tfull[i], 1); tc::mbar_init(&tempty[i], 8); }
         *abort_flag = 0;
         tc::mbar_init_fence();
@@ -139,10 +146,44 @@ __global__ void __launch_bounds__(tcm::NTHREADS, 1)
     __syncthreads();
     tc::tc_fence_after();
     const uint32_t tbase = *tmem_base_smem;
+#ifdef ZZ_TC_PROF
+    if (blockIdx.x == 0 && tid == 0) atomicAdd(&tc::g_tc_prof[30], (unsigned long long)clock64());
+#endif
+
+    // activation-tile issue loop (one thread); the tensor map is named with a constant
+    // index so it stays in parameter space
+    auto issue_b_tiles = [&]() {
+        uint32_t g = 0, last = 0;
+        bool any = false;
+        for (int t = blockIdx.x; t < T && !*abort_flag; t += gridDim.x) {
+            TcTile tl = tc_tile(a, t, MT);
+            const int N = (tl.it.count + 15) & ~15;
+            const int sel = N <= 16 ? 0 : N <= 32 ? 1 : 2;
+            const uint32_t bbytes = (16u << sel) * 64u;
+            bool ok = true;
+            for (int j = 0; j < nb && ok; j++, g++) {
+                const int bs = g % RB;
+                const uint32_t u = g / RB;
+                if (u && !tc::mbar_wait(&bempty[bs], (u - 1) & 1, abort_flag, err, 3)) { ok = false; break; }
+                tc::mbar_arrive_tx(&bfull[bs], bbytes);
+                uint8_t *dst = bring + bs * B_BYTES;
+                // rows row0.. of the pair-ordered activations, halves 32j..32j+31: one
+                // 64-byte-swizzled K-major tile
+                switch (sel) {
+                    case 0: tc::tma_load_2d(dst, &bmaps.m[0], j * 32, tl.it.row0, &bfull[bs]); break;
+                    case 1: tc::tma_load_2d(dst, &bmaps.m[1], j * 32, tl.it.row0, &bfull[bs]); break;
+                    default: tc::tma_load_2d(dst, &bmaps.m[2], j * 32, tl.it.row0, &bfull[bs]); break;
+                }
+                last = g;
+                any = true;
+            }
+        }
+        if (any) tc::mbar_wait(&bfull[last % RB], (last / RB) & 1, abort_flag, err, 12);
+    };
 
     if (warp == 12) {
-        // ---------------- TMA: weight codes -> ring ----------------
         if (lane == 0) {
+            // ---------------- TMA: weight codes -> ring (deep, from HBM) ----------------
             uint32_t c = 0;
             for (int t = blockIdx.x; t < T && !*abort_flag; t += gridDim.x) {
                 TcTile tl = tc_tile(a, t, MT);
@@ -157,48 +198,38 @@ __global__ void __launch_bounds__(tcm::NTHREADS, 1)
             }
             // bounded drain: do not leave the CTA with copies in flight
             if (c) tc::mbar_wait(&cfull[(c - 1) % RC], ((c - 1) / RC) & 1, abort_flag, err, 2);
+        } else if (lane == 1) {
+        }
+    } else if (warp == 14) {
+        // ---------------- TMA: activation tiles ----------------
+        if (lane == 0) issue_b_tiles();
+    } else if (warp == 15) {
+        if (lane == 0) {
+            // ---------------- bulk copies: the tiles' activation block scales ----------------
+            uint32_t g = 0;
+            for (int t = blockIdx.x; t < T && !*abort_flag; t += gridDim.x) {
+                TcTile tl = tc_tile(a, t, MT);
+                bool ok = true;
+                for (int j = 0; j < nb && ok; j++, g++) {
+                    const int ds = g % NDX;
+                    const uint32_t du = g / NDX;
+                    if (du && !tc::mbar_wait(&dempty[ds], (du - 1) & 1, abort_flag, err, 11)) { ok = false; break; }
+                    tc::mbar_arrive_tx(&dfull[ds], DX_BYTES);
+                    tc::bulk_load(dxring + ds * DX_BYTES, a.xsT + (size_t)j * a.ldT + tl.it.row0, DX_BYTES, &dfull[ds]);
+                }
+            }
+            if (g) tc::mbar_wait(&dfull[(g - 1) % NDX], ((g - 1) / NDX) & 1, abort_flag, err, 13);
         }
     } else if (warp >= 8 && warp < 12) {
-        // ---------------- producers ----------------
-        const int pt = tid - 256;  // weight row of the tile / activation piece index
-        uint32_t pb = 0, slot_base = 0;
-        const __half *xh = reinterpret_cast<const __half *>(a.xq);
+        // ---------------- producers: widen weight codes to fp16 ----------------
+        const int pt = tid - 256;  // weight row of the tile
+        uint32_t g = 0, slot_base = 0;
         for (int t = blockIdx.x; t < T && !*abort_flag; t += gridDim.x) {
-            TcTile tl = tc_tile(a, t, MT);
-            const int ncols = tl.it.count;
-            // this thread's activation pieces: rows n = pt/4 + 32 i, K-chunk pt%4
-            int xr[4];
-#pragma unroll
-            for (int i = 0; i < 4; i++) {
-                int n = (pt >> 2) + 32 * i;
-                xr[i] = n < ncols ? (a.gather ? a.gather[tl.it.row0 + n] / a.gather_div : tl.it.row0 + n) : -1;
-            }
-            const int xdx = pt < ncols ? (a.gather ? a.gather[tl.it.row0 + pt] / a.gather_div : tl.it.row0 + pt) : -1;
-            const int kc = pt & 3;
-            auto issue_b = [&](int jj) -> bool {
-                const uint32_t g = pb + jj;
+            bool ok = true;
+            for (int j = 0; j < nb && ok; j++, g++) {
                 const int st = g % NS;
                 const uint32_t u = g / NS;
-                if (u && !tc::mbar_wait(&sempty[st], (u - 1) & 1, abort_flag, err, 3)) return false;
-                uint8_t *sb = stages + st * STAGE + A_BYTES;
-#pragma unroll
-                for (int i = 0; i < 4; i++) {
-                    int n = (pt >> 2) + 32 * i;
-                    bool ok = xr[i] >= 0;
-                    const __half *src = xh + (size_t)(ok ? xr[i] : 0) * a.I + jj * 32 + kc * 8;
-                    cp_async16_zfill(sb + (n >> 3) * 512 + kc * 128 + (n & 7) * 16, src, ok);
-                }
-                const float *sxp = a.xs + (size_t)(xdx >= 0 ? xdx : 0) * nb + jj;
-                cp_async4_zfill(stages + st * STAGE + A_BYTES + B_BYTES + pt * 4, sxp, xdx >= 0);
-                cp_async_commit();
-                return true;
-            };
-            bool ok = true;
-            for (int jj = 0; jj < LB && jj < nb && ok; jj++) ok = issue_b(jj);
-            for (int j = 0; j < nb && ok; j++) {
-                if (j + LB < nb) ok = issue_b(j + LB);
-                if (!ok) break;
-                // codes of block j for this row
+                if (u && !tc::mbar_wait(&sempty[st], (u - 1) & 1, abort_flag, err, 14)) { ok = false; break; }
                 const int bb = blk_byte<FMT>(j);
                 const uint32_t sc = slot_base + bb / 64;
                 const int s = sc % RC;
@@ -206,8 +237,7 @@ __global__ void __launch_bounds__(tcm::NTHREADS, 1)
                 const bool last = ((bb + blk_span<FMT>()) % 64 == 0 && (FMT != GPU_FMT_TQ2 || (j & 1) == 1)) || j == nb - 1;
                 if (first && !tc::mbar_wait(&cfull[s], (sc / RC) & 1, abort_flag, err, 4)) { ok = false; break; }
                 uint4 w[4];
-                const int prow = pt;
-                widen_row<FMT>(ring + s * SLOT + prow * 64 + bb % 64, j, w);
+                widen_row<FMT>(ring + s * SLOT + pt * 64 + bb % 64, j, w);
                 if (last) {
                     // Release the slot to the TMA only once this thread's shared loads of it
                     // have returned (consume their values) and are ordered before the async
@@ -217,17 +247,12 @@ __global__ void __launch_bounds__(tcm::NTHREADS, 1)
                     tc::fence_proxy_async();
                     tc::mbar_arrive(&cempty[s]);
                 }
-                const uint32_t g = pb + j;
-                uint8_t *sa = stages + (g % NS) * STAGE + (prow >> 3) * 512 + (prow & 7) * 16;
+                uint8_t *sa = stages + st * A_BYTES + (pt >> 3) * 512 + (pt & 7) * 16;
 #pragma unroll
                 for (int k = 0; k < 4; k++) *reinterpret_cast<uint4 *>(sa + k * 128) = w[k];
-                if (j + LB < nb) cp_async_wait<LB>();
-                else cp_async_wait<0>();
                 tc::fence_proxy_async();
-                tc::mbar_arrive(&sfull[g % NS]);
+                tc::mbar_arrive(&sfull[st]);
             }
-            cp_async_wait<0>();
-            pb += nb;
             slot_base += nslots;
         }
     } else if (warp == 13) {
@@ -240,17 +265,20 @@ __global__ void __launch_bounds__(tcm::NTHREADS, 1)
                 const int N = (tl.it.count + 15) & ~15;
                 const uint32_t idesc = tc::idesc_f16(128, N);
                 for (int j = 0; j < nb; j++, g++) {
-                    const int s = g % NS, ac = g % NACC;
+                    const int s = g % NS, bs = g % RB, ac = g % NACC;
                     if (!tc::mbar_wait(&sfull[s], (g / NS) & 1, abort_flag, err, 5)) { ok = false; break; }
+                    if (!tc::mbar_wait(&bfull[bs], (g / RB) & 1, abort_flag, err, 15)) { ok = false; break; }
                     if (g >= NACC && !tc::mbar_wait(&tempty[ac], ((g / NACC) - 1) & 1, abort_flag, err, 6)) { ok = false; break; }
                     tc::tc_fence_after();
-                    const uint32_t sa = tc::smem_u32(stages + s * STAGE), sb = sa + A_BYTES;
-                    const uint64_t ad = tc::smem_desc(sa, 128, 512), bd = tc::smem_desc(sb, 128, 512);
+                    const uint32_t sa = tc::smem_u32(stages + s * A_BYTES), sb = tc::smem_u32(bring + bs * B_BYTES);
+                    // A: core matrix (row group r, K chunk kc) at r*512 + kc*128, no swizzle
+                    // B: 8-row x 64-byte swizzle atoms, 512 bytes apart
+                    const uint64_t ad = tc::smem_desc(sa, 128, 512), bd = tc::smem_desc_sw64(sb, 512);
                     const uint32_t td = tbase + ac * BN;
-                    tc::mma_f16_ss(td, ad, bd, idesc, 0u);               // k 0-15 (overwrite)
-                    tc::mma_f16_ss(td, ad + 16, bd + 16, idesc, 1u);     // k 16-31 (+256 bytes)
-                    // one commit per block: the epilogue frees the stage after it has seen
-                    // this commit, so the stage is released only once the MMAs are done
+                    tc::mma_f16_ss(td, ad, bd, idesc, 0u);                             // k 0-15 (overwrite)
+                    tc::mma_f16_ss(td, ad + (256 >> 4), bd + (32 >> 4), idesc, 1u);  // k 16-31
+                    tc::mma_commit(&sempty[s]);   // A stage free once these MMAs complete
+                    tc::mma_commit(&bempty[bs]);  // B slot likewise
                     tc::mma_commit(&tfull[ac]);
                 }
             }
@@ -264,7 +292,7 @@ __global__ void __launch_bounds__(tcm::NTHREADS, 1)
         for (int t = blockIdx.x; t < T; t += gridDim.x) {
             TcTile tl = tc_tile(a, t, MT);
             const int ncols = tl.it.count;
-            const bool c0 = h * 64 < ncols, c1 = h * 64 + 32 < ncols;
+            const bool cv = h * 32 < ncols;  // this warp's 32 columns hold tokens
             // per-column info for the output phase
             for (int n = tid; n < BN; n += 256) {
                 int r = tl.it.row0 + (n < ncols ? n : 0);
@@ -288,99 +316,124 @@ __global__ void __launch_bounds__(tcm::NTHREADS, 1)
                 dwrow = reinterpret_cast<const __half *>(reinterpret_cast<const uint8_t *>(a.scale) +
                                                          (long)tl.it.group * a.scale_gstride) +
                         (size_t)(tl.m0 + m) * nbp;
-            float2 acc[32];
+            float2 acc[16];
 #pragma unroll
-            for (int i = 0; i < 32; i++) acc[i] = make_float2(0.f, 0.f);
-            float dw_next = (FMT != GPU_FMT_TQ2) ? __half2float(dwrow[0]) : 1.f;
-            for (int j = 0; j < nb; j++, g++) {
-                const int s = g % NS, ac = g % NACC;
-                const float dw = dw_next;
-                if (FMT != GPU_FMT_TQ2 && j + 1 < nb) dw_next = __half2float(dwrow[j + 1]);
-                bool ok = tc::mbar_wait(&tfull[ac], (g / NACC) & 1, abort_flag, err, 8);
-                ok = ok && tc::mbar_wait(&sfull[s], (g / NS) & 1, abort_flag, err, 9);
+            for (int i = 0; i < 16; i++) acc[i] = make_float2(0.f, 0.f);
+            const uint32_t tl_lane = (uint32_t)(q * 32) << 16;
+            // Software pipeline over the K blocks: the TMEM load of block j+1 is in flight
+            // while block j is scaled into the accumulators (two register buffers).
+            uint32_t va_[32], vb_[32];
+            auto fetch = [&](uint32_t gg, uint32_t (&v)[32]) -> bool {
+                bool ok = tc::mbar_wait(&tfull[gg % NACC], (gg / NACC) & 1, abort_flag, err, 8);
+                ok = ok && tc::mbar_wait(&dfull[gg % NDX], (gg / NDX) & 1, abort_flag, err, 9);
                 ok = __all_sync(0xffffffffu, ok);  // tcgen05.ld is warp-collective
                 tc::tc_fence_after();
-                const float *dx = reinterpret_cast<const float *>(stages + s * STAGE + A_BYTES + B_BYTES) + h * 64;
-                const float2 dw2 = make_float2(dw, dw);
-#pragma unroll
-                for (int hc = 0; hc < 2; hc++) {
-                    if (!(ok && (hc == 0 ? c0 : c1))) continue;
-                    uint32_t v[32];
-                    tc::tmem_ld32(tbase + ((uint32_t)(q * 32) << 16) + ac * BN + h * 64 + hc * 32, v);
-                    tc::tmem_ld_wait();
-#pragma unroll
-                    for (int i = 0; i < 8; i++) {
-                        float4 d4 = *reinterpret_cast<const float4 *>(dx + hc * 32 + 4 * i);
-                        float2 va = make_float2(__uint_as_float(v[4 * i]), __uint_as_float(v[4 * i + 1]));
-                        float2 vb = make_float2(__uint_as_float(v[4 * i + 2]), __uint_as_float(v[4 * i + 3]));
-                        float2 da = make_float2(d4.x, d4.y), db = make_float2(d4.z, d4.w);
-                        if (FMT != GPU_FMT_TQ2) { da = fmul2(dw2, da); db = fmul2(dw2, db); }
-                        acc[hc * 16 + 2 * i] = ffma2(da, va, acc[hc * 16 + 2 * i]);
-                        acc[hc * 16 + 2 * i + 1] = ffma2(db, vb, acc[hc * 16 + 2 * i + 1]);
-                    }
-                }
+                if (ok && cv) tc::tmem_ld32(tbase + tl_lane + (gg % NACC) * BN + h * 32, v);
+                return ok;
+            };
+            float dw_next = (FMT != GPU_FMT_TQ2) ? __half2float(dwrow[0]) : 1.f;
+            bool okc = fetch(g, va_);
+            // one K block: results of block j are in `cur`; block j+1 is fetched into `nxt`
+            auto step = [&](int j, uint32_t (&cur)[32], uint32_t (&nxt)[32]) {
+                const int ac = g % NACC, ds = g % NDX;
+                const float dw = dw_next;
+                if (FMT != GPU_FMT_TQ2 && j + 1 < nb) dw_next = __half2float(dwrow[j + 1]);
+                if (okc && cv) tc::tmem_ld_wait();
                 tc::tc_fence_before();
                 __syncwarp();
-                if (lane == 0) tc::mbar_arrive(&tempty[ac]);
+                if (lane == 0) tc::mbar_arrive(&tempty[ac]);  // accumulator j is in registers
+                bool okn = true;
+                if (j + 1 < nb) okn = fetch(g + 1, nxt);
+                if (okc && cv) {
+                    const float *dx = reinterpret_cast<const float *>(dxring + ds * DX_BYTES) + h * 32;
+                    const float2 dw2 = make_float2(dw, dw);
+#pragma unroll
+                    for (int i = 0; i < 8; i++) {
+                        float4 d4 = *reinterpret_cast<const float4 *>(dx + 4 * i);
+                        float2 x0 = make_float2(__uint_as_float(cur[4 * i]), __uint_as_float(cur[4 * i + 1]));
+                        float2 x1 = make_float2(__uint_as_float(cur[4 * i + 2]), __uint_as_float(cur[4 * i + 3]));
+                        float2 da = make_float2(d4.x, d4.y), db = make_float2(d4.z, d4.w);
+                        if (FMT != GPU_FMT_TQ2) { da = fmul2(dw2, da); db = fmul2(dw2, db); }
+                        acc[2 * i] = ffma2(da, x0, acc[2 * i]);
+                        acc[2 * i + 1] = ffma2(db, x1, acc[2 * i + 1]);
+                    }
+                }
                 __syncwarp();
-                if (lane == 0) tc::mbar_arrive(&sempty[s]);
+                if (lane == 0) tc::mbar_arrive(&dempty[ds]);
+                okc = okn;
+                g++;
+            };
+#pragma unroll 1
+            for (int j = 0; j < nb; j += 2) {
+                step(j, va_, vb_);
+                if (j + 1 < nb) step(j + 1, vb_, va_);
             }
             // ---- tile output: 128 x ncols fp32 through shared memory ----
-#pragma unroll
-            for (int i = 0; i < 32; i++) *reinterpret_cast<float2 *>(ct + m * CS + h * 64 + 2 * i) = acc[i];
-            tc::named_sync(1, 256);
             const float *alpha = FMT == GPU_FMT_TQ2 ? reinterpret_cast<const float *>(
                                                           reinterpret_cast<const uint8_t *>(a.scale) +
                                                           (long)tl.it.group * a.scale_gstride)
                                                     : nullptr;
             const int m0 = tl.m0;
-            if (!*abort_flag) {
-                if (EPI == EPI_GATEUP) {
-                    const int f0 = (m0 / 128) * 64;
-                    const int MI = a.O / 2, nbh = MI / 32;
-                    for (int wi = warp; wi < ncols * 2; wi += 8) {
-                        int n = wi >> 1, hb = wi & 1;
-                        int f = hb * 32 + lane;
-                        float gv = ct[f * CS + n], uv = ct[(64 + f) * CS + n];
-                        if (FMT == GPU_FMT_TQ2) {
-                            float tot = col_sx[n];
-                            gv = alpha[m0 + f] * (gv - tot);
-                            uv = alpha[m0 + 64 + f] * (uv - tot);
-                        }
-                        float hv = gated_act(a.act, gv, uv, a.clamp), d;
-                        int8_t qv = quant_lane(hv, d);
-                        const size_t pr = (size_t)(tl.it.row0 + n);
-                        a.hq[pr * MI + f0 + f] = qv;
-                        a.hh[pr * MI + f0 + f] = __int2half_rn(qv);
-                        if (lane == 0) a.hs[pr * nbh + f0 / 32 + hb] = d;
-                        if (FMT == GPU_FMT_TQ2) {
-                            int sm = qv;
+            {
+                const int c0n = 0, nc = ncols;
 #pragma unroll
-                            for (int o = 16; o > 0; o >>= 1) sm += __shfl_xor_sync(0xffffffffu, sm, o);
-                            if (lane == 0) a.hblk[pr * nbh + f0 / 32 + hb] = sm;
+                for (int i = 0; i < 16; i++) *reinterpret_cast<float2 *>(ct + m * CS + h * 32 + 2 * i) = acc[i];
+                tc::named_sync(1, 256);
+                if (!*abort_flag) {
+                    if (EPI == EPI_GATEUP) {
+                        const int f0 = (m0 / 128) * 64;
+                        const int MI = a.O / 2, nbh = MI / 32;
+                        for (int wi = warp; wi < nc * 2; wi += 8) {
+                            int nl = wi >> 1, hb = wi & 1, n = c0n + nl;
+                            int f = hb * 32 + lane;
+                            float gv = ct[f * CS + nl], uv = ct[(64 + f) * CS + nl];
+                            if (FMT == GPU_FMT_TQ2) {
+                                float tot = col_sx[n];
+                                gv = alpha[m0 + f] * (gv - tot);
+                                uv = alpha[m0 + 64 + f] * (uv - tot);
+                            }
+                            float hv = gated_act(a.act, gv, uv, a.clamp), d;
+                            int8_t qv = quant_lane(hv, d);
+                            const size_t pr = (size_t)(tl.it.row0 + n);
+                            a.hq[pr * MI + f0 + f] = qv;
+                            a.hh[pr * MI + f0 + f] = __int2half_rn(qv);
+                            if (lane == 0) {
+                                a.hs[pr * nbh + f0 / 32 + hb] = d;
+                                a.hsT[(size_t)(f0 / 32 + hb) * a.ldT + pr] = d;
+                            }
+                            if (FMT == GPU_FMT_TQ2) {
+                                int sm = qv;
+#pragma unroll
+                                for (int o = 16; o > 0; o >>= 1) sm += __shfl_xor_sync(0xffffffffu, sm, o);
+                                if (lane == 0) a.hblk[pr * nbh + f0 / 32 + hb] = sm;
+                            }
                         }
-                    }
-                } else {  // EPI_DOWN
-                    for (int n = warp; n < ncols; n += 8) {
-                        const int pr = tl.it.row0 + n;
-                        const float w = a.pair_w[pr];
-                        const int tok = a.pair_src[pr] / a.K;
-                        const float tot = col_sx[n];
-                        const int r = lane * 4, o = m0 + r;
-                        float4 v;
-                        v.x = ct[r * CS + n]; v.y = ct[(r + 1) * CS + n]; v.z = ct[(r + 2) * CS + n]; v.w = ct[(r + 3) * CS + n];
-                        if (FMT == GPU_FMT_TQ2) {
-                            v.x = alpha[o] * (v.x - tot); v.y = alpha[o + 1] * (v.y - tot);
-                            v.z = alpha[o + 2] * (v.z - tot); v.w = alpha[o + 3] * (v.w - tot);
+                    } else {  // EPI_DOWN
+                        for (int nl = warp; nl < nc; nl += 8) {
+                            const int n = c0n + nl;
+                            const int pr = tl.it.row0 + n;
+                            const float w = a.pair_w[pr];
+                            const int tok = a.pair_src[pr] / a.K;
+                            const float tot = col_sx[n];
+                            const int r = lane * 4, o = m0 + r;
+                            float4 v;
+                            v.x = ct[r * CS + nl]; v.y = ct[(r + 1) * CS + nl]; v.z = ct[(r + 2) * CS + nl]; v.w = ct[(r + 3) * CS + nl];
+                            if (FMT == GPU_FMT_TQ2) {
+                                v.x = alpha[o] * (v.x - tot); v.y = alpha[o + 1] * (v.y - tot);
+                                v.z = alpha[o + 2] * (v.z - tot); v.w = alpha[o + 3] * (v.w - tot);
+                            }
+                            v.x *= w; v.y *= w; v.z *= w; v.w *= w;
+                            atomicAdd(reinterpret_cast<float4 *>(a.out + (size_t)tok * a.O + o), v);
                         }
-                        v.x *= w; v.y *= w; v.z *= w; v.w *= w;
-                        atomicAdd(reinterpret_cast<float4 *>(a.out + (size_t)tok * a.O + o), v);
                     }
                 }
+                tc::named_sync(1, 256);
             }
-            tc::named_sync(1, 256);
         }
     }
+#ifdef ZZ_TC_PROF
+    if (blockIdx.x == 0 && (tid & 31) == 0) atomicAdd(&tc::g_tc_prof[20 + (warp < 8 ? 0 : warp < 12 ? 1 : warp - 10)], (unsigned long long)clock64());
+#endif
     tc::tc_fence_before();
     __syncthreads();
     if (warp == 13) {
@@ -418,6 +471,22 @@ static int make_codes_map(CUtensorMap *map, const uint8_t *codes, long rows, int
     return 1;
 }
 
+// pair-ordered fp16 activation rows [rows, I] seen as (8 halves) x rows x (I/8 chunks),
+// so one box {8, 128, 4} lands a block's 128 x 32 tile as K-major core matrices
+static int make_b_map(CUtensorMap *map, const __half *xg, int rows, int I, int box_rows) {
+    if (!get_encode()) return 0;
+    if ((uintptr_t)xg & 15 || I % 32) return fail("tc: activation rows not 16-byte aligned");
+    cuuint64_t dims[2] = {(cuuint64_t)I, (cuuint64_t)rows};
+    cuuint64_t strides[1] = {(cuuint64_t)I * 2};
+    cuuint32_t box[2] = {32, (cuuint32_t)box_rows};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<__half *>(xg), dims, strides, box, estr,
+                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail("tc: activation tensor map failed (%d)", (int)r);
+    return 1;
+}
+
 template <int FMT, int EPI>
 static int launch_tc_t(const GemmArgs &a, int n_groups, int *err, cudaStream_t st) {
     static bool attr = false;
@@ -429,12 +498,15 @@ static int launch_tc_t(const GemmArgs &a, int n_groups, int *err, cudaStream_t s
     }
     const int row_bytes = FMT == GPU_FMT_Q40 ? a.I / 2 : FMT == GPU_FMT_Q80 ? a.I : a.I / 4;
     CUtensorMap map;
+    BMaps bmaps;
     if (!make_codes_map(&map, a.codes, (long)n_groups * a.O, row_bytes)) return 0;
+    for (int i = 0; i < 3; i++)
+        if (!make_b_map(&bmaps.m[i], a.xg, a.rows_cap, a.I, 16 << i)) return 0;
     int dev = 0, sms = 148;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     if (const char *e = getenv("ZZ_TC_GRID")) sms = atoi(e) > 0 ? atoi(e) : sms;
-    k_moe_tc<FMT, EPI><<<sms, tcm::NTHREADS, tcm::SMEM, st>>>(a, map, err);
+    k_moe_tc<FMT, EPI><<<sms, tcm::NTHREADS, tcm::SMEM, st>>>(a, map, bmaps, err);
     return check_cuda(cudaGetLastError(), "tc launch");
 }
 
@@ -453,3 +525,13 @@ int launch_moe_tc(int fmt, int epi, const GemmArgs &a, int n_groups, int *err, c
 }
 
 }  // namespace zz
+
+#ifdef ZZ_TC_PROF
+extern "C" int zz_tc_prof_read(unsigned long long *out) {
+    cudaDeviceSynchronize();
+    cudaMemcpyFromSymbol(out, zz::tc::g_tc_prof, sizeof(unsigned long long) * 32);
+    unsigned long long z[32] = {0};
+    cudaMemcpyToSymbol(zz::tc::g_tc_prof, z, sizeof z);
+    return 1;
+}
+#endif

@@ -37,8 +37,20 @@ __device__ __forceinline__ bool mbar_try(uint64_t *bar, uint32_t parity) {
         : "memory");
     return ok != 0;
 }
+#ifdef ZZ_TC_PROF
+__device__ unsigned long long g_tc_prof[32];
+#endif
 // bounded wait for the phase with the given parity to complete
 __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, volatile int *abort, int *err, int code) {
+#ifdef ZZ_TC_PROF
+    long long t0 = clock64();
+    struct Acc {
+        long long t0; int code;
+        __device__ ~Acc() {
+            if (blockIdx.x == 0 && (threadIdx.x & 31) == 0) atomicAdd(&g_tc_prof[code], (unsigned long long)(clock64() - t0));
+        }
+    } acc_{t0, code};
+#endif
     for (uint32_t i = 0; i < WAIT_LIMIT; i++) {
         if (mbar_try(bar, parity)) return true;
         if ((i & 255u) == 255u && *abort) return false;
@@ -61,6 +73,22 @@ __device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, i
         : "memory");
 }
 
+// 3-D TMA tile load (no multicast)
+__device__ __forceinline__ void tma_load_3d(void *dst, const CUtensorMap *map, int x, int y, int z, uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(
+            smem_u32(dst)),
+        "l"(map), "r"(x), "r"(y), "r"(z), "r"(smem_u32(bar))
+        : "memory");
+}
+// contiguous bulk copy global -> shared (16-byte aligned, size a multiple of 16)
+__device__ __forceinline__ void bulk_load(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                     smem_u32(dst)),
+                 "l"(src), "r"(bytes), "r"(smem_u32(bar))
+                 : "memory");
+}
+
 // TMEM: allocation by one full warp; the base address is written to shared memory
 __device__ __forceinline__ void tmem_alloc(uint32_t *dst_smem, uint32_t ncols) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst_smem)),
@@ -81,6 +109,17 @@ __device__ __forceinline__ uint64_t smem_desc(uint32_t addr, uint32_t lbo, uint3
     d |= (uint64_t)((sbo >> 4) & 0x3FFFu) << 32;
     d |= (uint64_t)1 << 46;  // descriptor version for sm_100
     return d;                // base offset 0, layout type 0 (no swizzle)
+}
+// K-major with 64-byte swizzle (the layout a SWIZZLE_64B TMA box of 64-byte rows
+// writes): 8-row x 64-byte atoms `sbo` bytes apart; the leading offset is unused
+__device__ __forceinline__ uint64_t smem_desc_sw64(uint32_t addr, uint32_t sbo) {
+    uint64_t d = 0;
+    d |= (uint64_t)((addr >> 4) & 0x3FFFu);
+    d |= (uint64_t)1 << 16;  // leading byte offset field = 1 (ignored for swizzled K-major)
+    d |= (uint64_t)((sbo >> 4) & 0x3FFFu) << 32;
+    d |= (uint64_t)1 << 46;  // descriptor version for sm_100
+    d |= (uint64_t)4 << 61;  // layout type: 64-byte swizzle
+    return d;
 }
 // Instruction descriptor, kind::f16: f16 A and B (K-major), f32 accumulator, M x N
 __host__ __device__ constexpr uint32_t idesc_f16(int M, int N) {
