@@ -14,6 +14,7 @@ Under torchrun (N > 1) experts are sharded across ranks (expert parallelism) and
 routed q8_0 activations move with an NCCL all-to-all; see zunzuncito_b200/ep.py.
 """
 import argparse
+import ctypes
 import json
 import os
 import sys
@@ -131,6 +132,21 @@ def timed(torch, fn, steps, warmup, stream):
     t1.record(stream)
     torch.cuda.synchronize()
     return t0.elapsed_time(t1) / steps
+
+
+def graph_timed(torch, fn, steps, warmup):
+    """capture fn once into a CUDA graph, replay it; device time per replay (ms)"""
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        for _ in range(2):
+            fn()
+    torch.cuda.current_stream().wait_stream(s)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        fn()
+    return timed(torch, g.replay, steps, warmup, torch.cuda.current_stream())
 
 
 # ----------------------------------------------------------------------------- CPU
@@ -324,7 +340,23 @@ def sub_benchmarks(zz, torch, synth, stream, banks, hbm_peak):
     gbs = G * GEMV_BYTES / (ms / 1e3) / 1e9
     res["q40_gemv_2816"] = {"unit": "GB/s", "value": gbs, "frac_hbm": gbs / hbm_peak, "us_per_launch": ms * 1e3,
                             "gemvs_per_launch": G, "bytes_per_gemv": GEMV_BYTES}
-    del T
+    # one 2816 x 2816 GEMV per launch, cycling through the same 64 distinct matrices
+    # (285 MB > L2), launches replayed from a CUDA graph
+    subs = [zz.QTensor(zz.GPU_FMT_Q40, 2816, 2816, T.t.codes + g * 2816 * 1408,
+                       T.t.scale + g * 2816 * 88 * 2) for g in range(G)]
+    ys = torch.empty((G, 2816), device="cuda")
+
+    def one_each():
+        for g in range(G):
+            zz.check(zz.lib.zz_matvec_dev(ctypes.byref(subs[g]), ctypes.c_void_p(xq.data_ptr()),
+                                          ctypes.c_void_p(sx.data_ptr()), None,
+                                          ctypes.c_void_p(ys[g].data_ptr()), 1,
+                                          ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)))
+
+    ms1 = graph_timed(torch, one_each, 20, 3) / G
+    res["q40_gemv_2816_single"] = {"unit": "GB/s", "value": GEMV_BYTES / (ms1 / 1e3) / 1e9,
+                                   "us_per_gemv": ms1 * 1e3, "launch": "cuda graph, 64 distinct matrices"}
+    del T, subs
     # config 2: decode, M=1, 8 routed experts per layer, over the 30 resident layers
     L = len(banks)
     r1 = [synth.zipf_routing(300 + l, 1, E, K)[:2] for l in range(L)]
@@ -339,9 +371,13 @@ def sub_benchmarks(zz, torch, synth, stream, banks, hbm_peak):
         for l in range(L):
             zz.moe_ffn(banks[l], x1, e1[l], w1[l], zz.ZZ_ACT_GEGLU_TANH, out=o1)
 
-    ms = timed(torch, dec, 10, 3, stream)
+    ms_eager = timed(torch, dec, 10, 3, stream)
+    # the same 30 layer calls captured once in a CUDA graph and replayed: decode is
+    # launch-bound otherwise (a few microseconds of weight streaming per layer)
+    ms = graph_timed(torch, dec, 20, 3)
     res["decode_8_experts"] = {"unit": "us per layer", "value": ms * 1e3 / L,
-                               "hbm_gbs": 8 * EXPERT_BYTES / (ms / L / 1e3) / 1e9}
+                               "hbm_gbs": 8 * EXPERT_BYTES / (ms / L / 1e3) / 1e9,
+                               "eager_us_per_layer": ms_eager * 1e3 / L, "launch": "cuda graph of 30 layers"}
     # S=4096 prefill layer (compute-bound regime)
     S4 = 4096
     r4 = [synth.zipf_routing(400 + l, S4, E, K)[:2] for l in range(2)]

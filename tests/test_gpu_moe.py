@@ -123,7 +123,7 @@ def check_pairs(orc, kind, blobs, X, eidx, ewt, out_gpu, bank, pairs=None):
     return flipped_tok
 
 
-@pytest.fixture(params=["auto", "mma", "tc", "dec"])
+@pytest.fixture(params=["auto", "mma", "mma8", "tc", "dec"])
 def engine(request, monkeypatch):
     """every expert engine: auto (GEMV for small S*K, else mma.sync), mma.sync, tcgen05,
     and the small-batch GEMV kernels forced (ZZ_MOE_KERNEL)"""

@@ -36,7 +36,10 @@ namespace zz {
 
 enum { EPI_STORE = 0, EPI_GATEUP = 1, EPI_DOWN = 2 };
 
-constexpr int G_BM = 128, G_BKB = 4, G_STAGES = 3, G_THREADS = 256;
+#ifndef ZZ_G_STAGES
+#define ZZ_G_STAGES 2
+#endif
+constexpr int G_BM = 128, G_BKB = 4, G_STAGES = ZZ_G_STAGES, G_THREADS = 256;
 
 template <int FMT>
 struct FmtTraits {
@@ -97,6 +100,14 @@ __device__ __forceinline__ void mma_f16(float d[4], uint32_t a0, uint32_t a1, ui
         "{%10,%11,%12,%13};"
         : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
         : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "f"(c0), "f"(c1), "f"(c2), "f"(c3));
+}
+__device__ __forceinline__ void mma_s8(int c[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+                                       uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%10,%11,%12,%13};"
+        : "=r"(c[0]), "=r"(c[1]), "=r"(c[2]), "=r"(c[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(0), "r"(0), "r"(0), "r"(0));
 }
 __device__ __forceinline__ void ldsm_x4(uint32_t &r0, uint32_t &r1, uint32_t &r2, uint32_t &r3, const void *p) {
     uint32_t s = (uint32_t)__cvta_generic_to_shared(p);
@@ -182,7 +193,9 @@ struct GemmSmem {
     static constexpr int TOTAL = (PIPE > EPI ? PIPE : EPI) + BN * 16;  // + per-column info
 };
 
-template <int FMT, int BN, int EPI, bool B_HALF>
+// S8: int8 tensor-core path (m16n8k32.s8, int8 activations in shared memory, int32
+// block sums converted to fp32); else the fp16-exact path described above.
+template <int FMT, int BN, int EPI, bool B_HALF, bool S8 = false>
 __global__ void __launch_bounds__(G_THREADS) k_gemm(GemmArgs a) {
     using T = FmtTraits<FMT>;
     using L = GemmSmem<FMT, BN, B_HALF>;
@@ -306,7 +319,59 @@ __global__ void __launch_bounds__(G_THREADS) k_gemm(GemmArgs a) {
         const uint8_t *sb = sas + L::AS_BYTES;
         const float *sbs = reinterpret_cast<const float *>(sb + L::B_BYTES);
         const int nbk = nb - c * G_BKB < G_BKB ? nb - c * G_BKB : G_BKB;
-        for (int kb = 0; kb < nbk; kb++) {
+        // one K block: fragments, MMAs for the valid n8 tiles, block-scale epilogue
+        auto block8 = [&](int kb) {
+            // A fragment of m16n8k32: {row g k 4t.., row g+8 k 4t.., row g k 16+4t.., row g+8 k 16+4t..}
+            uint32_t a0, a1, a2, a3;
+            const uint8_t *r0 = sa + rA * T::A_STRIDE, *r1 = r0 + 8 * T::A_STRIDE;
+            if (FMT == GPU_FMT_Q40) {
+                // the q4_0 byte layout is the fragment split: low nibbles k, high k+16
+                uint32_t w0 = *reinterpret_cast<const uint32_t *>(r0 + kb * 16 + 4 * t);
+                uint32_t w1 = *reinterpret_cast<const uint32_t *>(r1 + kb * 16 + 4 * t);
+                a0 = nib_to_s8(w0); a2 = nib_to_s8(w0 >> 4);
+                a1 = nib_to_s8(w1); a3 = nib_to_s8(w1 >> 4);
+            } else if (FMT == GPU_FMT_Q80) {
+                const uint8_t *p0 = r0 + kb * 32 + 4 * t, *p1 = r1 + kb * 32 + 4 * t;
+                a0 = *reinterpret_cast<const uint32_t *>(p0); a2 = *reinterpret_cast<const uint32_t *>(p0 + 16);
+                a1 = *reinterpret_cast<const uint32_t *>(p1); a3 = *reinterpret_cast<const uint32_t *>(p1 + 16);
+            } else {
+                const int sh = (kb & 1) * 4;
+                uint32_t w0 = *reinterpret_cast<const uint32_t *>(r0 + (kb >> 1) * 16 + 4 * t);
+                uint32_t w1 = *reinterpret_cast<const uint32_t *>(r1 + (kb >> 1) * 16 + 4 * t);
+                a0 = (w0 >> sh) & 0x03030303u; a2 = (w0 >> (sh + 2)) & 0x03030303u;
+                a1 = (w1 >> sh) & 0x03030303u; a3 = (w1 >> (sh + 2)) & 0x03030303u;
+            }
+            float2 dw0 = make_float2(1.f, 1.f), dw1 = make_float2(1.f, 1.f);
+            if (T::HAS_WSCALE) {
+                const __half *hs = reinterpret_cast<const __half *>(sas);
+                float w0 = __half2float(hs[rA * G_BKB + kb]), w1 = __half2float(hs[(rA + 8) * G_BKB + kb]);
+                dw0 = make_float2(w0, w0);
+                dw1 = make_float2(w1, w1);
+            }
+#pragma unroll
+            for (int j = 0; j < NT; j++) {
+                if (j < jv) {
+                    const uint8_t *pb = sb + (j * 8 + g) * L::B_STRIDE + kb * 32 + 4 * t;
+                    int c[4];
+                    mma_s8(c, a0, a1, a2, a3, *reinterpret_cast<const uint32_t *>(pb),
+                           *reinterpret_cast<const uint32_t *>(pb + 16));
+                    const float2 dx = *reinterpret_cast<const float2 *>(sbs + kb * BN + j * 8 + 2 * t);
+                    const float2 d01 = make_float2((float)c[0], (float)c[1]), d23 = make_float2((float)c[2], (float)c[3]);
+                    if (T::HAS_WSCALE) {
+                        acc[j][0] = ffma2(fmul2(dw0, dx), d01, acc[j][0]);
+                        acc[j][1] = ffma2(fmul2(dw1, dx), d23, acc[j][1]);
+                    } else {
+                        acc[j][0] = ffma2(dx, d01, acc[j][0]);
+                        acc[j][1] = ffma2(dx, d23, acc[j][1]);
+                    }
+                }
+            }
+        };
+        auto block = [&](int kb) {
+            if constexpr (S8) {
+                block8(kb);
+                return;
+            }
             // A fragments of the two k16 steps of this block: s0 = k 0..15, s1 = k 16..31
             uint32_t a0[4], a1[4];  // {row g k 2t.., row g+8 k 2t.., row g k 2t+8.., row g+8 k 2t+8..}
             {
@@ -376,6 +441,13 @@ __global__ void __launch_bounds__(G_THREADS) k_gemm(GemmArgs a) {
                     }
                 }
             }
+        };
+        if (nbk == G_BKB) {
+            // full chunk: unrolled so the 4 blocks' MMA -> FMA chains interleave
+#pragma unroll
+            for (int kb = 0; kb < G_BKB; kb++) block(kb);
+        } else {
+            for (int kb = 0; kb < nbk; kb++) block(kb);
         }
     }
     cp_async_wait<0>();
@@ -426,7 +498,7 @@ __global__ void __launch_bounds__(G_THREADS) k_gemm(GemmArgs a) {
             int8_t q = quant_lane(h, d);
             const size_t pr = (size_t)(it.row0 + n);
             a.hq[pr * MI + f0 + f] = q;
-            a.hh[pr * MI + f0 + f] = __int2half_rn(q);
+            if (a.hh) a.hh[pr * MI + f0 + f] = __int2half_rn(q);
             if (lane == 0) a.hs[pr * nbh + f0 / 32 + hb] = d;
             if (FMT == GPU_FMT_TQ2) {
                 int s = q;

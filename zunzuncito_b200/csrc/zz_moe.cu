@@ -38,46 +38,51 @@ int launch_moe_tc(int fmt, int epi, const GemmArgs &a, int n_groups, int *err, c
 int launch_moe_dec(int fmt, const GemmArgs &gu, const GemmArgs &dn, int max_items, float *hbuf, cudaStream_t st);
 
 // Expert engine. Default ("auto"): the small-batch GEMV kernels (zz_moe_dec.cu) when
-// S*K <= DEC_MAX_PAIRS, else the mma.sync GEMM (k_gemm). ZZ_MOE_KERNEL=dec|mma|tc forces
-// one (tc = the tcgen05 kernel, k_moe_tc). All are exact per block.
-enum { ENG_DEC = 0, ENG_MMA = 1, ENG_TC = 2 };
+// S*K <= DEC_MAX_PAIRS, else the int8 mma.sync GEMM (k_gemm<..., S8>), the fastest
+// measured. ZZ_MOE_KERNEL=dec|mma8|mma|tc forces one (mma = the fp16-exact mma.sync
+// variant, tc = the tcgen05 kernel k_moe_tc). All are exact per block.
+enum { ENG_DEC = 0, ENG_MMA = 1, ENG_TC = 2, ENG_MMA8 = 3 };
 constexpr int DEC_MAX_PAIRS = 64;
 static int moe_engine(int P) {
     const char *e = getenv("ZZ_MOE_KERNEL");
     if (e && !strcmp(e, "tc")) return ENG_TC;
     if (e && !strcmp(e, "mma")) return ENG_MMA;
+    if (e && !strcmp(e, "mma8")) return ENG_MMA8;
     if (e && !strcmp(e, "dec")) return ENG_DEC;
-    return P <= DEC_MAX_PAIRS ? ENG_DEC : ENG_MMA;
+    return P <= DEC_MAX_PAIRS ? ENG_DEC : ENG_MMA8;
 }
 constexpr int TC_BN = 64;
 
-constexpr int MOE_BN = 64;
+#ifndef ZZ_MOE_BN
+#define ZZ_MOE_BN 32
+#endif
+constexpr int MOE_BN = ZZ_MOE_BN;
 constexpr int ROW_ALIGN = 16;
 constexpr int DEC_BN = 2;      // rows per work item of the small-batch kernels (DEC_C)  // pair rows of each expert start on a 16-row boundary
 constexpr int DENSE_BN = 64;
 
 static inline size_t a256(size_t n) { return (n + 255) & ~(size_t)255; }
 
-template <int FMT, int BN, int EPI, bool BH>
+template <int FMT, int BN, int EPI, bool BH, bool S8>
 static int launch_gemm_t(const GemmArgs &a, dim3 grid, cudaStream_t st) {
     constexpr int smem = GemmSmem<FMT, BN, BH>::TOTAL;
     static bool attr_set = false;  // per process; the library drives one device
     if (!attr_set) {
-        if (!check_cuda(cudaFuncSetAttribute(k_gemm<FMT, BN, EPI, BH>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        if (!check_cuda(cudaFuncSetAttribute(k_gemm<FMT, BN, EPI, BH, S8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              smem),
                         "gemm smem attribute"))
             return 0;
         attr_set = true;
     }
-    k_gemm<FMT, BN, EPI, BH><<<grid, G_THREADS, smem, st>>>(a);
+    k_gemm<FMT, BN, EPI, BH, S8><<<grid, G_THREADS, smem, st>>>(a);
     return check_cuda(cudaGetLastError(), "gemm launch");
 }
 
-template <int EPI, int BN, bool BH>
+template <int EPI, int BN, bool BH, bool S8 = false>
 static int launch_gemm(int fmt, const GemmArgs &a, dim3 grid, cudaStream_t st) {
-    if (fmt == GPU_FMT_Q40) return launch_gemm_t<GPU_FMT_Q40, BN, EPI, BH>(a, grid, st);
-    if (fmt == GPU_FMT_Q80) return launch_gemm_t<GPU_FMT_Q80, BN, EPI, BH>(a, grid, st);
-    return launch_gemm_t<GPU_FMT_TQ2, BN, EPI, BH>(a, grid, st);
+    if (fmt == GPU_FMT_Q40) return launch_gemm_t<GPU_FMT_Q40, BN, EPI, BH, S8>(a, grid, st);
+    if (fmt == GPU_FMT_Q80) return launch_gemm_t<GPU_FMT_Q80, BN, EPI, BH, S8>(a, grid, st);
+    return launch_gemm_t<GPU_FMT_TQ2, BN, EPI, BH, S8>(a, grid, st);
 }
 
 // ---------------------------------------------------------------- routing
@@ -335,18 +340,20 @@ static int moe_impl(const zz_expert_bank *b, const float *X, const int8_t *xq_in
     }
     prof_mark(st);
     if (!check_cuda(cudaMemsetAsync(OUT, 0, (size_t)S * D * 4, st), "memset OUT")) return 0;
+    const int eng = moe_engine(P);
+    const bool tcp = eng == ENG_TC;
     const int8_t *xq = xq_in;
     const float *xs = xs_in;
     if (X) {
-        if (!launch_quant_act(X, S, D, w.xq, w.xs, fmt == GPU_FMT_TQ2 ? w.xsx : nullptr, w.xh, st)) return 0;
+        const bool want_h = eng == ENG_MMA || eng == ENG_TC;  // engines reading fp16 activations
+        if (!launch_quant_act(X, S, D, w.xq, w.xs, fmt == GPU_FMT_TQ2 ? w.xsx : nullptr, want_h ? w.xh : nullptr, st))
+            return 0;
         xq = w.xq;
         xs = w.xs;
     } else {
         if (fmt == GPU_FMT_TQ2) k_rows_sx<<<(S + 127) / 128, 128, 0, st>>>(xq, xs, S, D, w.xsx);
-        if (!launch_s8_to_h(xq, w.xh, (long)S * D, st)) return 0;
+        if ((eng == ENG_MMA || eng == ENG_TC) && !launch_s8_to_h(xq, w.xh, (long)S * D, st)) return 0;
     }
-    const int eng = moe_engine(P);
-    const bool tcp = eng == ENG_TC;
     if (!check_cuda(cudaMemsetAsync(w.pair_src, 0xFF, w.cap * 4, st), "memset pair_src")) return 0;
     if (!check_cuda(cudaMemsetAsync(w.tcerr, 0, 4, st), "memset tc error")) return 0;
     k_route<<<1, 1024, 4 * E * sizeof(int), st>>>(eidx, ewt, P, E, tcp ? TC_BN : eng == ENG_DEC ? DEC_BN : MOE_BN,
@@ -388,11 +395,14 @@ static int moe_impl(const zz_expert_bank *b, const float *X, const int8_t *xq_in
     g.xq = w.xh; g.xs = xs; g.xsx = w.xsx; g.xblk = nullptr; g.gather = w.pair_src; g.gather_div = K;
     g.items = w.items; g.n_items = w.n_items;
     g.act = act; g.clamp = clamp;
-    g.hq = w.hq; g.hs = w.hs; g.hblk = w.hblk; g.hh = w.hh;
+    g.hq = w.hq; g.hs = w.hs; g.hblk = w.hblk; g.hh = (eng == ENG_MMA || tcp) ? w.hh : nullptr;
     g.xg = w.xg; g.xsT = w.xsT; g.ldT = (int)w.ldT; g.hsT = w.hsT; g.rows_cap = (int)w.cap;
     prof_mark(st);
     if (tcp) {
         if (!launch_moe_tc(fmt, EPI_GATEUP, g, E, w.tcerr, st)) return 0;
+    } else if (eng == ENG_MMA8) {
+        g.xq = xq;  // int8 rows
+        if (!launch_gemm<EPI_GATEUP, MOE_BN, false, true>(fmt, g, dim3((2 * MI) / G_BM, maxit), st)) return 0;
     } else if (!launch_gemm<EPI_GATEUP, MOE_BN, true>(fmt, g, dim3((2 * MI) / G_BM, maxit), st)) {
         return 0;
     }
@@ -407,8 +417,10 @@ static int moe_impl(const zz_expert_bank *b, const float *X, const int8_t *xq_in
     d.items = w.items; d.n_items = w.n_items;
     d.out = OUT; d.pair_w = w.pair_w; d.pair_src = w.pair_src; d.K = K;
     d.xg = w.hh; d.xsT = w.hsT; d.ldT = (int)w.ldT; d.rows_cap = (int)w.cap;
+    if (eng == ENG_MMA8) d.xq = w.hq;
     int ok = tcp ? launch_moe_tc(fmt, EPI_DOWN, d, E, w.tcerr, st)
-                 : launch_gemm<EPI_DOWN, MOE_BN, true>(fmt, d, dim3((D + G_BM - 1) / G_BM, maxit), st);
+             : eng == ENG_MMA8 ? launch_gemm<EPI_DOWN, MOE_BN, false, true>(fmt, d, dim3((D + G_BM - 1) / G_BM, maxit), st)
+                               : launch_gemm<EPI_DOWN, MOE_BN, true>(fmt, d, dim3((D + G_BM - 1) / G_BM, maxit), st);
     prof_mark(st);
     return ok;
 }
