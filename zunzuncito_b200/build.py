@@ -34,7 +34,8 @@ def build(force=False, verbose=False):
             print(" ".join(cmd), flush=True)
         subprocess.run(cmd, check=True)
         objs.append(o)
-    cmd = [NVCC, "-gencode", "arch=compute_100a,code=sm_100a", "-shared", "-o", LIB, *objs]
+    # -z defs: an unresolved symbol is a build error, not a load-time surprise
+    cmd = [NVCC, "-gencode", "arch=compute_100a,code=sm_100a", "-shared", "-Xlinker", "-z,defs", "-o", LIB, *objs]
     subprocess.run(cmd, check=True)
     return LIB
 

@@ -32,8 +32,10 @@ int launch_gemv1(const zz_qtensor *W, const int8_t *xq, const float *sx, const f
                  cudaStream_t st);
 int launch_blocksums(const zz_qtensor *W, const int8_t *xq, int32_t *out, cudaStream_t st);
 int launch_quant_act(const float *x, int S, int I, int8_t *xq, float *sx, float *sxtot, __half *xh,
-                     cudaStream_t st);
+                     cudaStream_t st, float *zero_out, int zero_cols);
 int launch_s8_to_h(const int8_t *q, __half *h, long n, cudaStream_t st);
+__global__ void k_rows_sx(const int8_t *__restrict__ xq, const float *__restrict__ xs, int S, int I,
+                          float *__restrict__ xsx);
 int launch_moe_tc(int fmt, int epi, const GemmArgs &a, int n_groups, int *err, cudaStream_t st);
 int launch_moe_dec(int fmt, const GemmArgs &gu, const GemmArgs &dn, int max_items, float *hbuf, cudaStream_t st);
 
@@ -88,28 +90,65 @@ static int launch_gemm(int fmt, const GemmArgs &a, dim3 grid, cudaStream_t st) {
 // ---------------------------------------------------------------- routing
 // One CTA. Pairs p = s*K + k with a valid expert go to slot off[e] + rank; the rank
 // order inside an expert is arbitrary (each pair's result is independent of its slot).
+// block-wide exclusive scan of v (one value per thread, blockDim.x == 1024)
+__device__ __forceinline__ int block_excl_scan(int v, int *warp_tot, int &total) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    int x = v;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        int y = __shfl_up_sync(0xffffffffu, x, o);
+        if (lane >= o) x += y;
+    }
+    if (lane == 31) warp_tot[warp] = x;
+    __syncthreads();
+    if (warp == 0) {
+        int t = warp_tot[lane];
+        int u = t;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            int y = __shfl_up_sync(0xffffffffu, u, o);
+            if (lane >= o) u += y;
+        }
+        warp_tot[lane] = u - t;  // exclusive prefix of warp totals
+        if (lane == 31) warp_tot[32] = u;
+    }
+    __syncthreads();
+    total = warp_tot[32];
+    int r = x - v + warp_tot[warp];
+    __syncthreads();
+    return r;
+}
+
+// One CTA of 1024 threads. Pairs p = s*K + k with a valid expert go to row off[e] + rank
+// (rank order inside an expert is arbitrary: each pair's result is independent of its
+// row); each expert's rows start on a ROW_ALIGN boundary and padding rows get src -1.
+// Also clears the tensor-core error word of the call. E <= 2048.
 __global__ void __launch_bounds__(1024) k_route(const int32_t *__restrict__ eidx, const float *__restrict__ ewt,
-                                                int P, int E, int BN, int *__restrict__ pair_src,
+                                                int P, int E, int BN, int cap, int *__restrict__ pair_src,
                                                 float *__restrict__ pair_w, WorkItem *__restrict__ items,
-                                                int *__restrict__ n_items) {
+                                                int *__restrict__ n_items, int *__restrict__ tcerr) {
     extern __shared__ int sh[];
     int *cnt = sh, *off = sh + E, *ioff = sh + 2 * E, *cur = sh + 3 * E;
+    __shared__ int warp_tot[33];
     for (int e = threadIdx.x; e < E; e += blockDim.x) { cnt[e] = 0; cur[e] = 0; }
+    if (threadIdx.x == 0) *tcerr = 0;
     __syncthreads();
     for (int p = threadIdx.x; p < P; p += blockDim.x) {
         int e = eidx[p];
         if (e >= 0 && e < E) atomicAdd(&cnt[e], 1);
     }
     __syncthreads();
-    if (threadIdx.x == 0) {
-        int o = 0, io = 0;
-        for (int e = 0; e < E; e++) {
-            off[e] = o; ioff[e] = io;
-            o += (cnt[e] + ROW_ALIGN - 1) / ROW_ALIGN * ROW_ALIGN;  // segments start 16-row aligned
-            io += (cnt[e] + BN - 1) / BN;
-        }
-        *n_items = io;
-    }
+    // each thread owns experts 2t and 2t+1 (E <= 2048)
+    const int e0 = 2 * threadIdx.x, e1 = e0 + 1;
+    const int c0 = e0 < E ? cnt[e0] : 0, c1 = e1 < E ? cnt[e1] : 0;
+    const int a0 = (c0 + ROW_ALIGN - 1) / ROW_ALIGN * ROW_ALIGN, a1 = (c1 + ROW_ALIGN - 1) / ROW_ALIGN * ROW_ALIGN;
+    const int i0 = (c0 + BN - 1) / BN, i1 = (c1 + BN - 1) / BN;
+    int rows_total, items_total;
+    const int ro = block_excl_scan(a0 + a1, warp_tot, rows_total);
+    const int io = block_excl_scan(i0 + i1, warp_tot, items_total);
+    if (e0 < E) { off[e0] = ro; ioff[e0] = io; }
+    if (e1 < E) { off[e1] = ro + a0; ioff[e1] = io + i0; }
+    if (threadIdx.x == 0) *n_items = items_total;
     __syncthreads();
     for (int p = threadIdx.x; p < P; p += blockDim.x) {
         int e = eidx[p];
@@ -122,7 +161,10 @@ __global__ void __launch_bounds__(1024) k_route(const int32_t *__restrict__ eidx
     for (int e = threadIdx.x; e < E; e += blockDim.x) {
         int c = cnt[e], ni = (c + BN - 1) / BN;
         for (int i = 0; i < ni; i++) items[ioff[e] + i] = WorkItem{e, off[e] + i * BN, min(BN, c - i * BN), 0};
+        int pad_end = off[e] + (c + ROW_ALIGN - 1) / ROW_ALIGN * ROW_ALIGN;
+        for (int r = off[e] + c; r < pad_end; r++) pair_src[r] = -1;
     }
+    for (int r = rows_total + threadIdx.x; r < cap; r += blockDim.x) pair_src[r] = -1;
 }
 
 __global__ void k_count_bad(const int32_t *eidx, int P, int E, int *bad) {
@@ -291,26 +333,6 @@ extern "C" size_t zz_moe_workspace_offset(const zz_expert_bank *b, int S, int K,
     return (size_t)((const uint8_t *)p - base);
 }
 
-// Sx of q8_0 rows (tq2 offset total, tq2.h:103-107), one thread per row
-__global__ void k_rows_sx(const int8_t *__restrict__ xq, const float *__restrict__ xs, int S, int I,
-                          float *__restrict__ xsx) {
-    int r = blockIdx.x * blockDim.x + threadIdx.x;
-    if (r >= S) return;
-    const int nb = I / 32;
-    double tot = 0;
-    for (int b = 0; b < nb; b++) {
-        const char4 *q = reinterpret_cast<const char4 *>(xq + (size_t)r * I + (size_t)b * 32);
-        int s = 0;
-#pragma unroll
-        for (int i = 0; i < 8; i++) {
-            char4 c = q[i];
-            s += c.x + c.y + c.z + c.w;
-        }
-        tot += (double)xs[(size_t)r * nb + b] * (double)s;
-    }
-    xsx[r] = (float)tot;
-}
-
 // X != NULL: f32 rows quantized here; else xq/xs are q8_0 rows given by the caller.
 static int moe_impl(const zz_expert_bank *b, const float *X, const int8_t *xq_in, const float *xs_in,
                     const int32_t *eidx, const float *ewt, float *OUT, int S, int K, int act, float clamp,
@@ -339,26 +361,24 @@ static int moe_impl(const zz_expert_bank *b, const float *X, const int8_t *xq_in
         if (bad) return fail("zz_moe_ffn: %d expert ids outside [0, %d)", bad, E);
     }
     prof_mark(st);
-    if (!check_cuda(cudaMemsetAsync(OUT, 0, (size_t)S * D * 4, st), "memset OUT")) return 0;
     const int eng = moe_engine(P);
     const bool tcp = eng == ENG_TC;
     const int8_t *xq = xq_in;
     const float *xs = xs_in;
     if (X) {
         const bool want_h = eng == ENG_MMA || eng == ENG_TC;  // engines reading fp16 activations
-        if (!launch_quant_act(X, S, D, w.xq, w.xs, fmt == GPU_FMT_TQ2 ? w.xsx : nullptr, want_h ? w.xh : nullptr, st))
+        if (!launch_quant_act(X, S, D, w.xq, w.xs, fmt == GPU_FMT_TQ2 ? w.xsx : nullptr, want_h ? w.xh : nullptr, st,
+                              OUT, D))
             return 0;
         xq = w.xq;
         xs = w.xs;
     } else {
+        if (!check_cuda(cudaMemsetAsync(OUT, 0, (size_t)S * D * 4, st), "memset OUT")) return 0;
         if (fmt == GPU_FMT_TQ2) k_rows_sx<<<(S + 127) / 128, 128, 0, st>>>(xq, xs, S, D, w.xsx);
         if ((eng == ENG_MMA || eng == ENG_TC) && !launch_s8_to_h(xq, w.xh, (long)S * D, st)) return 0;
     }
-    if (!check_cuda(cudaMemsetAsync(w.pair_src, 0xFF, w.cap * 4, st), "memset pair_src")) return 0;
-    if (!check_cuda(cudaMemsetAsync(w.tcerr, 0, 4, st), "memset tc error")) return 0;
     k_route<<<1, 1024, 4 * E * sizeof(int), st>>>(eidx, ewt, P, E, tcp ? TC_BN : eng == ENG_DEC ? DEC_BN : MOE_BN,
-                                                  w.pair_src, w.pair_w, w.items,
-                                                  w.n_items);
+                                                  (int)w.cap, w.pair_src, w.pair_w, w.items, w.n_items, w.tcerr);
     if (!check_cuda(cudaGetLastError(), "route launch")) return 0;
     if (tcp) {
         k_gather_rows<<<(unsigned)w.cap, 128, 0, st>>>(w.pair_src, K, (int)w.cap, w.xh, xs, D, w.xg, w.xsT, (int)w.ldT);

@@ -29,36 +29,46 @@ size_t codes_bytes(int fmt, int O, int I) { return align256((size_t)O * code_row
 size_t scales_bytes(int fmt, int O, int I) { return align256((size_t)O * scale_row_bytes(fmt, I)); }
 
 // ---------------------------------------------------------------- activations
-// One CTA per row, one warp per 32-block (lane = element). Bit-exact with
-// q40_quant_act (q40.h:124-138); with sxtot, the tq2 total of tq2_quant_act
-// (tq2.h:98-108) summed serially in double in block order, then rounded to f32.
-__global__ void k_quant_act(const float *__restrict__ x, int I, int8_t *__restrict__ xq,
-                            float *__restrict__ sx, float *__restrict__ sxtot, __half *__restrict__ xh) {
-    extern __shared__ int blk_sum[];
+// Grid (rows, chunks of 8 blocks), one warp per 32-block (lane = element): every block
+// of every row is in flight at once. Bit-exact with q40_quant_act (q40.h:124-138).
+// xh (optional) receives the codes as fp16; zero_out (optional) is an fp32 [rows,
+// zero_cols] buffer this pass clears (the MoE output, accumulated into afterwards).
+__global__ void k_quant_act(const float *__restrict__ x, int I, int8_t *__restrict__ xq, float *__restrict__ sx,
+                            __half *__restrict__ xh, float *__restrict__ zero_out, int zero_cols) {
     const int row = blockIdx.x, nb = I / ZZ_BLK;
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
-    const float *xr = x + (size_t)row * I;
-    for (int b = warp; b < nb; b += nw) {
-        float v = xr[b * ZZ_BLK + lane], d;
-        int8_t q = quant_lane(v, d);
-        xq[(size_t)row * I + b * ZZ_BLK + lane] = q;
-        if (xh) xh[(size_t)row * I + b * ZZ_BLK + lane] = __int2half_rn(q);
-        if (lane == 0) sx[(size_t)row * nb + b] = d;
-        if (sxtot) {
-            int s = q;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int b = blockIdx.y * 8 + warp;
+    if (zero_out) {
+        const int c = blockIdx.y * 256 + threadIdx.x;
+        if (c < zero_cols) zero_out[(size_t)row * zero_cols + c] = 0.f;
+    }
+    if (b >= nb) return;
+    float v = x[(size_t)row * I + b * ZZ_BLK + lane], d;
+    int8_t q = quant_lane(v, d);
+    xq[(size_t)row * I + b * ZZ_BLK + lane] = q;
+    if (xh) xh[(size_t)row * I + b * ZZ_BLK + lane] = __int2half_rn(q);
+    if (lane == 0) sx[(size_t)row * nb + b] = d;
+}
+
+// tq2 offset total of quantized rows: Sx = (float) sum_b (double)sx[b] * sum_j xq,
+// summed serially in block order (tq2.h:103-107); one thread per row
+__global__ void k_rows_sx(const int8_t *__restrict__ xq, const float *__restrict__ xs, int S, int I,
+                          float *__restrict__ xsx) {
+    int r = blockIdx.x * blockDim.x + threadIdx.x;
+    if (r >= S) return;
+    const int nb = I / 32;
+    double tot = 0;
+    for (int b = 0; b < nb; b++) {
+        const char4 *q = reinterpret_cast<const char4 *>(xq + (size_t)r * I + (size_t)b * 32);
+        int s = 0;
 #pragma unroll
-            for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-            if (lane == 0) blk_sum[b] = s;
+        for (int i = 0; i < 8; i++) {
+            char4 c = q[i];
+            s += c.x + c.y + c.z + c.w;
         }
+        tot += (double)xs[(size_t)r * nb + b] * (double)s;
     }
-    if (sxtot) {
-        __syncthreads();
-        if (threadIdx.x == 0) {
-            double tot = 0;
-            for (int b = 0; b < nb; b++) tot += (double)sx[(size_t)row * nb + b] * (double)blk_sum[b];
-            sxtot[row] = (float)tot;
-        }
-    }
+    xsx[r] = (float)tot;
 }
 
 // ---------------------------------------------------------------- weight quantizers
@@ -264,13 +274,20 @@ int launch_s8_to_h(const int8_t *q, __half *h, long n, cudaStream_t st) {
     k_s8_to_h<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(q, h, n);
     return check_cuda(cudaGetLastError(), "s8_to_h launch");
 }
-// quantize rows; xh (optional) receives the int8 codes as fp16 for the GEMM's B operand
+// quantize rows; xh (optional) receives the int8 codes as fp16 for the GEMM's B operand;
+// zero_out (optional) [S, zero_cols] is cleared in the same pass
 int launch_quant_act(const float *x, int S, int I, int8_t *xq, float *sx, float *sxtot, __half *xh,
-                     cudaStream_t st) {
-    size_t smem = sxtot ? (size_t)(I / ZZ_BLK) * sizeof(int) : 0;
-    if (smem > 48 * 1024) return fail("quant_act: I=%d too large for the Sx reduction", I);
-    k_quant_act<<<S, 256, smem, st>>>(x, I, xq, sx, sxtot, xh);
-    return check_cuda(cudaGetLastError(), "quant_act launch");
+                     cudaStream_t st, float *zero_out, int zero_cols) {
+    const int nb = I / ZZ_BLK;
+    int gy = (nb + 7) / 8;
+    if (zero_out) gy = max(gy, (zero_cols + 255) / 256);
+    k_quant_act<<<dim3(S, gy), 256, 0, st>>>(x, I, xq, sx, xh, zero_out, zero_cols);
+    if (!check_cuda(cudaGetLastError(), "quant_act launch")) return 0;
+    if (sxtot) {
+        k_rows_sx<<<(S + 127) / 128, 128, 0, st>>>(xq, sx, S, I, sxtot);
+        if (!check_cuda(cudaGetLastError(), "rows_sx launch")) return 0;
+    }
+    return 1;
 }
 }  // namespace zz
 
@@ -279,5 +296,5 @@ extern "C" int zz_quant_act_dev(const float *x, int S, int I, int8_t *xq, float 
     if (S < 0 || I <= 0 || I % 32) return fail("zz_quant_act_dev: I=%d must be a positive multiple of 32", I);
     if (S == 0) return 1;
     if (!x || !xq || !sx) return fail("zz_quant_act_dev: null pointer");
-    return launch_quant_act(x, S, I, xq, sx, sxtot, nullptr, (cudaStream_t)stream);
+    return launch_quant_act(x, S, I, xq, sx, sxtot, nullptr, (cudaStream_t)stream, nullptr, 0);
 }
