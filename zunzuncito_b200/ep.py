@@ -26,56 +26,46 @@ import torch
 import torch.distributed as dist
 
 
-def _a2a_counts(send_counts, group):
-    recv = torch.empty_like(send_counts)
-    dist.all_to_all_single(recv, send_counts, group=group)
-    return recv
-
-
 def ep_moe_layer(xq, xs, eidx, ewt, n_experts, local_ffn, group=None):
     """One expert-parallel MoE layer on this rank's tokens.
 
     xq [S, D] int8, xs [S, D/32] f32: this rank's quantized tokens; eidx [S, K] int32
     global expert ids, ewt [S, K] f32. local_ffn(xq_r, xs_r, eidx_r, ewt_r) -> [R, D]
     f32 runs this rank's experts (local ids, -1 = skip) over the R received rows.
-    Returns out [S, D] f32 = sum_k ewt[s,k] * FFN_{eidx[s,k]}(x_s)."""
+    Returns out [S, D] f32 = sum_k ewt[s,k] * FFN_{eidx[s,k]}(x_s).
+
+    Static exchange: token s bound for rank d always travels in slot (d, s), with the
+    routing entries that are not d's experts set to -1, so both all-to-alls use equal
+    splits and nothing waits on the host (no size exchange, graph-capturable). A slot
+    whose token routes nothing to d carries only -1 ids and comes back as zeros."""
     world = dist.get_world_size(group)
-    rank = dist.get_rank(group)
     dev = xq.device
     S, D = xq.shape
     K = eidx.shape[1]
-    nb = xs.shape[1]
     per = n_experts // world
     dst = (eidx // per).long()                                            # [S, K]
-    onehot = torch.zeros((S, world), dtype=torch.bool, device=dev)
-    onehot.scatter_(1, dst, True)
-    # rows grouped by destination, tokens ascending within a destination
-    d_idx, s_idx = onehot.t().nonzero(as_tuple=True)
-    send_counts = onehot.sum(0).to(torch.int64)
-    # routing restricted to the destination, as local ids (or -1)
-    loc = eidx[s_idx].long() - d_idx[:, None] * per
-    mine = (loc >= 0) & (loc < per)
-    loc_e = torch.where(mine, loc, torch.full_like(loc, -1)).to(torch.int32)
-    loc_w = torch.where(mine, ewt[s_idx], torch.zeros_like(ewt[s_idx]))
-    # one byte row per dispatched (token, destination): q8 codes | scales | ids | weights
-    payload = torch.cat([xq[s_idx].view(torch.uint8), xs[s_idx].contiguous().view(torch.uint8),
-                         loc_e.contiguous().view(torch.uint8), loc_w.contiguous().view(torch.uint8)], dim=1)
-    row_bytes = D + 4 * nb + 8 * K
-    recv_counts = _a2a_counts(send_counts, group)
-    sc, rc = send_counts.tolist(), recv_counts.tolist()
-    recv = torch.empty((sum(rc), row_bytes), dtype=torch.uint8, device=dev)
-    dist.all_to_all_single(recv, payload, output_split_sizes=rc, input_split_sizes=sc, group=group)
-    R = recv.shape[0]
+    ranks = torch.arange(world, device=dev).view(world, 1, 1)
+    mine = dst.unsqueeze(0) == ranks                                      # [world, S, K]
+    loc_e = torch.where(mine, (eidx.unsqueeze(0) - ranks * per).to(torch.int32),
+                        torch.full((), -1, dtype=torch.int32, device=dev))
+    loc_w = torch.where(mine, ewt.unsqueeze(0), torch.zeros((), dtype=ewt.dtype, device=dev))
+    # one byte row per (destination, token): q8 codes | block scales | local ids | weights
+    tok = torch.cat([xq.view(torch.uint8), xs.contiguous().view(torch.uint8)], dim=1)  # [S, D + 4 nb]
+    payload = torch.cat([tok.unsqueeze(0).expand(world, S, tok.shape[1]),
+                         loc_e.view(torch.uint8).view(world, S, 4 * K),
+                         loc_w.contiguous().view(torch.uint8).view(world, S, 4 * K)], dim=2).contiguous()
+    recv = torch.empty_like(payload)
+    dist.all_to_all_single(recv.view(world, -1), payload.view(world, -1), group=group)
+    recv = recv.view(world * S, -1)
+    nb = xs.shape[1]
     r_xq = recv[:, :D].contiguous().view(torch.int8)
     r_xs = recv[:, D:D + 4 * nb].contiguous().view(torch.float32)
     r_e = recv[:, D + 4 * nb:D + 4 * nb + 4 * K].contiguous().view(torch.int32)
     r_w = recv[:, D + 4 * nb + 4 * K:].contiguous().view(torch.float32)
-    part = local_ffn(r_xq, r_xs, r_e, r_w) if R else torch.zeros((0, D), dtype=torch.float32, device=dev)
-    back = torch.empty((len(s_idx), D), dtype=torch.float32, device=dev)
-    dist.all_to_all_single(back, part.contiguous(), output_split_sizes=sc, input_split_sizes=rc, group=group)
-    out = torch.zeros((S, D), dtype=torch.float32, device=dev)
-    out.index_add_(0, s_idx, back)
-    return out
+    part = local_ffn(r_xq, r_xs, r_e, r_w).contiguous()                  # [world * S, D]
+    back = torch.empty_like(part)
+    dist.all_to_all_single(back.view(world, -1), part.view(world, -1), group=group)
+    return back.view(world, S, D).sum(0)
 
 
 # ----------------------------------------------------------------------------- bench
