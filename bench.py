@@ -43,6 +43,8 @@ def parse():
     ap.add_argument("--layers", type=int, default=LAYERS)
     ap.add_argument("--no-sub", action="store_true", help="skip the sub-benchmarks")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
+    ap.add_argument("--profile-case", choices=["moe", "gemv", "decode"],
+                    help="run a small case of one kernel family a few times and exit (for ncu)")
     return ap.parse_args()
 
 
@@ -132,6 +134,29 @@ def timed(torch, fn, steps, warmup, stream):
     t1.record(stream)
     torch.cuda.synchronize()
     return t0.elapsed_time(t1) / steps
+
+
+def profile_case(kind, zz, torch, synth):
+    """small cases sized for an ncu capture (a few GB at most on the device)"""
+    if kind == "gemv":
+        G = 64  # 64 distinct 2816 x 2816 q4_0 matrices stacked: 285 MB > L2
+        w = torch.randn((G * 2816, 2816), device="cuda") * 0.02
+        T = zz.QTensorDev(zz.GPU_FMT_Q40, zz.quant_rows(zz.GPU_FMT_Q40, w), G * 2816, 2816)
+        del w
+        xq, sx, _ = zz.quant_act(torch.randn((1, 2816), device="cuda"))
+        for _ in range(3):
+            zz.matvec(T, xq, sx)
+    else:
+        banks, _ = make_stack(zz, torch, 2, seed=77)
+        S = 512 if kind == "moe" else 1
+        for l in range(2):
+            r = synth.zipf_routing(88 + l, S, E, K)
+            X = torch.randn((S, D), device="cuda")
+            for _ in range(2):
+                zz.moe_ffn(banks[l], X, torch.from_numpy(r[0]).cuda(), torch.from_numpy(r[1]).cuda(),
+                           zz.ZZ_ACT_GEGLU_TANH)
+    torch.cuda.synchronize()
+    print(f"profile case {kind} done")
 
 
 def graph_timed(torch, fn, steps, warmup):
@@ -232,6 +257,9 @@ def main():
     from zunzuncito_b200 import synth
 
     torch.cuda.set_device(0)
+    if a.profile_case:
+        profile_case(a.profile_case, zz, torch, synth)
+        return
     stream = torch.cuda.current_stream()
     S, L = a.tokens, a.layers
     banks, host0 = make_stack(zz, torch, L, seed=1234, keep_host_layer0=not a.no_cpu)
