@@ -53,7 +53,7 @@ static int moe_engine(int P) {
     if (e && !strcmp(e, "dec")) return ENG_DEC;
     return P <= DEC_MAX_PAIRS ? ENG_DEC : ENG_MMA8;
 }
-constexpr int TC_BN = 64;
+constexpr int TC_BN = 32;
 
 #ifndef ZZ_MOE_BN
 #define ZZ_MOE_BN 32

@@ -1,22 +1,31 @@
 // zz_moe_tc.cu -- the batch-union expert GEMMs on the 5th-generation tensor cores.
 //
 // Persistent, warp-specialised kernel, one CTA per SM, looping over work tiles
-// (expert item x 128 weight rows). Roles (448 threads):
-//   warp 12      TMA: streams the packed weight codes of the tile (128 rows x 64 B
-//                boxes) into a 6-slot ring, ~48 KB in flight per SM
-//   warps 8-11   producers: thread r widens row r's codes of one 32-weight block to
+// (expert item of <= 32 token rows x 128 weight rows). K advances in stages of KB = 4
+// quantization blocks (K = 128); every hand-off between roles is one mbarrier phase
+// per stage. Roles (512 threads):
+//   warp 12      TMA: one box per stage of the tile's packed weight codes (128 rows x
+//                KB blocks, swizzled so the producers' 16-byte shared loads are bank-
+//                conflict free) into a 32 KB ring
+//   warp 14      TMA: the stage's fp16 activation tiles (one 64-byte-swizzled K-major
+//                box of the item's rows per block)
+//   warp 15      bulk copies: the stage's activation block scales; TMA: the tile's
+//                fp16 weight block scales, 128 rows x 8 blocks per box
+//   warps 8-11   producers: thread r widens row r's codes of the stage's blocks to
 //                fp16 in the UMMA canonical K-major layout (8-row x 16-byte core
-//                matrices, no swizzle), and gathers the token rows' fp16 activations
-//                and their block scales with cp.async, several blocks ahead
-//   warp 13      MMA: one thread issues two tcgen05.mma kind::f16 (M=128, N = tokens
-//                rounded to 16, K=16 each) per block into one of 4 TMEM accumulators
-//   warps 0-7    epilogue: tcgen05.ld of the block's 128 x N f32 results, which are
-//                the reference's exact per-block integer sums (the fp16 operands are
-//                the integer codes themselves), then acc += (dw*dx) * sum in packed
-//                fp32 (the decomposition of q40.h:20-31); at the tile end the fused
-//                gate/up GeGLU + q8 requant or down-projection scatter-add.
-// Per block the tensor cores run while the producers widen the next blocks and the
-// epilogue scales the previous one; TMEM decouples MMA from the epilogue.
+//                matrices, no swizzle); the fp16 values are the integer codes
+//   warp 13      MMA: one thread issues, per block of the stage, two tcgen05.mma
+//                kind::f16 (M=128, N = item rows rounded to 16, K=16) into that
+//                block's own TMEM accumulator (KB accumulators per stage, four stages
+//                resident)
+//   warps 0-7    epilogue: tcgen05.ld (16x256b shape: 4 rows x 8 tokens per thread)
+//                of each block's 128 x N f32 results -- the reference's exact per-block
+//                integer sums -- then acc += (dw*dx) * sum in packed fp32 (the
+//                decomposition of q40.h:20-31). The two warp groups take alternate
+//                stages and add their partial sums at the tile end, so every token's
+//                sum has the same order whatever tile it lands in; then the fused
+//                gate/up GeGLU + q8 requant or the down-projection scatter-add.
+// Waits are bounded (2 s); one that runs out sets the kernel's error word.
 #include <cstdlib>
 #include <cuda.h>
 #include <cudaTypedefs.h>
@@ -27,61 +36,68 @@ namespace zz {
 
 namespace tcm {
 constexpr int NTHREADS = 512;
-constexpr int BN = 64;            // max activation rows per tile
-constexpr int NACC = 8;           // TMEM accumulators (NACC * BN = 512 columns)
-constexpr int RC = 4;             // weight-code ring slots (4 blocks each for q4_0)
-constexpr int SLOT = 128 * 64;    // one code box: 128 rows x 64 bytes
-constexpr int NS = 4;             // widened-weight (A) stages
-constexpr int RB = 24;            // activation (B) ring slots
-constexpr int A_BYTES = 128 * 64;  // 128 rows x 32 fp16, K-major core matrices
-constexpr int B_BYTES = BN * 64;   // up to 64 rows x 32 fp16, 64-byte swizzle
-constexpr int DX_BYTES = BN * 4;
-constexpr int NDX = 16;           // activation-scale ring (freed by the epilogue)
-constexpr int CS = BN + 4;        // padded row of the fp32 result tile
-constexpr int OFF_B = 0;          // 1024-aligned (swizzled TMA destination)
-constexpr int OFF_RING = OFF_B + RB * B_BYTES;
-constexpr int OFF_A = OFF_RING + RC * SLOT;
-constexpr int OFF_DX = OFF_A + NS * A_BYTES;
-constexpr int OFF_CT = OFF_DX + NDX * DX_BYTES;
+constexpr int BN = 32;             // max activation rows per tile
+constexpr int KB = 4;              // quantization blocks per stage
+constexpr int NACC = 4;            // TMEM stages: NACC * KB * BN = 512 columns
+constexpr int RING = 32 * 1024;    // weight-code ring
+constexpr int NS = 2;              // widened-weight (A) stages
+constexpr int A_BLK = 128 * 64;    // one block: 128 rows x 32 fp16, K-major core matrices
+constexpr int A_STAGE = KB * A_BLK;
+constexpr int RB = 8;              // activation (B) stages
+constexpr int B_BLK = BN * 64;     // up to 32 rows x 32 fp16, 64-byte swizzle
+constexpr int B_STAGE = KB * B_BLK;
+constexpr int ND = 16;             // activation-scale stages
+constexpr int DX_BLK = BN * 4;
+constexpr int DX_STAGE = KB * DX_BLK;
+constexpr int CS = BN + 4;         // padded row of the fp32 result tile
+constexpr int RC_MAX = 8;          // ring slots for the narrowest format (tq2)
+constexpr int NW = 8;              // weight-scale ring: 128 rows x 8 fp16 (two stages) per slot
+constexpr int W_SLOT = 128 * 16;
+constexpr int OFF_B = 0;           // 1 KB aligned (swizzled TMA destinations)
+constexpr int OFF_RING = OFF_B + RB * B_STAGE;
+constexpr int OFF_A = OFF_RING + RING;
+constexpr int OFF_DX = OFF_A + NS * A_STAGE;
+constexpr int OFF_W = OFF_DX + ND * DX_STAGE;
+constexpr int OFF_CT = OFF_W + NW * W_SLOT;
 constexpr int OFF_INFO = OFF_CT + 128 * CS * 4;
-constexpr int OFF_BAR = OFF_INFO + BN * 12;
-constexpr int NBAR = 2 * RC + 2 * NS + 2 * RB + 2 * NACC + 2 * NDX;
+constexpr int OFF_BAR = OFF_INFO + BN * 8;
+constexpr int NBAR = 2 * RC_MAX + 2 * NS + 2 * RB + 2 * NACC + 2 * ND + 2 * NW;
 constexpr int SMEM = OFF_BAR + NBAR * 8 + 16 + 1024;  // + slack to align the base to 1 KB
+static_assert(SMEM <= 232448, "shared memory");
 }  // namespace tcm
 
-// offset of block j's codes inside one weight row, and the bytes it spans
+// code bytes of one row for one stage (KB blocks); the TMA box is 128 rows of this
 template <int FMT>
-__device__ __forceinline__ int blk_byte(int j) {
-    return FMT == GPU_FMT_Q40 ? j * 16 : FMT == GPU_FMT_Q80 ? j * 32 : (j >> 1) * 16;
-}
+__host__ __device__ constexpr int tc_cb() { return FMT == GPU_FMT_Q40 ? 64 : FMT == GPU_FMT_Q80 ? 128 : 32; }
 template <int FMT>
-__device__ __forceinline__ int blk_span() { return FMT == GPU_FMT_Q80 ? 32 : 16; }
+__host__ __device__ constexpr int tc_rc() { return tcm::RING / (128 * tc_cb<FMT>()); }
 
 __device__ __forceinline__ uint32_t spread_lo(uint32_t w) { return __byte_perm(w, 0u, 0x4140u); }
 __device__ __forceinline__ uint32_t spread_hi(uint32_t w) { return __byte_perm(w, 0u, 0x4342u); }
 
-// widen one row's codes of one block into the 4 K-chunks (8 fp16 each) of the A tile
+// widen one row's codes of block jj of the stage (in registers, 16-byte chunks of
+// the row's stage bytes) into the block's 4 K-chunks of 8 fp16
 template <int FMT>
-__device__ __forceinline__ void widen_row(const uint8_t *src, int j, uint4 out[4]) {
+__device__ __forceinline__ void widen_blk(const uint4 (&c)[tc_cb<FMT>() / 16], int jj, uint4 out[4]) {
     if (FMT == GPU_FMT_Q40) {
-        uint4 w = *reinterpret_cast<const uint4 *>(src);
-        // k 0-7: low nibbles of bytes 0-7; k 8-15: bytes 8-15; k 16-31: the high nibbles
+        const uint4 w = c[jj];
+        // k 0-15: low nibbles of bytes 0-15; k 16-31: the high nibbles
         out[0] = make_uint4(q4lo_h2(spread_lo(w.x)), q4lo_h2(spread_hi(w.x)), q4lo_h2(spread_lo(w.y)), q4lo_h2(spread_hi(w.y)));
         out[1] = make_uint4(q4lo_h2(spread_lo(w.z)), q4lo_h2(spread_hi(w.z)), q4lo_h2(spread_lo(w.w)), q4lo_h2(spread_hi(w.w)));
         out[2] = make_uint4(q4hi_h2(spread_lo(w.x)), q4hi_h2(spread_hi(w.x)), q4hi_h2(spread_lo(w.y)), q4hi_h2(spread_hi(w.y)));
         out[3] = make_uint4(q4hi_h2(spread_lo(w.z)), q4hi_h2(spread_hi(w.z)), q4hi_h2(spread_lo(w.w)), q4hi_h2(spread_hi(w.w)));
     } else if (FMT == GPU_FMT_Q80) {
-        const uint4 *p = reinterpret_cast<const uint4 *>(src);
-        uint4 w0 = p[0], w1 = p[1];
+        const uint4 w0 = c[2 * jj], w1 = c[2 * jj + 1];
         out[0] = make_uint4(s8_h2(spread_lo(w0.x)), s8_h2(spread_hi(w0.x)), s8_h2(spread_lo(w0.y)), s8_h2(spread_hi(w0.y)));
         out[1] = make_uint4(s8_h2(spread_lo(w0.z)), s8_h2(spread_hi(w0.z)), s8_h2(spread_lo(w0.w)), s8_h2(spread_hi(w0.w)));
         out[2] = make_uint4(s8_h2(spread_lo(w1.x)), s8_h2(spread_hi(w1.x)), s8_h2(spread_lo(w1.y)), s8_h2(spread_hi(w1.y)));
         out[3] = make_uint4(s8_h2(spread_lo(w1.z)), s8_h2(spread_hi(w1.z)), s8_h2(spread_lo(w1.w)), s8_h2(spread_hi(w1.w)));
     } else {
-        // tq2: the block's 32 codes sit in the 16 bytes of its 64-weight group, at bit
-        // offset sh (k 0-15) and sh+2 (k 16-31), sh = 0 for even blocks, 4 for odd
-        uint4 w = *reinterpret_cast<const uint4 *>(src);
-        const int sh = (j & 1) * 4;
+        // tq2: a pair of blocks shares the 16 bytes of its 64-weight group; block jj's
+        // codes sit at bit offset sh (k 0-15) and sh+2 (k 16-31), sh = 0 / 4 for the
+        // even / odd block
+        const uint4 w = c[jj >> 1];
+        const int sh = (jj & 1) * 4;
         out[0] = make_uint4(c2_h2(spread_lo(w.x), sh), c2_h2(spread_hi(w.x), sh), c2_h2(spread_lo(w.y), sh), c2_h2(spread_hi(w.y), sh));
         out[1] = make_uint4(c2_h2(spread_lo(w.z), sh), c2_h2(spread_hi(w.z), sh), c2_h2(spread_lo(w.w), sh), c2_h2(spread_hi(w.w), sh));
         out[2] = make_uint4(c2_h2(spread_lo(w.x), sh + 2), c2_h2(spread_hi(w.x), sh + 2), c2_h2(spread_lo(w.y), sh + 2), c2_h2(spread_hi(w.y), sh + 2));
@@ -90,7 +106,7 @@ __device__ __forceinline__ void widen_row(const uint8_t *src, int j, uint4 out[4
 }
 
 struct BMaps {
-    CUtensorMap m[3];  // activation boxes of 16, 32 and 64 rows
+    CUtensorMap m[2];  // activation boxes of 16 and 32 rows
 };
 
 struct TcTile {
@@ -103,157 +119,193 @@ __device__ __forceinline__ TcTile tc_tile(const GemmArgs &a, int t, int MT) {
     r.m0 = (t % MT) * 128;
     return r;
 }
+__device__ __forceinline__ int tc_sel(int count) {
+    const int N = (count + 15) & ~15;
+    return N <= 16 ? 0 : 1;
+}
 
 template <int FMT, int EPI>
 __global__ void __launch_bounds__(tcm::NTHREADS, 1)
-    k_moe_tc(const GemmArgs a, const __grid_constant__ CUtensorMap codes_map, const __grid_constant__ BMaps bmaps,
-             int *err) {
+    k_moe_tc(const GemmArgs a, const __grid_constant__ CUtensorMap codes_map,
+             const __grid_constant__ CUtensorMap scale_map, const __grid_constant__ BMaps bmaps, int *err) {
     using namespace tcm;
+    constexpr int CB = tc_cb<FMT>(), RC = tc_rc<FMT>(), SLOTB = 128 * CB, NCH = CB / 16;
     extern __shared__ __align__(128) uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
     uint8_t *ring = smem + OFF_RING;
     uint8_t *stages = smem + OFF_A;
     uint8_t *bring = smem + OFF_B;
+    uint8_t *dxring = smem + OFF_DX;
     float *ct = reinterpret_cast<float *>(smem + OFF_CT);
     int *col_xrow = reinterpret_cast<int *>(smem + OFF_INFO);
     float *col_sx = reinterpret_cast<float *>(smem + OFF_INFO + BN * 4);
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem + OFF_BAR);
-    uint64_t *cfull = bars, *cempty = bars + RC, *sfull = bars + 2 * RC, *sempty = bars + 2 * RC + NS;
-    uint64_t *tfull = bars + 2 * RC + 2 * NS, *tempty = bars + 2 * RC + 2 * NS + NACC;
-    uint64_t *dfull = tempty + NACC, *dempty = dfull + NDX, *bfull = dempty + NDX, *bempty = bfull + RB;
-    uint8_t *dxring = smem + OFF_DX;
+    uint64_t *cfull = bars, *cempty = bars + RC_MAX;
+    uint64_t *sfull = bars + 2 * RC_MAX, *sempty = sfull + NS;
+    uint64_t *bfull = sempty + NS, *bempty = bfull + RB;
+    uint64_t *tfull = bempty + RB, *tempty = tfull + NACC;
+    uint64_t *dfull = tempty + NACC, *dempty = dfull + ND;
+    uint64_t *wfull = dempty + ND, *wempty = wfull + NW;
+    uint8_t *wring = smem + OFF_W;
+    constexpr bool HAS_DW = FMT != GPU_FMT_TQ2;
     uint32_t *tmem_base_smem = reinterpret_cast<uint32_t *>(smem + OFF_BAR + NBAR * 8);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + OFF_BAR + NBAR * 8 + 4);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int nb = a.I / ZZ_BLK, nbp = (nb + 7) & ~7;
+    const int nb = a.I / ZZ_BLK;
+    const int nss = (nb + KB - 1) / KB;
     const int MT = a.O / 128;
     const int T = *a.n_items * MT;
-    const int row_bytes = FMT == GPU_FMT_Q40 ? a.I / 2 : FMT == GPU_FMT_Q80 ? a.I : a.I / 4;
-    const int nslots = (row_bytes + 63) / 64;
 
     if (tid == 0) {
-        for (int i = 0; i < RC; i++) { tc::mbar_init(&cfull[i], 1); tc::mbar_init(&cempty[i], 128); }
-        for (int i = 0; i < NS; i++) { tc::mbar_init(&sfull[i], 128); tc::mbar_init(&sempty[i], 1); }
-        for (int i = 0; i < NDX; i++) { tc::mbar_init(&dfull[i], 1); tc::mbar_init(&dempty[i], 8); }
+        for (int i = 0; i < RC; i++) { tc::mbar_init(&cfull[i], 1); tc::mbar_init(&cempty[i], 4); }
+        for (int i = 0; i < NS; i++) { tc::mbar_init(&sfull[i], 4); tc::mbar_init(&sempty[i], 1); }
         for (int i = 0; i < RB; i++) { tc::mbar_init(&bfull[i], 1); tc::mbar_init(&bempty[i], 1); }
         for (int i = 0; i < NACC; i++) { tc::mbar_init(&tfull[i], 1); tc::mbar_init(&tempty[i], 8); }
+        for (int i = 0; i < ND; i++) { tc::mbar_init(&dfull[i], 1); tc::mbar_init(&dempty[i], 8); }
+        for (int i = 0; i < NW; i++) { tc::mbar_init(&wfull[i], 1); tc::mbar_init(&wempty[i], 8); }
         *abort_flag = 0;
         tc::mbar_init_fence();
     }
-    if (warp == 13) tc::tmem_alloc(tmem_base_smem, NACC * BN);
+    if (warp == 13) tc::tmem_alloc(tmem_base_smem, NACC * KB * BN);
     tc::tc_fence_before();
     __syncthreads();
     tc::tc_fence_after();
     const uint32_t tbase = *tmem_base_smem;
 #ifdef ZZ_TC_PROF
-    if (blockIdx.x == 0 && tid == 0) atomicAdd(&tc::g_tc_prof[30], (unsigned long long)clock64());
+    const long long prof_t0 = clock64();
 #endif
-
-    // activation-tile issue loop (one thread); the tensor map is named with a constant
-    // index so it stays in parameter space
-    auto issue_b_tiles = [&]() {
-        uint32_t g = 0, last = 0;
-        bool any = false;
-        for (int t = blockIdx.x; t < T && !*abort_flag; t += gridDim.x) {
-            TcTile tl = tc_tile(a, t, MT);
-            const int N = (tl.it.count + 15) & ~15;
-            const int sel = N <= 16 ? 0 : N <= 32 ? 1 : 2;
-            const uint32_t bbytes = (16u << sel) * 64u;
-            bool ok = true;
-            for (int j = 0; j < nb && ok; j++, g++) {
-                const int bs = g % RB;
-                const uint32_t u = g / RB;
-                if (u && !tc::mbar_wait(&bempty[bs], (u - 1) & 1, abort_flag, err, 3)) { ok = false; break; }
-                tc::mbar_arrive_tx(&bfull[bs], bbytes);
-                uint8_t *dst = bring + bs * B_BYTES;
-                // rows row0.. of the pair-ordered activations, halves 32j..32j+31: one
-                // 64-byte-swizzled K-major tile
-                switch (sel) {
-                    case 0: tc::tma_load_2d(dst, &bmaps.m[0], j * 32, tl.it.row0, &bfull[bs]); break;
-                    case 1: tc::tma_load_2d(dst, &bmaps.m[1], j * 32, tl.it.row0, &bfull[bs]); break;
-                    default: tc::tma_load_2d(dst, &bmaps.m[2], j * 32, tl.it.row0, &bfull[bs]); break;
-                }
-                last = g;
-                any = true;
-            }
-        }
-        if (any) tc::mbar_wait(&bfull[last % RB], (last / RB) & 1, abort_flag, err, 12);
-    };
 
     if (warp == 12) {
         if (lane == 0) {
-            // ---------------- TMA: weight codes -> ring (deep, from HBM) ----------------
-            uint32_t c = 0;
-            for (int t = blockIdx.x; t < T && !*abort_flag; t += gridDim.x) {
-                TcTile tl = tc_tile(a, t, MT);
-                const int y = tl.it.group * a.O + tl.m0;
-                for (int i = 0; i < nslots; i++, c++) {
-                    const int s = c % RC;
-                    const uint32_t u = c / RC;
-                    if (u && !tc::mbar_wait(&cempty[s], (u - 1) & 1, abort_flag, err, 1)) break;
-                    tc::mbar_arrive_tx(&cfull[s], SLOT);
-                    tc::tma_load_2d(ring + s * SLOT, &codes_map, i * 64, y, &cfull[s]);
-                }
-            }
-            // bounded drain: do not leave the CTA with copies in flight
-            if (c) tc::mbar_wait(&cfull[(c - 1) % RC], ((c - 1) / RC) & 1, abort_flag, err, 2);
-        } else if (lane == 1) {
-        }
-    } else if (warp == 14) {
-        // ---------------- TMA: activation tiles ----------------
-        if (lane == 0) issue_b_tiles();
-    } else if (warp == 15) {
-        if (lane == 0) {
-            // ---------------- bulk copies: the tiles' activation block scales ----------------
+            // ---------------- TMA: weight codes -> ring, one box per stage ----------------
             uint32_t g = 0;
             for (int t = blockIdx.x; t < T && !*abort_flag; t += gridDim.x) {
                 TcTile tl = tc_tile(a, t, MT);
+                const int y = tl.it.group * a.O + tl.m0;
                 bool ok = true;
-                for (int j = 0; j < nb && ok; j++, g++) {
-                    const int ds = g % NDX;
-                    const uint32_t du = g / NDX;
-                    if (du && !tc::mbar_wait(&dempty[ds], (du - 1) & 1, abort_flag, err, 11)) { ok = false; break; }
-                    tc::mbar_arrive_tx(&dfull[ds], DX_BYTES);
-                    tc::bulk_load(dxring + ds * DX_BYTES, a.xsT + (size_t)j * a.ldT + tl.it.row0, DX_BYTES, &dfull[ds]);
+                for (int ss = 0; ss < nss; ss++, g++) {
+                    const int s = g % RC;
+                    const uint32_t u = g / RC;
+                    if (u && !tc::mbar_wait(&cempty[s], (u - 1) & 1, abort_flag, err, 1)) { ok = false; break; }
+                    tc::mbar_arrive_tx(&cfull[s], SLOTB);
+                    tc::tma_load_2d(ring + s * SLOTB, &codes_map, ss * CB, y, &cfull[s]);
                 }
+                if (!ok) break;
             }
-            if (g) tc::mbar_wait(&dfull[(g - 1) % NDX], ((g - 1) / NDX) & 1, abort_flag, err, 13);
+            // bounded drain: do not leave the CTA with copies in flight
+            if (g) tc::mbar_wait(&cfull[(g - 1) % RC], ((g - 1) / RC) & 1, abort_flag, err, 2);
+        }
+    } else if (warp == 14) {
+        if (lane == 0) {
+            // ---------------- TMA: activation tiles, one box per block ----------------
+            uint32_t g = 0;
+            for (int t = blockIdx.x; t < T && !*abort_flag; t += gridDim.x) {
+                TcTile tl = tc_tile(a, t, MT);
+                const int sel = tc_sel(tl.it.count);
+                const uint32_t bblk = (16u << sel) * 64u;
+                bool ok = true;
+                for (int ss = 0; ss < nss; ss++, g++) {
+                    const int bs = g % RB;
+                    const uint32_t u = g / RB;
+                    if (u && !tc::mbar_wait(&bempty[bs], (u - 1) & 1, abort_flag, err, 3)) { ok = false; break; }
+                    const int nbl = min(KB, nb - ss * KB);
+                    tc::mbar_arrive_tx(&bfull[bs], bblk * nbl);
+                    uint8_t *dst = bring + bs * B_STAGE;
+                    // rows row0.. of the pair-ordered activations, halves 32j..32j+31 of
+                    // block j: one 64-byte-swizzled K-major box. The map is named with a
+                    // constant index so it stays in parameter space.
+                    for (int jj = 0; jj < nbl; jj++) {
+                        const int x = (ss * KB + jj) * 32;
+                        switch (sel) {
+                            case 0: tc::tma_load_2d(dst + jj * bblk, &bmaps.m[0], x, tl.it.row0, &bfull[bs]); break;
+                            default: tc::tma_load_2d(dst + jj * bblk, &bmaps.m[1], x, tl.it.row0, &bfull[bs]); break;
+                        }
+                    }
+                }
+                if (!ok) break;
+            }
+            if (g) tc::mbar_wait(&bfull[(g - 1) % RB], ((g - 1) / RB) & 1, abort_flag, err, 12);
+        }
+    } else if (warp == 15) {
+        if (lane == 0) {
+            // ---------------- bulk copies: the stage's activation block scales; TMA: the
+            // weight scales of every two stages (128 rows x 8 fp16) ----------------
+            uint32_t g = 0, gw = 0;
+            for (int t = blockIdx.x; t < T && !*abort_flag; t += gridDim.x) {
+                TcTile tl = tc_tile(a, t, MT);
+                bool ok = true;
+                for (int ss = 0; ss < nss; ss++, g++) {
+                    const int ds = g % ND;
+                    const uint32_t du = g / ND;
+                    if (HAS_DW && (ss & 1) == 0) {
+                        const int ws = gw % NW;
+                        const uint32_t wu = gw / NW;
+                        if (wu && !tc::mbar_wait(&wempty[ws], (wu - 1) & 1, abort_flag, err, 16)) { ok = false; break; }
+                        tc::mbar_arrive_tx(&wfull[ws], W_SLOT);
+                        tc::tma_load_3d(wring + ws * W_SLOT, &scale_map, ss * KB, tl.m0, tl.it.group, &wfull[ws]);
+                        gw++;
+                    }
+                    if (du && !tc::mbar_wait(&dempty[ds], (du - 1) & 1, abort_flag, err, 11)) { ok = false; break; }
+                    const int nbl = min(KB, nb - ss * KB);
+                    tc::mbar_arrive_tx(&dfull[ds], DX_BLK * nbl);
+                    for (int jj = 0; jj < nbl; jj++)
+                        tc::bulk_load(dxring + ds * DX_STAGE + jj * DX_BLK,
+                                      a.xsT + (size_t)(ss * KB + jj) * a.ldT + tl.it.row0, DX_BLK, &dfull[ds]);
+                }
+                if (!ok) break;
+            }
+            if (g) tc::mbar_wait(&dfull[(g - 1) % ND], ((g - 1) / ND) & 1, abort_flag, err, 13);
+            if (gw) tc::mbar_wait(&wfull[(gw - 1) % NW], ((gw - 1) / NW) & 1, abort_flag, err, 17);
         }
     } else if (warp >= 8 && warp < 12) {
         // ---------------- producers: widen weight codes to fp16 ----------------
         const int pt = tid - 256;  // weight row of the tile
-        uint32_t g = 0, slot_base = 0;
-        for (int t = blockIdx.x; t < T && !*abort_flag; t += gridDim.x) {
-            bool ok = true;
-            for (int j = 0; j < nb && ok; j++, g++) {
-                const int st = g % NS;
-                const uint32_t u = g / NS;
-                if (u && !tc::mbar_wait(&sempty[st], (u - 1) & 1, abort_flag, err, 14)) { ok = false; break; }
-                const int bb = blk_byte<FMT>(j);
-                const uint32_t sc = slot_base + bb / 64;
-                const int s = sc % RC;
-                const bool first = (bb % 64 == 0) && (FMT != GPU_FMT_TQ2 || (j & 1) == 0);
-                const bool last = ((bb + blk_span<FMT>()) % 64 == 0 && (FMT != GPU_FMT_TQ2 || (j & 1) == 1)) || j == nb - 1;
-                if (first && !tc::mbar_wait(&cfull[s], (sc / RC) & 1, abort_flag, err, 4)) { ok = false; break; }
-                uint4 w[4];
-                widen_row<FMT>(ring + s * SLOT + pt * 64 + bb % 64, j, w);
-                if (last) {
-                    // Release the slot to the TMA only once this thread's shared loads of it
-                    // have returned (consume their values) and are ordered before the async
-                    // proxy's refill: an arrive alone lets an L2-fast TMA overwrite the slot
-                    // under loads still in flight.
-                    asm volatile("" ::"r"(w[0].x), "r"(w[3].w) : "memory");
-                    tc::fence_proxy_async();
-                    tc::mbar_arrive(&cempty[s]);
-                }
-                uint8_t *sa = stages + st * A_BYTES + (pt >> 3) * 512 + (pt & 7) * 16;
+        // 16-byte chunk c of this row sits at chunk c ^ swz (the TMA swizzle of a CB-byte row)
+        const int swz = ((pt * CB) >> 7) & (NCH - 1);
+        const int my_tiles = T > (int)blockIdx.x ? (T - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
+        const uint32_t G = (uint32_t)my_tiles * nss;  // stages of all this CTA's tiles, in order
+        auto fetch = [&](uint32_t g, uint4 (&c)[NCH]) -> bool {
+            const int s = g % RC;
+            if (!tc::mbar_wait(&cfull[s], (g / RC) & 1, abort_flag, err, 4)) return false;
+            const uint8_t *row = ring + s * SLOTB + pt * CB;
 #pragma unroll
-                for (int k = 0; k < 4; k++) *reinterpret_cast<uint4 *>(sa + k * 128) = w[k];
-                tc::fence_proxy_async();
+            for (int k = 0; k < NCH; k++) c[k] = *reinterpret_cast<const uint4 *>(row + 16 * (k ^ swz));
+            return true;
+        };
+        uint4 c[NCH];
+        bool ok = G == 0 || fetch(0, c);
+        for (uint32_t g = 0; g < G && ok; g++) {
+            uint4 cn[NCH];
+            if (g + 1 < G && !fetch(g + 1, cn)) { ok = false; break; }  // next stage's codes in flight
+            const int st = g % NS;
+            if (g >= NS && !tc::mbar_wait(&sempty[st], ((g / NS) - 1) & 1, abort_flag, err, 14)) { ok = false; break; }
+            const int nbl = min(KB, nb - (int)(g % nss) * KB);
+            uint8_t *sa = stages + st * A_STAGE + (pt >> 3) * 512 + (pt & 7) * 16;
+            TC_PROF_T(p_w);
+#pragma unroll
+            for (int jj = 0; jj < KB; jj++) {
+                if (jj < nbl) {
+                    uint4 w[4];
+                    widen_blk<FMT>(c, jj, w);
+#pragma unroll
+                    for (int k = 0; k < 4; k++) *reinterpret_cast<uint4 *>(sa + jj * A_BLK + k * 128) = w[k];
+                }
+            }
+            // One proxy fence per thread orders both its shared stores of the stage (read
+            // next by the tensor cores) and its shared loads of the code slot (consumed by
+            // the widening above; refilled next by the TMA) before the async proxy; then one
+            // elected arrive per warp on each barrier. (An arrive alone would let an
+            // L2-fast TMA overwrite the slot under loads still in flight.)
+            tc::fence_proxy_async();
+            __syncwarp();
+            if (lane == 0) {
+                tc::mbar_arrive(&cempty[g % RC]);
                 tc::mbar_arrive(&sfull[st]);
             }
-            slot_base += nslots;
+            TC_PROF_ADD(43, p_w);
+#pragma unroll
+            for (int k = 0; k < NCH; k++) c[k] = cn[k];
         }
     } else if (warp == 13) {
         // ---------------- MMA issue ----------------
@@ -264,21 +316,26 @@ __global__ void __launch_bounds__(tcm::NTHREADS, 1)
                 TcTile tl = tc_tile(a, t, MT);
                 const int N = (tl.it.count + 15) & ~15;
                 const uint32_t idesc = tc::idesc_f16(128, N);
-                for (int j = 0; j < nb; j++, g++) {
-                    const int s = g % NS, bs = g % RB, ac = g % NACC;
-                    if (!tc::mbar_wait(&sfull[s], (g / NS) & 1, abort_flag, err, 5)) { ok = false; break; }
+                const uint32_t bblk = (16u << tc_sel(tl.it.count)) * 64u;
+                for (int ss = 0; ss < nss; ss++, g++) {
+                    const int st = g % NS, bs = g % RB, ac = g % NACC;
+                    if (!tc::mbar_wait(&sfull[st], (g / NS) & 1, abort_flag, err, 5)) { ok = false; break; }
                     if (!tc::mbar_wait(&bfull[bs], (g / RB) & 1, abort_flag, err, 15)) { ok = false; break; }
                     if (g >= NACC && !tc::mbar_wait(&tempty[ac], ((g / NACC) - 1) & 1, abort_flag, err, 6)) { ok = false; break; }
                     tc::tc_fence_after();
-                    const uint32_t sa = tc::smem_u32(stages + s * A_BYTES), sb = tc::smem_u32(bring + bs * B_BYTES);
-                    // A: core matrix (row group r, K chunk kc) at r*512 + kc*128, no swizzle
-                    // B: 8-row x 64-byte swizzle atoms, 512 bytes apart
-                    const uint64_t ad = tc::smem_desc(sa, 128, 512), bd = tc::smem_desc_sw64(sb, 512);
-                    const uint32_t td = tbase + ac * BN;
-                    tc::mma_f16_ss(td, ad, bd, idesc, 0u);                             // k 0-15 (overwrite)
-                    tc::mma_f16_ss(td, ad + (256 >> 4), bd + (32 >> 4), idesc, 1u);  // k 16-31
-                    tc::mma_commit(&sempty[s]);   // A stage free once these MMAs complete
-                    tc::mma_commit(&bempty[bs]);  // B slot likewise
+                    const int nbl = min(KB, nb - ss * KB);
+                    const uint32_t sa = tc::smem_u32(stages + st * A_STAGE), sb = tc::smem_u32(bring + bs * B_STAGE);
+                    for (int jj = 0; jj < nbl; jj++) {
+                        // A: core matrix (row group r, K chunk kc) at r*512 + kc*128, no swizzle
+                        // B: 8-row x 64-byte swizzle atoms, 512 bytes apart
+                        const uint64_t ad = tc::smem_desc(sa + jj * A_BLK, 128, 512);
+                        const uint64_t bd = tc::smem_desc_sw64(sb + jj * bblk, 512);
+                        const uint32_t td = tbase + (ac * KB + jj) * BN;
+                        tc::mma_f16_ss(td, ad, bd, idesc, 0u);                             // k 0-15 (overwrite)
+                        tc::mma_f16_ss(td, ad + (256 >> 4), bd + (32 >> 4), idesc, 1u);  // k 16-31
+                    }
+                    tc::mma_commit(&sempty[st]);  // A stage free once these MMAs complete
+                    tc::mma_commit(&bempty[bs]);  // B stage likewise
                     tc::mma_commit(&tfull[ac]);
                 }
             }
@@ -287,12 +344,11 @@ __global__ void __launch_bounds__(tcm::NTHREADS, 1)
     } else {
         // ---------------- epilogue (warps 0-7) ----------------
         const int q = warp & 3, h = warp >> 2;
-        const int m = q * 32 + lane;  // tile row = TMEM lane
-        uint32_t g = 0;
+        const uint32_t tl_lane = (uint32_t)(q * 32) << 16;
+        uint32_t g = 0, gw = 0;
         for (int t = blockIdx.x; t < T; t += gridDim.x) {
             TcTile tl = tc_tile(a, t, MT);
             const int ncols = tl.it.count;
-            const bool cv = h * 32 < ncols;  // this warp's 32 columns hold tokens
             // per-column info for the output phase
             for (int n = tid; n < BN; n += 256) {
                 int r = tl.it.row0 + (n < ncols ? n : 0);
@@ -311,63 +367,114 @@ __global__ void __launch_bounds__(tcm::NTHREADS, 1)
                 }
                 col_sx[n] = tot;
             }
-            const __half *dwrow = nullptr;
-            if (FMT != GPU_FMT_TQ2)
-                dwrow = reinterpret_cast<const __half *>(reinterpret_cast<const uint8_t *>(a.scale) +
-                                                         (long)tl.it.group * a.scale_gstride) +
-                        (size_t)(tl.m0 + m) * nbp;
-            float2 acc[16];
+            // Thread layout of the results (the 16x256b TMEM access shape): rows
+            // q*32 + r0 + 8k (k = 0..3) and columns cp + 8i + {0,1} (i = 0..3), so each
+            // thread needs 8 activation scales per block instead of 32.
+            const int r0 = lane >> 2, cp = (lane & 3) * 2;
+            float2 acc[16];  // [k][i]
 #pragma unroll
             for (int i = 0; i < 16; i++) acc[i] = make_float2(0.f, 0.f);
-            const uint32_t tl_lane = (uint32_t)(q * 32) << 16;
-            // Software pipeline over the K blocks: the TMEM load of block j+1 is in flight
-            // while block j is scaled into the accumulators (two register buffers).
-            uint32_t va_[32], vb_[32];
-            auto fetch = [&](uint32_t gg, uint32_t (&v)[32]) -> bool {
-                bool ok = tc::mbar_wait(&tfull[gg % NACC], (gg / NACC) & 1, abort_flag, err, 8);
-                ok = ok && tc::mbar_wait(&dfull[gg % NDX], (gg / NDX) & 1, abort_flag, err, 9);
-                ok = __all_sync(0xffffffffu, ok);  // tcgen05.ld is warp-collective
-                tc::tc_fence_after();
-                if (ok && cv) tc::tmem_ld32(tbase + tl_lane + (gg % NACC) * BN + h * 32, v);
-                return ok;
-            };
-            float dw_next = (FMT != GPU_FMT_TQ2) ? __half2float(dwrow[0]) : 1.f;
-            bool okc = fetch(g, va_);
-            // one K block: results of block j are in `cur`; block j+1 is fetched into `nxt`
-            auto step = [&](int j, uint32_t (&cur)[32], uint32_t (&nxt)[32]) {
-                const int ac = g % NACC, ds = g % NDX;
-                const float dw = dw_next;
-                if (FMT != GPU_FMT_TQ2 && j + 1 < nb) dw_next = __half2float(dwrow[j + 1]);
-                if (okc && cv) tc::tmem_ld_wait();
-                tc::tc_fence_before();
-                __syncwarp();
-                if (lane == 0) tc::mbar_arrive(&tempty[ac]);  // accumulator j is in registers
-                bool okn = true;
-                if (j + 1 < nb) okn = fetch(g + 1, nxt);
-                if (okc && cv) {
-                    const float *dx = reinterpret_cast<const float *>(dxring + ds * DX_BYTES) + h * 32;
-                    const float2 dw2 = make_float2(dw, dw);
+            // one block's results (lo: rows r0, r0+8; hi: rows r0+16, r0+24) scaled into acc
+            auto scale_blk = [&](const uint32_t (&lo)[16], const uint32_t (&hi)[16], const float *dx, const uint2 (&dwr)[4],
+                                 int jj) {
+                float dwk[4];
 #pragma unroll
-                    for (int i = 0; i < 8; i++) {
-                        float4 d4 = *reinterpret_cast<const float4 *>(dx + 4 * i);
-                        float2 x0 = make_float2(__uint_as_float(cur[4 * i]), __uint_as_float(cur[4 * i + 1]));
-                        float2 x1 = make_float2(__uint_as_float(cur[4 * i + 2]), __uint_as_float(cur[4 * i + 3]));
-                        float2 da = make_float2(d4.x, d4.y), db = make_float2(d4.z, d4.w);
-                        if (FMT != GPU_FMT_TQ2) { da = fmul2(dw2, da); db = fmul2(dw2, db); }
-                        acc[2 * i] = ffma2(da, x0, acc[2 * i]);
-                        acc[2 * i + 1] = ffma2(db, x1, acc[2 * i + 1]);
+                for (int k = 0; k < 4; k++) {
+                    const uint32_t w = (jj < 2) ? dwr[k].x : dwr[k].y;
+                    const __half2 hw = *reinterpret_cast<const __half2 *>(&w);
+                    dwk[k] = HAS_DW ? ((jj & 1) ? __high2float(hw) : __low2float(hw)) : 1.f;
+                }
+#pragma unroll
+                for (int i = 0; i < 4; i++) {
+                    const float2 d = *reinterpret_cast<const float2 *>(dx + 8 * i + cp);
+#pragma unroll
+                    for (int k = 0; k < 4; k++) {
+                        const uint32_t *v = k < 2 ? lo : hi;
+                        const int b = 4 * i + 2 * (k & 1);
+                        const float2 x = make_float2(__uint_as_float(v[b]), __uint_as_float(v[b + 1]));
+                        const float2 sc = HAS_DW ? fmul2(make_float2(dwk[k], dwk[k]), d) : d;
+                        acc[4 * k + i] = ffma2(sc, x, acc[4 * k + i]);
                     }
                 }
-                __syncwarp();
-                if (lane == 0) tc::mbar_arrive(&dempty[ds]);
-                okc = okn;
-                g++;
             };
 #pragma unroll 1
-            for (int j = 0; j < nb; j += 2) {
-                step(j, va_, vb_);
-                if (j + 1 < nb) step(j + 1, vb_, va_);
+            for (int ss = 0; ss < nss; ss++, g++) {
+                const int ac = g % NACC, ds = g % ND, ws = gw % NW;
+                const int nbl = min(KB, nb - ss * KB);
+                uint2 dwr[4] = {};
+                if (HAS_DW) {
+                    // (a wait that gives up sets the abort flag; the stage's other waits
+                    // then fail too and no result is formed from these values)
+                    if ((ss & 1) == 0) tc::mbar_wait(&wfull[ws], (gw / NW) & 1, abort_flag, err, 18);
+                    // the 4 fp16 weight scales of the stage for each of this thread's rows
+#pragma unroll
+                    for (int k = 0; k < 4; k++)
+                        dwr[k] = *reinterpret_cast<const uint2 *>(wring + ws * W_SLOT + (q * 32 + r0 + 8 * k) * 16 +
+                                                                  (ss & 1) * 8);
+                    if ((ss & 1) == 1 || ss == nss - 1) {
+                        // values consumed, then ordered before the TMA's refill of the slot
+                        asm volatile("" ::"r"(dwr[0].x), "r"(dwr[1].x), "r"(dwr[2].x), "r"(dwr[3].x), "r"(dwr[0].y),
+                                     "r"(dwr[1].y), "r"(dwr[2].y), "r"(dwr[3].y)
+                                     : "memory");
+                        tc::fence_proxy_async();
+                        __syncwarp();
+                        if (lane == 0) tc::mbar_arrive(&wempty[ws]);
+                        gw++;
+                    }
+                }
+                bool ok = tc::mbar_wait(&tfull[ac], (g / NACC) & 1, abort_flag, err, 8);
+                ok = tc::mbar_wait(&dfull[ds], (g / ND) & 1, abort_flag, err, 9) && ok;
+                ok = __all_sync(0xffffffffu, ok);  // tcgen05.ld is warp-collective
+                // the two warp groups take alternate K stages (group h the stages in odd /
+                // even TMEM slots); their partial sums meet in shared memory at the tile
+                // end, in the same order for every tile
+                const bool work = ok && (ac & 1) == h;
+                tc::tc_fence_after();
+                const uint32_t tb = tbase + tl_lane + (uint32_t)(ac * KB * BN);
+                const float *dx = reinterpret_cast<const float *>(dxring + ds * DX_STAGE);
+                uint32_t va[16], vb[16], vc[16], vd[16];
+                // blocks 0 and 1 of the stage
+                TC_PROF_T(p_ld);
+                if (work) {
+                    tc::tmem_ld16x256_x4(tb, va);
+                    tc::tmem_ld16x256_x4(tb + (16u << 16), vb);
+                    if (nbl > 1) {
+                        tc::tmem_ld16x256_x4(tb + BN, vc);
+                        tc::tmem_ld16x256_x4(tb + BN + (16u << 16), vd);
+                    }
+                    tc::tmem_ld_wait();
+                }
+                TC_PROF_ADD(40, p_ld);
+                if (nbl <= 2 || !work) {
+                    tc::tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) tc::mbar_arrive(&tempty[ac]);  // the stage's accumulators are read
+                }
+                TC_PROF_T(p_sc);
+                if (work) {
+                    scale_blk(va, vb, dx, dwr, 0);
+                    if (nbl > 1) scale_blk(vc, vd, dx + BN, dwr, 1);
+                    // blocks 2 and 3
+                    if (nbl > 2) {
+                        tc::tmem_ld16x256_x4(tb + 2 * BN, va);
+                        tc::tmem_ld16x256_x4(tb + 2 * BN + (16u << 16), vb);
+                        if (nbl > 3) {
+                            tc::tmem_ld16x256_x4(tb + 3 * BN, vc);
+                            tc::tmem_ld16x256_x4(tb + 3 * BN + (16u << 16), vd);
+                        }
+                        tc::tmem_ld_wait();
+                        tc::tc_fence_before();
+                        __syncwarp();
+                        if (lane == 0) tc::mbar_arrive(&tempty[ac]);
+                        scale_blk(va, vb, dx + 2 * BN, dwr, 2);
+                        if (nbl > 3) scale_blk(vc, vd, dx + 3 * BN, dwr, 3);
+                    }
+                }
+                TC_PROF_ADD(41, p_sc);
+                __syncwarp();
+                if (lane == 0) tc::mbar_arrive(&dempty[ds]);
             }
+            TC_PROF_T(p_out);
             // ---- tile output: 128 x ncols fp32 through shared memory ----
             const float *alpha = FMT == GPU_FMT_TQ2 ? reinterpret_cast<const float *>(
                                                           reinterpret_cast<const uint8_t *>(a.scale) +
@@ -376,8 +483,25 @@ __global__ void __launch_bounds__(tcm::NTHREADS, 1)
             const int m0 = tl.m0;
             {
                 const int c0n = 0, nc = ncols;
+                if (h == 1) {
 #pragma unroll
-                for (int i = 0; i < 16; i++) *reinterpret_cast<float2 *>(ct + m * CS + h * 32 + 2 * i) = acc[i];
+                    for (int k = 0; k < 4; k++)
+#pragma unroll
+                        for (int i = 0; i < 4; i++)
+                            *reinterpret_cast<float2 *>(ct + (q * 32 + r0 + 8 * k) * CS + 8 * i + cp) = acc[4 * k + i];
+                }
+                // group 0 adds its stages' partial sums to group 1's
+                tc::named_sync(1, 256);
+                if (h == 0) {
+#pragma unroll
+                    for (int k = 0; k < 4; k++)
+#pragma unroll
+                        for (int i = 0; i < 4; i++) {
+                            float2 *p = reinterpret_cast<float2 *>(ct + (q * 32 + r0 + 8 * k) * CS + 8 * i + cp);
+                            const float2 o = *p;
+                            *p = make_float2(o.x + acc[4 * k + i].x, o.y + acc[4 * k + i].y);
+                        }
+                }
                 tc::named_sync(1, 256);
                 if (!*abort_flag) {
                     if (EPI == EPI_GATEUP) {
@@ -429,16 +553,20 @@ __global__ void __launch_bounds__(tcm::NTHREADS, 1)
                 }
                 tc::named_sync(1, 256);
             }
+            TC_PROF_ADD(42, p_out);
         }
     }
 #ifdef ZZ_TC_PROF
-    if (blockIdx.x == 0 && (tid & 31) == 0) atomicAdd(&tc::g_tc_prof[20 + (warp < 8 ? 0 : warp < 12 ? 1 : warp - 10)], (unsigned long long)clock64());
+    // per-role busy span: 32 epilogue, 33 producers, 34 code TMA, 35 MMA, 36 B TMA, 37 dx copies
+    if (blockIdx.x == 0 && (tid & 31) == 0)
+        atomicAdd(&tc::g_tc_prof[32 + (warp < 8 ? 0 : warp < 12 ? 1 : warp - 10)],
+                  (unsigned long long)(clock64() - prof_t0));
 #endif
     tc::tc_fence_before();
     __syncthreads();
     if (warp == 13) {
         tc::tc_fence_after();
-        tc::tmem_dealloc(tbase, NACC * tcm::BN);
+        tc::tmem_dealloc(tbase, NACC * KB * BN);
     }
 }
 
@@ -456,18 +584,39 @@ static int get_encode() {
     return 1;
 }
 
-// codes plane of a whole bank: rows = experts * O, row = row_bytes bytes
-static int make_codes_map(CUtensorMap *map, const uint8_t *codes, long rows, int row_bytes) {
+// codes plane of a whole bank: rows = experts * O, row = row_bytes bytes; one box is
+// 128 rows x cb bytes (one K stage), swizzled by its width so that the producers'
+// 16-byte loads of one row each hit distinct banks
+static int make_codes_map(CUtensorMap *map, const uint8_t *codes, long rows, int row_bytes, int cb) {
     if (!get_encode()) return 0;
     if ((uintptr_t)codes & 15 || row_bytes % 16) return fail("tc: codes plane not 16-byte aligned");
     cuuint64_t dims[2] = {(cuuint64_t)row_bytes, (cuuint64_t)rows};
     cuuint64_t strides[1] = {(cuuint64_t)row_bytes};
-    cuuint32_t box[2] = {64, 128};
+    cuuint32_t box[2] = {(cuuint32_t)cb, 128};
+    const CUtensorMapSwizzle sw = cb == 128  ? CU_TENSOR_MAP_SWIZZLE_128B
+                                  : cb == 64 ? CU_TENSOR_MAP_SWIZZLE_64B
+                                             : CU_TENSOR_MAP_SWIZZLE_32B;
     cuuint32_t estr[2] = {1, 1};
     CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<uint8_t *>(codes), dims, strides, box, estr,
-                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                          CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) return fail("tc: cuTensorMapEncodeTiled failed (%d)", (int)r);
+    return 1;
+}
+
+// fp16 weight-scale planes of a bank: [experts][O][nbp] (rows padded to 8 blocks), each
+// expert `gstride` bytes apart; one box is 128 rows x 8 scales (two K stages)
+static int make_scale_map(CUtensorMap *map, const void *scale, int E, int O, int nbp, long gstride) {
+    if (!get_encode()) return 0;
+    if ((uintptr_t)scale & 15 || gstride % 16 || nbp % 8) return fail("tc: scale planes not 16-byte aligned");
+    cuuint64_t dims[3] = {(cuuint64_t)nbp, (cuuint64_t)O, (cuuint64_t)E};
+    cuuint64_t strides[2] = {(cuuint64_t)nbp * 2, (cuuint64_t)gstride};
+    cuuint32_t box[3] = {8, 128, 1};
+    cuuint32_t estr[3] = {1, 1, 1};
+    CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void *>(scale), dims, strides, box, estr,
+                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail("tc: scale tensor map failed (%d)", (int)r);
     return 1;
 }
 
@@ -497,16 +646,20 @@ static int launch_tc_t(const GemmArgs &a, int n_groups, int *err, cudaStream_t s
         attr = true;
     }
     const int row_bytes = FMT == GPU_FMT_Q40 ? a.I / 2 : FMT == GPU_FMT_Q80 ? a.I : a.I / 4;
-    CUtensorMap map;
+    CUtensorMap map, smap;
     BMaps bmaps;
-    if (!make_codes_map(&map, a.codes, (long)n_groups * a.O, row_bytes)) return 0;
-    for (int i = 0; i < 3; i++)
+    if (!make_codes_map(&map, a.codes, (long)n_groups * a.O, row_bytes, tc_cb<FMT>())) return 0;
+    if (FMT == GPU_FMT_TQ2)
+        smap = map;  // tq2 has one fp32 alpha per row, applied at the tile end
+    else if (!make_scale_map(&smap, a.scale, n_groups, a.O, ((a.I / ZZ_BLK) + 7) & ~7, a.scale_gstride))
+        return 0;
+    for (int i = 0; i < 2; i++)
         if (!make_b_map(&bmaps.m[i], a.xg, a.rows_cap, a.I, 16 << i)) return 0;
     int dev = 0, sms = 148;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     if (const char *e = getenv("ZZ_TC_GRID")) sms = atoi(e) > 0 ? atoi(e) : sms;
-    k_moe_tc<FMT, EPI><<<sms, tcm::NTHREADS, tcm::SMEM, st>>>(a, map, bmaps, err);
+    k_moe_tc<FMT, EPI><<<sms, tcm::NTHREADS, tcm::SMEM, st>>>(a, map, smap, bmaps, err);
     return check_cuda(cudaGetLastError(), "tc launch");
 }
 
@@ -529,8 +682,8 @@ int launch_moe_tc(int fmt, int epi, const GemmArgs &a, int n_groups, int *err, c
 #ifdef ZZ_TC_PROF
 extern "C" int zz_tc_prof_read(unsigned long long *out) {
     cudaDeviceSynchronize();
-    cudaMemcpyFromSymbol(out, zz::tc::g_tc_prof, sizeof(unsigned long long) * 32);
-    unsigned long long z[32] = {0};
+    cudaMemcpyFromSymbol(out, zz::tc::g_tc_prof, sizeof(unsigned long long) * 128);
+    unsigned long long z[128] = {0};
     cudaMemcpyToSymbol(zz::tc::g_tc_prof, z, sizeof z);
     return 1;
 }

@@ -1,7 +1,7 @@
 // zz_tc.cuh -- Blackwell (sm_100a) primitives: mbarriers with bounded waits, TMA
 // tile loads, TMEM allocation, tcgen05 MMA / commit / load. Hand-written inline PTX.
 //
-// Every wait here has an iteration limit. A wait that runs out sets the CTA's abort
+// Every wait here has a time limit (2 s of %globaltimer). A wait that runs out sets the CTA's abort
 // flag and the kernel's error word and returns false; the caller then stops issuing
 // work, drains what it can with the same bounded waits, frees its TMEM and returns,
 // so the context stays usable and the host sees the error.
@@ -12,7 +12,8 @@
 namespace zz {
 namespace tc {
 
-constexpr uint32_t WAIT_LIMIT = 1u << 22;  // try_wait iterations (each may suspend briefly)
+constexpr unsigned long long WAIT_LIMIT_NS = 2000000000ull;  // a wait gives up after 2 s
+constexpr uint32_t SUSPEND_NS = 20000;                        // suspend-time hint of one try
 
 __device__ __forceinline__ uint32_t smem_u32(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
 
@@ -38,22 +39,58 @@ __device__ __forceinline__ bool mbar_try(uint64_t *bar, uint32_t parity) {
     return ok != 0;
 }
 #ifdef ZZ_TC_PROF
-__device__ unsigned long long g_tc_prof[32];
+// diagnostic build only: cycles spent in each wait site, summed over block 0's warps
+__device__ unsigned long long g_tc_prof[128];
 #endif
+#ifdef ZZ_TC_PROF
+#define TC_PROF_T(v) const long long v = clock64()
+#define TC_PROF_ADD(code, t0)                                                                        \
+    do {                                                                                             \
+        if (blockIdx.x == 0 && (threadIdx.x & 31) == 0)                                              \
+            atomicAdd(&::zz::tc::g_tc_prof[code], (unsigned long long)(clock64() - (t0)));           \
+    } while (0)
+#else
+#define TC_PROF_T(v)
+#define TC_PROF_ADD(code, t0)
+#endif
+// as mbar_try, but the thread may be suspended (up to `ns`) until the phase completes,
+// so a waiting role does not take issue slots from the warps doing the work
+__device__ __forceinline__ bool mbar_try_suspend(uint64_t *bar, uint32_t parity, uint32_t ns) {
+    uint32_t ok;
+    asm volatile(
+        "{.reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3; selp.u32 %0, 1, 0, p;}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity), "r"(ns)
+        : "memory");
+    return ok != 0;
+}
+__device__ __forceinline__ unsigned long long global_ns() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
 // bounded wait for the phase with the given parity to complete
 __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, volatile int *abort, int *err, int code) {
 #ifdef ZZ_TC_PROF
-    long long t0 = clock64();
+    const long long t0 = clock64();
     struct Acc {
-        long long t0; int code;
+        long long t0;
+        int code;
         __device__ ~Acc() {
-            if (blockIdx.x == 0 && (threadIdx.x & 31) == 0) atomicAdd(&g_tc_prof[code], (unsigned long long)(clock64() - t0));
+            if (blockIdx.x == 0 && (threadIdx.x & 31) == 0)
+                atomicAdd(&g_tc_prof[code], (unsigned long long)(clock64() - t0));
         }
     } acc_{t0, code};
 #endif
-    for (uint32_t i = 0; i < WAIT_LIMIT; i++) {
-        if (mbar_try(bar, parity)) return true;
-        if ((i & 255u) == 255u && *abort) return false;
+    if (mbar_try(bar, parity)) return true;
+    const unsigned long long w0 = global_ns();
+    for (;;) {
+#ifdef ZZ_TC_PROF
+        if (blockIdx.x == 0 && (threadIdx.x & 31) == 0) atomicAdd(&g_tc_prof[64 + code], 1ull);
+#endif
+        if (mbar_try_suspend(bar, parity, SUSPEND_NS)) return true;
+        if (*abort) return false;
+        if (global_ns() - w0 > WAIT_LIMIT_NS) break;
     }
     *abort = 1;
     atomicCAS(err, 0, code);
@@ -148,6 +185,15 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
           "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
           "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
           "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr));
+}
+// 16 lanes x 4 x 256 bits: thread t gets, for i = 0..3, lane (t/4) columns 8i + 2(t%4) + {0,1}
+// in r[4i], r[4i+1] and lane (t/4)+8 the same columns in r[4i+2], r[4i+3]
+__device__ __forceinline__ void tmem_ld16x256_x4(uint32_t taddr, uint32_t (&r)[16]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.16x256b.x4.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
         : "r"(taddr));
 }
 __device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
