@@ -116,6 +116,27 @@ def test_matvec_many_rows(orc, fmt, S, O, I):
         assert rel(y[s], oracle_matvec(orc, fmt, Wb, O, I, xq[s], sx[s], tot[s])) < TOL, s
 
 
+@pytest.mark.parametrize("fmt,reps", [(zz.GPU_FMT_Q40, 12), (zz.GPU_FMT_Q80, 12), (zz.GPU_FMT_TQ2, 24)])
+def test_matvec_streamed(orc, fmt, reps):
+    """Matrices of >= 64 MB take the bulk-copy streamed kernel: 4099 distinct rows tiled
+    `reps` times (O not a multiple of the 16-row tile), every row against the oracle."""
+    O0, I = 4099, 2816
+    W0 = q_weights(orc, fmt, 40, O0, I)
+    O = O0 * reps
+    if fmt == zz.GPU_FMT_TQ2:  # alpha[O] then codes[O][I/4]
+        al, cd = W0[:4 * O0].view(np.float32), W0[4 * O0:].reshape(O0, I // 4)
+        Wb = np.concatenate([np.tile(al, reps).view(np.uint8), np.tile(cd, (reps, 1)).reshape(-1)])
+    else:
+        Wb = np.tile(W0.reshape(O0, -1), (reps, 1)).reshape(-1)
+    assert zz.lib.zz_qtensor_bytes(fmt, O, I) >= 64 << 20
+    x = synth.gaussian(41, (1, I))
+    xq, sx, tot = orc.tq2_quant_act(x)
+    t = zz.QTensorDev(fmt, dev(Wb), O, I)
+    y = zz.matvec(t, dev(xq), dev(sx), dev(tot)).cpu().numpy()[0]
+    want = oracle_matvec(orc, fmt, W0, O0, I, xq[0], sx[0], tot[0])
+    assert rel(y, np.tile(want, reps)) < TOL
+
+
 def test_gpu_h_surface(orc):
     """gpu_init / gpu_map / gpu_matmul exactly as an engine calls them (gemma4.c:445)."""
     L = zz.lib

@@ -7,7 +7,9 @@
 // is loaded into registers once and reused for all rows the warp visits. Weight codes
 // stream with 16-byte L1-bypassing loads (a warp reads 512 contiguous bytes per step);
 // two rows are in flight per warp to cover HBM latency.
+#include <cstdlib>
 #include "zz_dot.cuh"
+#include "zz_tc.cuh"
 
 namespace zz {
 
@@ -147,6 +149,174 @@ __global__ void __launch_bounds__(256) k_gemv_tq2(const uint8_t *__restrict__ co
     }
 }
 
+// ---------------------------------------------------------------- streamed matvec
+// For matrices well beyond L2 (stacked layers, lm_head): a persistent grid in which one
+// producer thread per CTA streams whole tiles of R consecutive rows -- the rows' code
+// bytes and fp16 scale rows are each one contiguous range of their plane -- into a
+// 4-stage shared-memory ring with cp.async.bulk, so ~100 KB per CTA is in flight
+// regardless of registers; 8 consumer warps compute from shared memory with the same
+// per-lane block split, dot products and reduction order as k_gemv_q (identical y).
+namespace gs {
+constexpr int NST = 4, WARPS = 8, THREADS = (WARPS + 1) * 32;
+}
+__device__ int g_gemv_err;
+
+__host__ __device__ inline int gs_align(int x) { return (x + 127) & ~127; }
+
+template <int FMT, int NBL>
+__global__ void __launch_bounds__(gs::THREADS) k_gemv_stream(const uint8_t *__restrict__ codes, const void *__restrict__ scale,
+                                                             int O, int I, int R, const int8_t *__restrict__ xq,
+                                                             const float *__restrict__ sx, const float *__restrict__ sxtot,
+                                                             float *__restrict__ y) {
+    using namespace gs;
+    extern __shared__ __align__(128) uint8_t smem[];
+    constexpr bool TQ2 = FMT == GPU_FMT_TQ2;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int nb = I / ZZ_BLK, nbp = (nb + 7) & ~7;
+    const int rowb = TQ2 ? I / 4 : FMT == GPU_FMT_Q40 ? I / 2 : I;
+    const int srow = TQ2 ? 0 : nbp * 2;  // scale bytes per row (tq2: alpha read directly)
+    const int cbytes = gs_align(R * rowb), stage = cbytes + gs_align(R * srow);
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem + NST * stage), *empty = full + NST;
+    volatile int *abort_flag = reinterpret_cast<volatile int *>(empty + NST);
+    const int ntiles = (O + R - 1) / R;
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < NST; i++) { tc::mbar_init(&full[i], 1); tc::mbar_init(&empty[i], WARPS); }
+        *abort_flag = 0;
+        tc::mbar_init_fence();
+    }
+    __syncthreads();
+    if (warp == WARPS) {
+        // ---------------- producer ----------------
+        if (lane == 0) {
+            uint32_t i = 0;
+            for (int t = blockIdx.x; t < ntiles; t += gridDim.x, i++) {
+                const int s = i % NST;
+                if (i >= NST && !tc::mbar_wait(&empty[s], ((i / NST) - 1) & 1, abort_flag, &g_gemv_err, 1)) break;
+                const int rows = min(R, O - t * R);
+                tc::mbar_arrive_tx(&full[s], (uint32_t)(rows * rowb + rows * srow));
+                tc::bulk_load(smem + s * stage, codes + (size_t)t * R * rowb, (uint32_t)(rows * rowb), &full[s]);
+                if (!TQ2)
+                    tc::bulk_load(smem + s * stage + cbytes, reinterpret_cast<const uint8_t *>(scale) + (size_t)t * R * srow,
+                                  (uint32_t)(rows * srow), &full[s]);
+            }
+            if (i) tc::mbar_wait(&full[(i - 1) % NST], ((i - 1) / NST) & 1, abort_flag, &g_gemv_err, 2);
+        }
+        return;
+    }
+    // ---------------- consumers ----------------
+    constexpr int XW = TQ2 ? 16 : 8;  // activation words per unit (tq2: 64-weight group)
+    uint32_t xr[NBL][XW];
+    float xs0[NBL], xs1[NBL];
+    const int nu = TQ2 ? I / 64 : nb;  // units per row
+#pragma unroll
+    for (int i = 0; i < NBL; i++) {
+        int u = lane + 32 * i;
+        if (u < nu) {
+            const uint4 *p = reinterpret_cast<const uint4 *>(xq + (size_t)u * XW * 4);
+#pragma unroll
+            for (int k = 0; k < XW / 4; k++) {
+                uint4 v = p[k];
+                xr[i][4 * k] = v.x; xr[i][4 * k + 1] = v.y; xr[i][4 * k + 2] = v.z; xr[i][4 * k + 3] = v.w;
+            }
+            xs0[i] = TQ2 ? sx[2 * u] : sx[u];
+            xs1[i] = TQ2 ? sx[2 * u + 1] : 0.f;
+        } else {
+#pragma unroll
+            for (int k = 0; k < XW; k++) xr[i][k] = 0;
+            xs0[i] = xs1[i] = 0.f;
+        }
+    }
+    const float tot = TQ2 ? sxtot[0] : 0.f;
+    uint32_t i = 0;
+    for (int t = blockIdx.x; t < ntiles; t += gridDim.x, i++) {
+        const int s = i % NST;
+        const bool ok = tc::mbar_wait(&full[s], (i / NST) & 1, abort_flag, &g_gemv_err, 3);
+        const int rows = min(R, O - t * R);
+        const uint8_t *sc = smem + s * stage;
+        const __half *ss = reinterpret_cast<const __half *>(sc + cbytes);
+        for (int r = warp; ok && r < rows; r += WARPS) {
+            const uint8_t *crow = sc + (size_t)r * rowb;
+            float acc = 0.f;
+#pragma unroll
+            for (int j = 0; j < NBL; j++) {
+                int u = lane + 32 * j;
+                if (u < nu) {
+                    if (FMT == GPU_FMT_Q40) {
+                        const uint4 w = *reinterpret_cast<const uint4 *>(crow + u * 16);
+                        acc = fmaf(__half2float(ss[r * nbp + u]) * xs0[j], (float)q40_block_dot(w, xr[j]), acc);
+                    } else if (FMT == GPU_FMT_Q80) {
+                        const uint4 w0 = *reinterpret_cast<const uint4 *>(crow + u * 32);
+                        const uint4 w1 = *reinterpret_cast<const uint4 *>(crow + u * 32 + 16);
+                        acc = fmaf(__half2float(ss[r * nbp + u]) * xs0[j], (float)q80_block_dot(w0, w1, xr[j]), acc);
+                    } else {
+                        int s0, s1;
+                        tq2_group_dot(*reinterpret_cast<const uint4 *>(crow + u * 16), xr[j], s0, s1);
+                        acc = fmaf(xs0[j], (float)s0, acc);
+                        acc = fmaf(xs1[j], (float)s1, acc);
+                    }
+                }
+            }
+            acc = warp_sum(acc);
+            if (lane == 0) {
+                const int o = t * R + r;
+                y[o] = TQ2 ? reinterpret_cast<const float *>(scale)[o] * (acc - tot) : acc;
+            }
+        }
+        __syncwarp();
+        if (lane == 0) tc::mbar_arrive(&empty[s]);
+    }
+}
+
+// rows per streamed tile: 16, fewer for long rows (a stage stays <= 32 KB)
+static int gs_rows(int rowb, int srow) {
+    int R = 16;
+    while (R > 1 && R * (rowb + srow) > 32 * 1024) R >>= 1;
+    return R;
+}
+
+// streamed matvec; returns 0 if the shape has no instantiation
+static int launch_gemv_stream(const zz_qtensor *W, const int8_t *xq, const float *sx, const float *sxtot, float *y,
+                              cudaStream_t st) {
+    const int O = W->O, I = W->I, nb = I / ZZ_BLK, nbp = (nb + 7) & ~7;
+    const bool tq2 = W->fmt == GPU_FMT_TQ2;
+    const int rowb = tq2 ? I / 4 : W->fmt == GPU_FMT_Q40 ? I / 2 : I, srow = tq2 ? 0 : nbp * 2;
+    if (rowb % 16 || ((uintptr_t)W->codes & 15) || (!tq2 && ((uintptr_t)W->scale & 15))) return 0;
+    const int R = gs_rows(rowb, srow);
+    const int stage = gs_align(R * rowb) + gs_align(R * srow);
+    const int smem = gs::NST * stage + 2 * gs::NST * 8 + 16;
+    int dev = 0, sms = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const int ntiles = (O + R - 1) / R;
+    const int per_sm = smem <= 110 * 1024 ? 2 : 1;
+    const int grid = ntiles < per_sm * sms ? ntiles : per_sm * sms;
+    const int nu = tq2 ? I / 64 : nb, nbl = (nu + 31) / 32;
+#define ZZ_GS(F, N)                                                                                           \
+    case N: {                                                                                                  \
+        static bool attr = false;                                                                              \
+        if (!attr) {                                                                                           \
+            cudaFuncSetAttribute(k_gemv_stream<F, N>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024); \
+            attr = true;                                                                                       \
+        }                                                                                                      \
+        k_gemv_stream<F, N><<<grid, gs::THREADS, smem, st>>>(W->codes, W->scale, O, I, R, xq, sx, sxtot, y);    \
+        break;                                                                                                 \
+    }
+    if (W->fmt == GPU_FMT_Q40) {
+        switch (nbl) { ZZ_GS(GPU_FMT_Q40, 1) ZZ_GS(GPU_FMT_Q40, 2) ZZ_GS(GPU_FMT_Q40, 3) ZZ_GS(GPU_FMT_Q40, 4)
+                       ZZ_GS(GPU_FMT_Q40, 5) ZZ_GS(GPU_FMT_Q40, 6) ZZ_GS(GPU_FMT_Q40, 7) ZZ_GS(GPU_FMT_Q40, 8)
+                       default: return 0; }
+    } else if (W->fmt == GPU_FMT_Q80) {
+        switch (nbl) { ZZ_GS(GPU_FMT_Q80, 1) ZZ_GS(GPU_FMT_Q80, 2) ZZ_GS(GPU_FMT_Q80, 3) ZZ_GS(GPU_FMT_Q80, 4)
+                       ZZ_GS(GPU_FMT_Q80, 5) ZZ_GS(GPU_FMT_Q80, 6) ZZ_GS(GPU_FMT_Q80, 7) ZZ_GS(GPU_FMT_Q80, 8)
+                       default: return 0; }
+    } else {
+        switch (nbl) { ZZ_GS(GPU_FMT_TQ2, 1) ZZ_GS(GPU_FMT_TQ2, 2) ZZ_GS(GPU_FMT_TQ2, 3) ZZ_GS(GPU_FMT_TQ2, 4)
+                       default: return 0; }
+    }
+#undef ZZ_GS
+    return check_cuda(cudaGetLastError(), "gemv stream launch") ? 1 : -1;
+}
+
 // per-block integer sums, one thread per (row, block): the bit-exact parity quantity
 template <int FMT>
 __global__ void k_blocksums(const uint8_t *__restrict__ codes, int O, int I, const int8_t *__restrict__ xq,
@@ -182,6 +352,15 @@ static int gemv_grid(int O) {
 int launch_gemv1(const zz_qtensor *W, const int8_t *xq, const float *sx, const float *sxtot, float *y,
                  cudaStream_t st) {
     const int O = W->O, I = W->I, grid = gemv_grid(O);
+    // matrices that stream from HBM (well beyond L2) take the bulk-copy kernel; small
+    // ones (latency-bound) the register kernel. ZZ_GEMV=stream|reg overrides.
+    static const char *mode = getenv("ZZ_GEMV");
+    const size_t bytes = zz_qtensor_bytes(W->fmt, O, I);
+    const bool stream = mode ? mode[0] == 's' : bytes >= ((size_t)64 << 20);
+    if (stream) {
+        int r = launch_gemv_stream(W, xq, sx, sxtot, y, st);
+        if (r) return r;
+    }
     if (W->fmt == GPU_FMT_TQ2) {
         int ngl = (I / 64 + 31) / 32;
         switch (ngl) {
