@@ -126,7 +126,8 @@ def check_pairs(orc, kind, blobs, X, eidx, ewt, out_gpu, bank, pairs=None):
 @pytest.fixture(params=["auto", "mma", "mma8", "tc", "dec"])
 def engine(request, monkeypatch):
     """every expert engine: auto (GEMV for small S*K, else mma.sync), mma.sync, tcgen05,
-    and the small-batch GEMV kernels forced (ZZ_MOE_KERNEL)"""
+    and the small-batch GEMV kernels forced (ZZ_MOE_KERNEL; calls of more than 64 pairs
+    take the int8 mma.sync engine there)"""
     monkeypatch.setenv("ZZ_MOE_KERNEL", request.param)
     return request.param
 

@@ -93,6 +93,7 @@ struct GemmArgs {
     float *hsT;              // gate/up: transposed hidden scales [O/64][ldT]
 };
 
+
 __device__ __forceinline__ void mma_f16(float d[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
                                         uint32_t b0, uint32_t b1, float c0, float c1, float c2, float c3) {
     asm volatile(

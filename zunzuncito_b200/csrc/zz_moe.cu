@@ -37,7 +37,7 @@ int launch_s8_to_h(const int8_t *q, __half *h, long n, cudaStream_t st);
 __global__ void k_rows_sx(const int8_t *__restrict__ xq, const float *__restrict__ xs, int S, int I,
                           float *__restrict__ xsx);
 int launch_moe_tc(int fmt, int epi, const GemmArgs &a, int n_groups, int *err, cudaStream_t st);
-int launch_moe_dec(int fmt, const GemmArgs &gu, const GemmArgs &dn, int max_items, float *hbuf, cudaStream_t st);
+int launch_moe_dec(int fmt, const GemmArgs &gu, const GemmArgs &dn, int P, float *hbuf, cudaStream_t st);
 
 // Expert engine. Default ("auto"): the small-batch GEMV kernels (zz_moe_dec.cu) when
 // S*K <= DEC_MAX_PAIRS, else the int8 mma.sync GEMM (k_gemm<..., S8>), the fastest
@@ -50,7 +50,8 @@ static int moe_engine(int P) {
     if (e && !strcmp(e, "tc")) return ENG_TC;
     if (e && !strcmp(e, "mma")) return ENG_MMA;
     if (e && !strcmp(e, "mma8")) return ENG_MMA8;
-    if (e && !strcmp(e, "dec")) return ENG_DEC;
+    // the decode kernels take calls of up to DEC_MAX_PAIRS pairs; larger ones go to mma8
+    if (e && !strcmp(e, "dec")) return P <= DEC_MAX_PAIRS ? ENG_DEC : ENG_MMA8;
     return P <= DEC_MAX_PAIRS ? ENG_DEC : ENG_MMA8;
 }
 constexpr int TC_BN = 32;
@@ -60,7 +61,7 @@ constexpr int TC_BN = 32;
 #endif
 constexpr int MOE_BN = ZZ_MOE_BN;
 constexpr int ROW_ALIGN = 16;
-constexpr int DEC_BN = 2;      // rows per work item of the small-batch kernels (DEC_C)  // pair rows of each expert start on a 16-row boundary
+constexpr int DEC_BN = 2;      // rows per work item of the small-batch kernels (DEC_C)
 constexpr int DENSE_BN = 64;
 
 static inline size_t a256(size_t n) { return (n + 255) & ~(size_t)255; }
@@ -401,7 +402,6 @@ static int moe_impl(const zz_expert_bank *b, const float *X, const int8_t *xq_in
         dn.items = w.items; dn.n_items = w.n_items; dn.pair_src = w.pair_src; dn.pair_w = w.pair_w; dn.K = K;
         dn.out = OUT; dn.hq = w.hq; dn.hs = w.hs;
         prof_mark(st);
-        // items of <= DEC_BN rows: at most P items (plus one empty tail)
         int ok = launch_moe_dec(fmt, gu, dn, P, w.hf, st);
         prof_mark(st);
         prof_mark(st);

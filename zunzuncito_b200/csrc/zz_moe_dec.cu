@@ -56,8 +56,17 @@ __device__ __forceinline__ void load_x8(const int8_t *p, uint32_t x[8]) {
     x[4] = hi.x; x[5] = hi.y; x[6] = hi.z; x[7] = hi.w;
 }
 
-template <int FMT>
+constexpr int DEC_MAX_P = 64;  // pairs of a call on this path (S*K)
+
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" :::); }
+
+
+// NBL: blocks per lane of a gate/up row, ceil(nb / 32)
+template <int FMT, int NBL>
 __global__ void __launch_bounds__(256) k_dec_gateup(GemmArgs a, float *__restrict__ hbuf) {
+    // the down kernel (a programmatic dependent launch) may start its prefetch now
+    griddep_launch_dependents();
     const int item = blockIdx.y;
     if (item >= *a.n_items) return;
     const WorkItem it = a.items[item];
@@ -65,16 +74,32 @@ __global__ void __launch_bounds__(256) k_dec_gateup(GemmArgs a, float *__restric
     const int MI = a.O / 2, D = a.I, nb = D / ZZ_BLK, nbp = (nb + 7) & ~7;
     const int f = blockIdx.x * 8 + warp;
     if (f >= MI) return;
+    const int grp = f / 64, fi = f % 64;
+    const int rg = grp * 128 + fi, ru = rg + 64;  // rows of the interleaved gate/up stack
+    const int CB = FMT == GPU_FMT_Q40 ? 16 : FMT == GPU_FMT_Q80 ? 32 : 8;
+    const uint8_t *codes = a.codes + (long)it.group * a.codes_gstride;
+    const uint8_t *grow = codes + (size_t)rg * nb * CB, *urow = codes + (size_t)ru * nb * CB;
+    const __half *sc = reinterpret_cast<const __half *>(reinterpret_cast<const uint8_t *>(a.scale) +
+                                                        (long)it.group * a.scale_gstride);
+    const __half *gs = FMT == GPU_FMT_TQ2 ? nullptr : sc + (size_t)rg * nbp;
+    const __half *us = FMT == GPU_FMT_TQ2 ? nullptr : sc + (size_t)ru * nbp;
+    // both rows' code blocks of this lane are requested first, then the token rows
+    WBlock kg[NBL], ku[NBL];
+#pragma unroll
+    for (int i = 0; i < NBL; i++) {
+        const int b = lane + 32 * i;
+        if (b < nb) { kg[i] = load_block<FMT>(grow, b, gs); ku[i] = load_block<FMT>(urow, b, us); }
+    }
     const int nc = it.count;
     // the item's token rows, this lane's blocks b = lane + 32 i, in registers
-    uint32_t xr[DEC_C][DEC_NBL][8];
-    float xsc[DEC_C][DEC_NBL], tot[DEC_C];
+    uint32_t xr[DEC_C][NBL][8];
+    float xsc[DEC_C][NBL], tot[DEC_C];
 #pragma unroll
     for (int c = 0; c < DEC_C; c++) {
         const int tok = c < nc ? a.pair_src[it.row0 + c] / a.K : 0;
         tot[c] = FMT == GPU_FMT_TQ2 ? a.xsx[tok] : 0.f;
 #pragma unroll
-        for (int i = 0; i < DEC_NBL; i++) {
+        for (int i = 0; i < NBL; i++) {
             const int b = lane + 32 * i;
             if (c < nc && b < nb) {
                 load_x8(reinterpret_cast<const int8_t *>(a.xq) + (size_t)tok * D + (size_t)b * 32, xr[c][i]);
@@ -86,28 +111,17 @@ __global__ void __launch_bounds__(256) k_dec_gateup(GemmArgs a, float *__restric
             }
         }
     }
-    const int grp = f / 64, fi = f % 64;
-    const int rg = grp * 128 + fi, ru = rg + 64;  // rows of the interleaved gate/up stack
-    const int CB = FMT == GPU_FMT_Q40 ? 16 : FMT == GPU_FMT_Q80 ? 32 : 8;
-    const uint8_t *codes = a.codes + (long)it.group * a.codes_gstride;
-    const uint8_t *grow = codes + (size_t)rg * nb * CB, *urow = codes + (size_t)ru * nb * CB;
-    const __half *sc = reinterpret_cast<const __half *>(reinterpret_cast<const uint8_t *>(a.scale) +
-                                                        (long)it.group * a.scale_gstride);
-    const __half *gs = FMT == GPU_FMT_TQ2 ? nullptr : sc + (size_t)rg * nbp;
-    const __half *us = FMT == GPU_FMT_TQ2 ? nullptr : sc + (size_t)ru * nbp;
     float ag[DEC_C], au[DEC_C];
 #pragma unroll
     for (int c = 0; c < DEC_C; c++) ag[c] = au[c] = 0.f;
 #pragma unroll
-    for (int i = 0; i < DEC_NBL; i++) {
+    for (int i = 0; i < NBL; i++) {
         const int b = lane + 32 * i;
         if (b < nb) {
-            // both rows' codes are loaded before any dot, so the loads overlap
-            const WBlock kg = load_block<FMT>(grow, b, gs), ku = load_block<FMT>(urow, b, us);
 #pragma unroll
             for (int c = 0; c < DEC_C; c++) {
-                ag[c] = fmaf(kg.scale * xsc[c][i], (float)block_dot<FMT>(kg, xr[c][i]), ag[c]);
-                au[c] = fmaf(ku.scale * xsc[c][i], (float)block_dot<FMT>(ku, xr[c][i]), au[c]);
+                ag[c] = fmaf(kg[i].scale * xsc[c][i], (float)block_dot<FMT>(kg[i], xr[c][i]), ag[c]);
+                au[c] = fmaf(ku[i].scale * xsc[c][i], (float)block_dot<FMT>(ku[i], xr[c][i]), au[c]);
             }
         }
     }
@@ -125,20 +139,53 @@ __global__ void __launch_bounds__(256) k_dec_gateup(GemmArgs a, float *__restric
     }
 }
 
-template <int FMT>
+// NB8: blocks per lane of a down row (8 lanes per row), ceil(nb / 8)
+template <int FMT, int NB8>
 __global__ void __launch_bounds__(256) k_dec_down(GemmArgs a, const float *__restrict__ hbuf) {
+    // Launched as a programmatic dependent of the gate/up kernel: the items (written by
+    // the routing kernel, which completed before gate/up started) and this CTA's weight
+    // loads proceed while gate/up runs; griddep_wait() then orders every read of the
+    // hidden rows, and every write, after gate/up has completed.
     const int item = blockIdx.y;
-    if (item >= *a.n_items) return;
+    if (item >= *a.n_items) { griddep_wait(); return; }
     const WorkItem it = a.items[item];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int D = a.O, MI = a.I, nb = MI / ZZ_BLK, nbp = (nb + 7) & ~7;
     const int nc = it.count;
+    const int CB = FMT == GPU_FMT_Q40 ? 16 : FMT == GPU_FMT_Q80 ? 32 : 8;
+    const uint8_t *codes = a.codes + (long)it.group * a.codes_gstride;
+    const __half *sc = reinterpret_cast<const __half *>(reinterpret_cast<const uint8_t *>(a.scale) +
+                                                        (long)it.group * a.scale_gstride);
+    // Each warp takes 4 output rows at once, 8 lanes per row: lane l works on row
+    // o0 + l/8 and its blocks b = l%8 + 8 i; all of a lane's weight loads are issued
+    // here, before the wait for the gate/up kernel (one DRAM round trip per warp,
+    // overlapped with gate/up).
+    const int rl = lane >> 3, sl = lane & 7;
+    const int o = blockIdx.x * 32 + warp * 4 + rl;
+    const bool orow = o < D;
+    const uint8_t *row = codes + (size_t)(orow ? o : 0) * nb * CB;
+    const __half *srow = FMT == GPU_FMT_TQ2 ? nullptr : sc + (size_t)(orow ? o : 0) * nbp;
+    WBlock k[NB8];
+#pragma unroll
+    for (int i = 0; i < NB8; i++) {
+        const int b = sl + 8 * i;
+        if (orow && b < nb) k[i] = load_block<FMT>(row, b, srow);
+    }
+    float wt[DEC_C];
+    int tok[DEC_C];
+#pragma unroll
+    for (int c = 0; c < DEC_C; c++) {
+        wt[c] = c < nc ? a.pair_w[it.row0 + c] : 0.f;
+        tok[c] = c < nc ? a.pair_src[it.row0 + c] / a.K : 0;
+    }
+    griddep_wait();  // gate/up's hidden rows are complete and visible from here on
+
     __shared__ __align__(16) int8_t hq_s[DEC_C][DEC_NBL * 32 * 32];
     __shared__ float hs_s[DEC_C][DEC_NBL * 32];
     __shared__ int hb_s[DEC_C][DEC_NBL * 32];
     __shared__ float tot_s[DEC_C];
     // requantize the item's hidden rows (one warp per 32-block); CTA 0 also records
-    // hq / hs / hblk of the pair rows in the workspace, as the GEMM path does
+    // hq / hs of the pair rows in the workspace, as the GEMM path does
     for (int w = warp; w < DEC_C * nb; w += 8) {
         const int c = w / nb, b = w % nb;
         if (c >= nc) continue;
@@ -148,7 +195,7 @@ __global__ void __launch_bounds__(256) k_dec_down(GemmArgs a, const float *__res
         hq_s[c][b * 32 + lane] = q;
         int s = q;
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+        for (int m = 16; m > 0; m >>= 1) s += __shfl_xor_sync(0xffffffffu, s, m);
         if (lane == 0) { hs_s[c][b] = d; hb_s[c][b] = s; }
         if (blockIdx.x == 0) {
             a.hq[pr * MI + b * 32 + lane] = q;
@@ -163,78 +210,76 @@ __global__ void __launch_bounds__(256) k_dec_down(GemmArgs a, const float *__res
         tot_s[c] = (float)t;
     }
     __syncthreads();
-    uint32_t xr[DEC_C][DEC_NBL][8];
-    float xsc[DEC_C][DEC_NBL];
+    float acc[DEC_C];
 #pragma unroll
-    for (int c = 0; c < DEC_C; c++)
+    for (int c = 0; c < DEC_C; c++) acc[c] = 0.f;
 #pragma unroll
-        for (int i = 0; i < DEC_NBL; i++) {
-            const int b = lane + 32 * i;
-            if (c < nc && b < nb) {
-                load_x8(&hq_s[c][b * 32], xr[c][i]);
-                xsc[c][i] = hs_s[c][b];
-            } else {
+    for (int i = 0; i < NB8; i++) {
+        const int b = sl + 8 * i;
+        if (orow && b < nb) {
 #pragma unroll
-                for (int k = 0; k < 8; k++) xr[c][i][k] = 0;
-                xsc[c][i] = 0.f;
+            for (int c = 0; c < DEC_C; c++) {
+                if (c < nc) {
+                    uint32_t x[8];
+                    load_x8(&hq_s[c][b * 32], x);
+                    acc[c] = fmaf(k[i].scale * hs_s[c][b], (float)block_dot<FMT>(k[i], x), acc[c]);
+                }
             }
         }
-    float wt[DEC_C];
-    int tok[DEC_C];
+    }
 #pragma unroll
     for (int c = 0; c < DEC_C; c++) {
-        wt[c] = c < nc ? a.pair_w[it.row0 + c] : 0.f;
-        tok[c] = c < nc ? a.pair_src[it.row0 + c] / a.K : 0;
-    }
-    const int CB = FMT == GPU_FMT_Q40 ? 16 : FMT == GPU_FMT_Q80 ? 32 : 8;
-    const uint8_t *codes = a.codes + (long)it.group * a.codes_gstride;
-    const __half *sc = reinterpret_cast<const __half *>(reinterpret_cast<const uint8_t *>(a.scale) +
-                                                        (long)it.group * a.scale_gstride);
-    const int o0 = blockIdx.x * 32 + warp * 4;
+        float y = acc[c];
 #pragma unroll
-    for (int r = 0; r < 4; r++) {
-        const int o = o0 + r;
-        if (o >= D) break;
-        const uint8_t *row = codes + (size_t)o * nb * CB;
-        const __half *srow = FMT == GPU_FMT_TQ2 ? nullptr : sc + (size_t)o * nbp;
-        float acc[DEC_C];
-#pragma unroll
-        for (int c = 0; c < DEC_C; c++) acc[c] = 0.f;
-#pragma unroll
-        for (int i = 0; i < DEC_NBL; i++) {
-            const int b = lane + 32 * i;
-            if (b < nb) {
-                const WBlock k = load_block<FMT>(row, b, srow);
-#pragma unroll
-                for (int c = 0; c < DEC_C; c++) acc[c] = fmaf(k.scale * xsc[c][i], (float)block_dot<FMT>(k, xr[c][i]), acc[c]);
-            }
-        }
-#pragma unroll
-        for (int c = 0; c < DEC_C; c++) {
-            float y = warp_sum(acc[c]);
-            if (lane == 0 && c < nc) {
-                if (FMT == GPU_FMT_TQ2) y = reinterpret_cast<const float *>(sc)[o] * (y - tot_s[c]);
-                atomicAdd(a.out + (size_t)tok[c] * D + o, wt[c] * y);
-            }
+        for (int m = 4; m > 0; m >>= 1) y += __shfl_xor_sync(0xffffffffu, y, m);
+        if (sl == 0 && orow && c < nc) {
+            if (FMT == GPU_FMT_TQ2) y = reinterpret_cast<const float *>(sc)[o] * (y - tot_s[c]);
+            atomicAdd(a.out + (size_t)tok[c] * D + o, wt[c] * y);
         }
     }
 }
 
-// gate/up then down for items of <= DEC_C tokens; hbuf: [pair rows][inter] fp32
-int launch_moe_dec(int fmt, const GemmArgs &gu, const GemmArgs &dn, int max_items, float *hbuf, cudaStream_t st) {
+// gate/up then down for a decode call (P <= DEC_MAX_P pairs, routed by k_route); hbuf:
+// [pair rows][inter] fp32. The down kernel is a programmatic dependent launch of gate/up.
+int launch_moe_dec(int fmt, const GemmArgs &gu, const GemmArgs &dn, int P, float *hbuf, cudaStream_t st) {
     const int MI = gu.O / 2, D = dn.O;
+    if (P > DEC_MAX_P) return fail("dec: %d pairs exceed the decode path's %d", P, DEC_MAX_P);
     if (gu.I / 32 > DEC_NBL * 32 || dn.I / 32 > DEC_NBL * 32) return fail("dec: K too large for the decode path");
+    const int max_items = P > 0 ? P : 1;  // items of <= DEC_C rows: at most one per pair
     dim3 g1((MI + 7) / 8, max_items), g2((D + 31) / 32, max_items);
-    if (fmt == GPU_FMT_Q40) {
-        k_dec_gateup<GPU_FMT_Q40><<<g1, 256, 0, st>>>(gu, hbuf);
-        k_dec_down<GPU_FMT_Q40><<<g2, 256, 0, st>>>(dn, hbuf);
-    } else if (fmt == GPU_FMT_Q80) {
-        k_dec_gateup<GPU_FMT_Q80><<<g1, 256, 0, st>>>(gu, hbuf);
-        k_dec_down<GPU_FMT_Q80><<<g2, 256, 0, st>>>(dn, hbuf);
-    } else {
-        k_dec_gateup<GPU_FMT_TQ2><<<g1, 256, 0, st>>>(gu, hbuf);
-        k_dec_down<GPU_FMT_TQ2><<<g2, 256, 0, st>>>(dn, hbuf);
+    cudaLaunchAttribute pdl[1];
+    pdl[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    pdl[0].val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchConfig_t cfg2{};
+    cfg2.gridDim = g2; cfg2.blockDim = dim3(256); cfg2.dynamicSmemBytes = 0; cfg2.stream = st;
+    cfg2.attrs = pdl; cfg2.numAttrs = 1;
+    const int nbl = (gu.I / 32 + 31) / 32, nb8 = (dn.I / 32 + 7) / 8;
+    cudaError_t e = cudaSuccess;
+#define ZZ_GU(F, N) case N: k_dec_gateup<F, N><<<g1, 256, 0, st>>>(gu, hbuf); break;
+#define ZZ_GUS(F) \
+    switch (nbl) { ZZ_GU(F, 1) ZZ_GU(F, 2) ZZ_GU(F, 3) ZZ_GU(F, 4) default: return fail("dec: K too large for the decode path"); }
+#define ZZ_DN(F, N) case N: e = cudaLaunchKernelEx(&cfg2, k_dec_down<F, N>, dn, (const float *)hbuf); break;
+#define ZZ_DNS(F)                                                                                           \
+    switch (nb8) {                                                                                          \
+        ZZ_DN(F, 1) ZZ_DN(F, 2) ZZ_DN(F, 3) ZZ_DN(F, 4) ZZ_DN(F, 5) ZZ_DN(F, 6) ZZ_DN(F, 7) ZZ_DN(F, 8)     \
+        ZZ_DN(F, 9) ZZ_DN(F, 10) ZZ_DN(F, 11) ZZ_DN(F, 12) ZZ_DN(F, 13) ZZ_DN(F, 14) ZZ_DN(F, 15) ZZ_DN(F, 16) \
+        default: return fail("dec: K too large for the decode path");                                       \
     }
+    if (fmt == GPU_FMT_Q40) {
+        ZZ_GUS(GPU_FMT_Q40)
+        ZZ_DNS(GPU_FMT_Q40)
+    } else if (fmt == GPU_FMT_Q80) {
+        ZZ_GUS(GPU_FMT_Q80)
+        ZZ_DNS(GPU_FMT_Q80)
+    } else {
+        ZZ_GUS(GPU_FMT_TQ2)
+        ZZ_DNS(GPU_FMT_TQ2)
+    }
+#undef ZZ_DNS
+#undef ZZ_DN
+#undef ZZ_GUS
+#undef ZZ_GU
+    if (!check_cuda(e, "dec down launch")) return 0;
     return check_cuda(cudaGetLastError(), "dec launch");
 }
 
