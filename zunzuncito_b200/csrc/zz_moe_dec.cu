@@ -72,8 +72,9 @@ __global__ void __launch_bounds__(256) k_dec_gateup(GemmArgs a, float *__restric
     const WorkItem it = a.items[item];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int MI = a.O / 2, D = a.I, nb = D / ZZ_BLK, nbp = (nb + 7) & ~7;
-    const int f = blockIdx.x * 8 + warp;
-    if (f >= MI) return;
+    const int f0 = blockIdx.x * 8 + warp;
+    const bool fv = f0 < MI;
+    const int f = fv ? f0 : MI - 1;
     const int grp = f / 64, fi = f % 64;
     const int rg = grp * 128 + fi, ru = rg + 64;  // rows of the interleaved gate/up stack
     const int CB = FMT == GPU_FMT_Q40 ? 16 : FMT == GPU_FMT_Q80 ? 32 : 8;
@@ -91,26 +92,21 @@ __global__ void __launch_bounds__(256) k_dec_gateup(GemmArgs a, float *__restric
         if (b < nb) { kg[i] = load_block<FMT>(grow, b, gs); ku[i] = load_block<FMT>(urow, b, us); }
     }
     const int nc = it.count;
-    // the item's token rows, this lane's blocks b = lane + 32 i, in registers
-    uint32_t xr[DEC_C][NBL][8];
-    float xsc[DEC_C][NBL], tot[DEC_C];
+    // the item's token rows (q8_0 codes and block scales) staged in shared memory
+    __shared__ __align__(16) int8_t xs_q[DEC_C][DEC_NBL * 32 * 32];
+    __shared__ float xs_d[DEC_C][DEC_NBL * 32];
+    float tot[DEC_C];
 #pragma unroll
     for (int c = 0; c < DEC_C; c++) {
         const int tok = c < nc ? a.pair_src[it.row0 + c] / a.K : 0;
-        tot[c] = FMT == GPU_FMT_TQ2 ? a.xsx[tok] : 0.f;
-#pragma unroll
-        for (int i = 0; i < NBL; i++) {
-            const int b = lane + 32 * i;
-            if (c < nc && b < nb) {
-                load_x8(reinterpret_cast<const int8_t *>(a.xq) + (size_t)tok * D + (size_t)b * 32, xr[c][i]);
-                xsc[c][i] = a.xs[(size_t)tok * nb + b];
-            } else {
-#pragma unroll
-                for (int k = 0; k < 8; k++) xr[c][i][k] = 0;
-                xsc[c][i] = 0.f;
-            }
+        tot[c] = FMT == GPU_FMT_TQ2 && c < nc ? a.xsx[tok] : 0.f;
+        if (c < nc) {
+            const uint4 *src = reinterpret_cast<const uint4 *>(reinterpret_cast<const int8_t *>(a.xq) + (size_t)tok * D);
+            for (int i = threadIdx.x; i < D / 16; i += blockDim.x) reinterpret_cast<uint4 *>(xs_q[c])[i] = src[i];
+            for (int i = threadIdx.x; i < nb; i += blockDim.x) xs_d[c][i] = a.xs[(size_t)tok * nb + i];
         }
     }
+    __syncthreads();
     float ag[DEC_C], au[DEC_C];
 #pragma unroll
     for (int c = 0; c < DEC_C; c++) ag[c] = au[c] = 0.f;
@@ -120,15 +116,20 @@ __global__ void __launch_bounds__(256) k_dec_gateup(GemmArgs a, float *__restric
         if (b < nb) {
 #pragma unroll
             for (int c = 0; c < DEC_C; c++) {
-                ag[c] = fmaf(kg[i].scale * xsc[c][i], (float)block_dot<FMT>(kg[i], xr[c][i]), ag[c]);
-                au[c] = fmaf(ku[i].scale * xsc[c][i], (float)block_dot<FMT>(ku[i], xr[c][i]), au[c]);
+                if (c < nc) {
+                    uint32_t x[8];
+                    load_x8(&xs_q[c][b * 32], x);
+                    const float dx = xs_d[c][b];
+                    ag[c] = fmaf(kg[i].scale * dx, (float)block_dot<FMT>(kg[i], x), ag[c]);
+                    au[c] = fmaf(ku[i].scale * dx, (float)block_dot<FMT>(ku[i], x), au[c]);
+                }
             }
         }
     }
 #pragma unroll
     for (int c = 0; c < DEC_C; c++) {
         float g = warp_sum(ag[c]), u = warp_sum(au[c]);
-        if (lane == 0 && c < nc) {
+        if (lane == 0 && c < nc && fv) {
             if (FMT == GPU_FMT_TQ2) {
                 const float *alpha = reinterpret_cast<const float *>(sc);
                 g = alpha[rg] * (g - tot[c]);
