@@ -123,9 +123,9 @@ def check_pairs(orc, kind, blobs, X, eidx, ewt, out_gpu, bank, pairs=None):
     return flipped_tok
 
 
-@pytest.fixture(params=["auto", "mma", "mma8", "tc", "dec"])
+@pytest.fixture(params=["auto", "mma", "mma8", "tc", "tcw", "dec"])
 def engine(request, monkeypatch):
-    """every expert engine: auto (GEMV for small S*K, else mma.sync), mma.sync, tcgen05,
+    """every expert engine: auto (GEMV for small S*K, else mma.sync), mma.sync, tcgen05 (32- and 128-token tiles),
     and the small-batch GEMV kernels forced (ZZ_MOE_KERNEL; calls of more than 64 pairs
     take the int8 mma.sync engine there)"""
     monkeypatch.setenv("ZZ_MOE_KERNEL", request.param)

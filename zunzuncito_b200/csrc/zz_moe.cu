@@ -37,17 +37,19 @@ int launch_s8_to_h(const int8_t *q, __half *h, long n, cudaStream_t st);
 __global__ void k_rows_sx(const int8_t *__restrict__ xq, const float *__restrict__ xs, int S, int I,
                           float *__restrict__ xsx);
 int launch_moe_tc(int fmt, int epi, const GemmArgs &a, int n_groups, int *err, cudaStream_t st);
+int launch_moe_tcw(int fmt, int epi, const GemmArgs &a, int n_groups, int *err, cudaStream_t st);
 int launch_moe_dec(int fmt, const GemmArgs &gu, const GemmArgs &dn, int P, float *hbuf, cudaStream_t st);
 
 // Expert engine. Default ("auto"): the small-batch GEMV kernels (zz_moe_dec.cu) when
 // S*K <= DEC_MAX_PAIRS, else the int8 mma.sync GEMM (k_gemm<..., S8>), the fastest
 // measured. ZZ_MOE_KERNEL=dec|mma8|mma|tc forces one (mma = the fp16-exact mma.sync
 // variant, tc = the tcgen05 kernel k_moe_tc). All are exact per block.
-enum { ENG_DEC = 0, ENG_MMA = 1, ENG_TC = 2, ENG_MMA8 = 3 };
+enum { ENG_DEC = 0, ENG_MMA = 1, ENG_TC = 2, ENG_MMA8 = 3, ENG_TCW = 4 };
 constexpr int DEC_MAX_PAIRS = 64;
 static int moe_engine(int P) {
     const char *e = getenv("ZZ_MOE_KERNEL");
     if (e && !strcmp(e, "tc")) return ENG_TC;
+    if (e && !strcmp(e, "tcw")) return ENG_TCW;
     if (e && !strcmp(e, "mma")) return ENG_MMA;
     if (e && !strcmp(e, "mma8")) return ENG_MMA8;
     // the decode kernels take calls of up to DEC_MAX_PAIRS pairs; larger ones go to mma8
@@ -55,6 +57,7 @@ static int moe_engine(int P) {
     return P <= DEC_MAX_PAIRS ? ENG_DEC : ENG_MMA8;
 }
 constexpr int TC_BN = 32;
+constexpr int TCW_BN = 128;
 
 #ifndef ZZ_MOE_BN
 #define ZZ_MOE_BN 32
@@ -363,11 +366,12 @@ static int moe_impl(const zz_expert_bank *b, const float *X, const int8_t *xq_in
     }
     prof_mark(st);
     const int eng = moe_engine(P);
-    const bool tcp = eng == ENG_TC;
+    const bool tcw = eng == ENG_TCW;
+    const bool tcp = eng == ENG_TC || tcw;  // engines on tcgen05 (pair-ordered fp16 rows)
     const int8_t *xq = xq_in;
     const float *xs = xs_in;
     if (X) {
-        const bool want_h = eng == ENG_MMA || eng == ENG_TC;  // engines reading fp16 activations
+        const bool want_h = eng == ENG_MMA || tcp;  // engines reading fp16 activations
         if (!launch_quant_act(X, S, D, w.xq, w.xs, fmt == GPU_FMT_TQ2 ? w.xsx : nullptr, want_h ? w.xh : nullptr, st,
                               OUT, D))
             return 0;
@@ -376,9 +380,9 @@ static int moe_impl(const zz_expert_bank *b, const float *X, const int8_t *xq_in
     } else {
         if (!check_cuda(cudaMemsetAsync(OUT, 0, (size_t)S * D * 4, st), "memset OUT")) return 0;
         if (fmt == GPU_FMT_TQ2) k_rows_sx<<<(S + 127) / 128, 128, 0, st>>>(xq, xs, S, D, w.xsx);
-        if ((eng == ENG_MMA || eng == ENG_TC) && !launch_s8_to_h(xq, w.xh, (long)S * D, st)) return 0;
+        if ((eng == ENG_MMA || tcp) && !launch_s8_to_h(xq, w.xh, (long)S * D, st)) return 0;
     }
-    k_route<<<1, 1024, 4 * E * sizeof(int), st>>>(eidx, ewt, P, E, tcp ? TC_BN : eng == ENG_DEC ? DEC_BN : MOE_BN,
+    k_route<<<1, 1024, 4 * E * sizeof(int), st>>>(eidx, ewt, P, E, tcw ? TCW_BN : tcp ? TC_BN : eng == ENG_DEC ? DEC_BN : MOE_BN,
                                                   (int)w.cap, w.pair_src, w.pair_w, w.items, w.n_items, w.tcerr);
     if (!check_cuda(cudaGetLastError(), "route launch")) return 0;
     if (tcp) {
@@ -419,7 +423,7 @@ static int moe_impl(const zz_expert_bank *b, const float *X, const int8_t *xq_in
     g.xg = w.xg; g.xsT = w.xsT; g.ldT = (int)w.ldT; g.hsT = w.hsT; g.rows_cap = (int)w.cap;
     prof_mark(st);
     if (tcp) {
-        if (!launch_moe_tc(fmt, EPI_GATEUP, g, E, w.tcerr, st)) return 0;
+        if (!(tcw ? launch_moe_tcw : launch_moe_tc)(fmt, EPI_GATEUP, g, E, w.tcerr, st)) return 0;
     } else if (eng == ENG_MMA8) {
         g.xq = xq;  // int8 rows
         if (!launch_gemm<EPI_GATEUP, MOE_BN, false, true>(fmt, g, dim3((2 * MI) / G_BM, maxit), st)) return 0;
@@ -438,7 +442,7 @@ static int moe_impl(const zz_expert_bank *b, const float *X, const int8_t *xq_in
     d.out = OUT; d.pair_w = w.pair_w; d.pair_src = w.pair_src; d.K = K;
     d.xg = w.hh; d.xsT = w.hsT; d.ldT = (int)w.ldT; d.rows_cap = (int)w.cap;
     if (eng == ENG_MMA8) d.xq = w.hq;
-    int ok = tcp ? launch_moe_tc(fmt, EPI_DOWN, d, E, w.tcerr, st)
+    int ok = tcp ? (tcw ? launch_moe_tcw : launch_moe_tc)(fmt, EPI_DOWN, d, E, w.tcerr, st)
              : eng == ENG_MMA8 ? launch_gemm<EPI_DOWN, MOE_BN, false, true>(fmt, d, dim3((D + G_BM - 1) / G_BM, maxit), st)
                                : launch_gemm<EPI_DOWN, MOE_BN, true>(fmt, d, dim3((D + G_BM - 1) / G_BM, maxit), st);
     prof_mark(st);

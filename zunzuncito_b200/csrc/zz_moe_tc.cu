@@ -31,6 +31,7 @@
 #include <cudaTypedefs.h>
 #include "zz_gemm.cuh"
 #include "zz_tc.cuh"
+#include "zz_tc_widen.cuh"
 
 namespace zz {
 
@@ -66,45 +67,6 @@ constexpr int SMEM = OFF_BAR + NBAR * 8 + 16 + 1024;  // + slack to align the ba
 static_assert(SMEM <= 232448, "shared memory");
 }  // namespace tcm
 
-// code bytes of one row for one stage (KB blocks); the TMA box is 128 rows of this
-template <int FMT>
-__host__ __device__ constexpr int tc_cb() { return FMT == GPU_FMT_Q40 ? 64 : FMT == GPU_FMT_Q80 ? 128 : 32; }
-template <int FMT>
-__host__ __device__ constexpr int tc_rc() { return tcm::RING / (128 * tc_cb<FMT>()); }
-
-__device__ __forceinline__ uint32_t spread_lo(uint32_t w) { return __byte_perm(w, 0u, 0x4140u); }
-__device__ __forceinline__ uint32_t spread_hi(uint32_t w) { return __byte_perm(w, 0u, 0x4342u); }
-
-// widen one row's codes of block jj of the stage (in registers, 16-byte chunks of
-// the row's stage bytes) into the block's 4 K-chunks of 8 fp16
-template <int FMT>
-__device__ __forceinline__ void widen_blk(const uint4 (&c)[tc_cb<FMT>() / 16], int jj, uint4 out[4]) {
-    if (FMT == GPU_FMT_Q40) {
-        const uint4 w = c[jj];
-        // k 0-15: low nibbles of bytes 0-15; k 16-31: the high nibbles
-        out[0] = make_uint4(q4lo_h2(spread_lo(w.x)), q4lo_h2(spread_hi(w.x)), q4lo_h2(spread_lo(w.y)), q4lo_h2(spread_hi(w.y)));
-        out[1] = make_uint4(q4lo_h2(spread_lo(w.z)), q4lo_h2(spread_hi(w.z)), q4lo_h2(spread_lo(w.w)), q4lo_h2(spread_hi(w.w)));
-        out[2] = make_uint4(q4hi_h2(spread_lo(w.x)), q4hi_h2(spread_hi(w.x)), q4hi_h2(spread_lo(w.y)), q4hi_h2(spread_hi(w.y)));
-        out[3] = make_uint4(q4hi_h2(spread_lo(w.z)), q4hi_h2(spread_hi(w.z)), q4hi_h2(spread_lo(w.w)), q4hi_h2(spread_hi(w.w)));
-    } else if (FMT == GPU_FMT_Q80) {
-        const uint4 w0 = c[2 * jj], w1 = c[2 * jj + 1];
-        out[0] = make_uint4(s8_h2(spread_lo(w0.x)), s8_h2(spread_hi(w0.x)), s8_h2(spread_lo(w0.y)), s8_h2(spread_hi(w0.y)));
-        out[1] = make_uint4(s8_h2(spread_lo(w0.z)), s8_h2(spread_hi(w0.z)), s8_h2(spread_lo(w0.w)), s8_h2(spread_hi(w0.w)));
-        out[2] = make_uint4(s8_h2(spread_lo(w1.x)), s8_h2(spread_hi(w1.x)), s8_h2(spread_lo(w1.y)), s8_h2(spread_hi(w1.y)));
-        out[3] = make_uint4(s8_h2(spread_lo(w1.z)), s8_h2(spread_hi(w1.z)), s8_h2(spread_lo(w1.w)), s8_h2(spread_hi(w1.w)));
-    } else {
-        // tq2: a pair of blocks shares the 16 bytes of its 64-weight group; block jj's
-        // codes sit at bit offset sh (k 0-15) and sh+2 (k 16-31), sh = 0 / 4 for the
-        // even / odd block
-        const uint4 w = c[jj >> 1];
-        const int sh = (jj & 1) * 4;
-        out[0] = make_uint4(c2_h2(spread_lo(w.x), sh), c2_h2(spread_hi(w.x), sh), c2_h2(spread_lo(w.y), sh), c2_h2(spread_hi(w.y), sh));
-        out[1] = make_uint4(c2_h2(spread_lo(w.z), sh), c2_h2(spread_hi(w.z), sh), c2_h2(spread_lo(w.w), sh), c2_h2(spread_hi(w.w), sh));
-        out[2] = make_uint4(c2_h2(spread_lo(w.x), sh + 2), c2_h2(spread_hi(w.x), sh + 2), c2_h2(spread_lo(w.y), sh + 2), c2_h2(spread_hi(w.y), sh + 2));
-        out[3] = make_uint4(c2_h2(spread_lo(w.z), sh + 2), c2_h2(spread_hi(w.z), sh + 2), c2_h2(spread_lo(w.w), sh + 2), c2_h2(spread_hi(w.w), sh + 2));
-    }
-}
-
 struct BMaps {
     CUtensorMap m[2];  // activation boxes of 16 and 32 rows
 };
@@ -129,7 +91,7 @@ __global__ void __launch_bounds__(tcm::NTHREADS, 1)
     k_moe_tc(const GemmArgs a, const __grid_constant__ CUtensorMap codes_map,
              const __grid_constant__ CUtensorMap scale_map, const __grid_constant__ BMaps bmaps, int *err) {
     using namespace tcm;
-    constexpr int CB = tc_cb<FMT>(), RC = tc_rc<FMT>(), SLOTB = 128 * CB, NCH = CB / 16;
+    constexpr int CB = tc_cb<FMT>(), RC = RING / (128 * CB), SLOTB = 128 * CB, NCH = CB / 16;
     extern __shared__ __align__(128) uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
     uint8_t *ring = smem + OFF_RING;
@@ -573,7 +535,7 @@ __global__ void __launch_bounds__(tcm::NTHREADS, 1)
 // ---------------------------------------------------------------- host side
 static PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
 
-static int get_encode() {
+int tc_get_encode() {
     if (g_encode) return 1;
     cudaDriverEntryPointQueryResult q;
     void *fn = nullptr;
@@ -587,8 +549,8 @@ static int get_encode() {
 // codes plane of a whole bank: rows = experts * O, row = row_bytes bytes; one box is
 // 128 rows x cb bytes (one K stage), swizzled by its width so that the producers'
 // 16-byte loads of one row each hit distinct banks
-static int make_codes_map(CUtensorMap *map, const uint8_t *codes, long rows, int row_bytes, int cb) {
-    if (!get_encode()) return 0;
+int tc_make_codes_map(CUtensorMap *map, const uint8_t *codes, long rows, int row_bytes, int cb) {
+    if (!tc_get_encode()) return 0;
     if ((uintptr_t)codes & 15 || row_bytes % 16) return fail("tc: codes plane not 16-byte aligned");
     cuuint64_t dims[2] = {(cuuint64_t)row_bytes, (cuuint64_t)rows};
     cuuint64_t strides[1] = {(cuuint64_t)row_bytes};
@@ -606,8 +568,8 @@ static int make_codes_map(CUtensorMap *map, const uint8_t *codes, long rows, int
 
 // fp16 weight-scale planes of a bank: [experts][O][nbp] (rows padded to 8 blocks), each
 // expert `gstride` bytes apart; one box is 128 rows x 8 scales (two K stages)
-static int make_scale_map(CUtensorMap *map, const void *scale, int E, int O, int nbp, long gstride) {
-    if (!get_encode()) return 0;
+int tc_make_scale_map(CUtensorMap *map, const void *scale, int E, int O, int nbp, long gstride) {
+    if (!tc_get_encode()) return 0;
     if ((uintptr_t)scale & 15 || gstride % 16 || nbp % 8) return fail("tc: scale planes not 16-byte aligned");
     cuuint64_t dims[3] = {(cuuint64_t)nbp, (cuuint64_t)O, (cuuint64_t)E};
     cuuint64_t strides[2] = {(cuuint64_t)nbp * 2, (cuuint64_t)gstride};
@@ -622,8 +584,8 @@ static int make_scale_map(CUtensorMap *map, const void *scale, int E, int O, int
 
 // pair-ordered fp16 activation rows [rows, I] seen as (8 halves) x rows x (I/8 chunks),
 // so one box {8, 128, 4} lands a block's 128 x 32 tile as K-major core matrices
-static int make_b_map(CUtensorMap *map, const __half *xg, int rows, int I, int box_rows) {
-    if (!get_encode()) return 0;
+int tc_make_b_map(CUtensorMap *map, const __half *xg, int rows, int I, int box_rows) {
+    if (!tc_get_encode()) return 0;
     if ((uintptr_t)xg & 15 || I % 32) return fail("tc: activation rows not 16-byte aligned");
     cuuint64_t dims[2] = {(cuuint64_t)I, (cuuint64_t)rows};
     cuuint64_t strides[1] = {(cuuint64_t)I * 2};
@@ -648,13 +610,13 @@ static int launch_tc_t(const GemmArgs &a, int n_groups, int *err, cudaStream_t s
     const int row_bytes = FMT == GPU_FMT_Q40 ? a.I / 2 : FMT == GPU_FMT_Q80 ? a.I : a.I / 4;
     CUtensorMap map, smap;
     BMaps bmaps;
-    if (!make_codes_map(&map, a.codes, (long)n_groups * a.O, row_bytes, tc_cb<FMT>())) return 0;
+    if (!tc_make_codes_map(&map, a.codes, (long)n_groups * a.O, row_bytes, tc_cb<FMT>())) return 0;
     if (FMT == GPU_FMT_TQ2)
         smap = map;  // tq2 has one fp32 alpha per row, applied at the tile end
-    else if (!make_scale_map(&smap, a.scale, n_groups, a.O, ((a.I / ZZ_BLK) + 7) & ~7, a.scale_gstride))
+    else if (!tc_make_scale_map(&smap, a.scale, n_groups, a.O, ((a.I / ZZ_BLK) + 7) & ~7, a.scale_gstride))
         return 0;
     for (int i = 0; i < 2; i++)
-        if (!make_b_map(&bmaps.m[i], a.xg, a.rows_cap, a.I, 16 << i)) return 0;
+        if (!tc_make_b_map(&bmaps.m[i], a.xg, a.rows_cap, a.I, 16 << i)) return 0;
     int dev = 0, sms = 148;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
