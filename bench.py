@@ -280,7 +280,7 @@ def main():
     import torch
     if world > 1:
         from zunzuncito_b200 import ep
-        ep.bench_main(a, rank, world)
+        ep.bench_main(a, rank, world, ClockSampler)
         return
     import zunzuncito_b200 as zz
     from zunzuncito_b200 import synth

@@ -69,7 +69,7 @@ def ep_moe_layer(xq, xs, eidx, ewt, n_experts, local_ffn, group=None):
 
 
 # ----------------------------------------------------------------------------- bench
-def bench_main(a, rank, world):
+def bench_main(a, rank, world, clock_sampler=None):
     """bench.py under torchrun: weak scaling, each rank S tokens and E/G experts per
     layer of the 30-layer Gemma-4 stack; time = max over ranks of the device time."""
     import json
@@ -114,17 +114,59 @@ def bench_main(a, rank, world):
         step()
     torch.cuda.synchronize()
     dist.barrier()
+    # Eager issue: a CUDA graph of the step (NCCL all-to-alls captured) timed within 4%
+    # of eager, and its teardown with the process group did not finish, so it is not used.
+    mode, run = "eager", step
+    torch.cuda.synchronize()
+    dist.barrier()
     torch.cuda.synchronize()
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    sampler = clock_sampler(local) if clock_sampler else None
+    if sampler:
+        sampler.__enter__()
     t0.record()
     for _ in range(a.steps):
-        step()
+        run()
     t1.record()
     torch.cuda.synchronize()
+    if sampler:
+        sampler.__exit__(None, None, None)
     ms = torch.tensor([t0.elapsed_time(t1) / a.steps], device="cuda")
     dist.all_reduce(ms, op=dist.ReduceOp.MAX)
     dist.barrier()
     ms = float(ms.item())
+    # e2e: the same layers through the public API with this rank's tokens and routing
+    # copied in from pinned host memory and each layer's output copied back
+    Xh = torch.from_numpy(synth.gaussian(7 + rank, (S, D))).pin_memory()
+    eh = [torch.from_numpy(r[0]).pin_memory() for r in routes]
+    wh = [torch.from_numpy(r[1]).pin_memory() for r in routes]
+    oh = torch.empty((L, S, D), dtype=torch.float32).pin_memory()
+    Xd = torch.empty((S, D), device="cuda")
+    ed = torch.empty((S, K), dtype=torch.int32, device="cuda")
+    wd = torch.empty((S, K), device="cuda")
+
+    def step_e2e():
+        for l in range(L):
+            Xd.copy_(Xh, non_blocking=True)
+            ed.copy_(eh[l], non_blocking=True)
+            wd.copy_(wh[l], non_blocking=True)
+            xq, xs, _ = zz.quant_act(Xd)
+            ffn = lambda q, s, e, w, b=banks[l]: zz.moe_ffn_q8(b, q, s, e, w, zz.ZZ_ACT_GEGLU_TANH)
+            oh[l].copy_(ep_moe_layer(xq, xs, ed, wd, E, ffn), non_blocking=True)
+
+    step_e2e()
+    torch.cuda.synchronize()
+    dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ne = max(2, a.steps // 2)
+    e0.record()
+    for _ in range(ne):
+        step_e2e()
+    e1.record()
+    torch.cuda.synchronize()
+    ems = torch.tensor([e0.elapsed_time(e1) / ne], device="cuda")
+    dist.all_reduce(ems, op=dist.ReduceOp.MAX)
+    ems = float(ems.item())
     if rank == 0:
         value = S * world * L / (ms / 1e3)
         line = {"metric": "moe_layer_tok_per_s", "value": value, "unit": "token-layers/s", "n_gpus": world,
@@ -133,7 +175,11 @@ def bench_main(a, rank, world):
                 "config": {"workload": f"Gemma-4 batch-union MoE stack, {L} layers x 128 q4_0 experts sharded "
                                        f"{per}/GPU, S={S} tokens per GPU per step, top-8 Zipf(1.1), NCCL all-to-all "
                                        "of q8_0 rows", "tokens_per_gpu": S, "layers": L, "parallelism": f"ep{world}",
-                           "l2": "no flush: per-layer expert reads exceed L2"},
+                           "l2": "no flush: per-layer expert reads exceed L2", "timing": mode},
+                "clocks": sampler.summary() if sampler else None,
+                "e2e": {"value": S * world * L / (ems / 1e3), "unit": "token-layers/s",
+                        "h2d_bytes_per_step": world * L * (S * D * 4 + S * K * 8),
+                        "d2h_bytes_per_step": world * L * S * D * 4},
                 "gpu_launches": a.steps * L * 5}
         print(json.dumps(line), flush=True)
     dist.destroy_process_group()
