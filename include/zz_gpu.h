@@ -168,6 +168,21 @@ int zz_moe_ffn_noalloc_dev(const zz_expert_bank *bank, const float *X, const int
                            const float *ewt, float *OUT, int S, int K, int act, float clamp,
                            void *stream);
 
+/* ---- expert-parallel exchange layout (no reference counterpart: the reference runs
+ * one process; these pack and unpack the rows of the NCCL all-to-all that shards the
+ * experts over the GPUs of a node).
+ * One row per (destination rank d, token s), zz_ep_row_bytes(D, K) bytes:
+ *   q8_0 codes int8[D] | block scales f32[D/32] | local expert ids int32[K] | weights f32[K]
+ * ids are the token's experts held by d as id - d*per_rank, -1 for the others (weight 0).
+ * zz_ep_pack_dev writes payload[world][S] rows (destination-major, so an equal-split
+ * all-to-all sends each rank its S rows); zz_ep_unpack_dev splits R received rows into
+ * the four arrays zz_moe_ffn_q8_dev takes. Pointers 4-byte aligned, D % 32 == 0. */
+size_t zz_ep_row_bytes(int D, int K);
+int zz_ep_pack_dev(const int8_t *xq, const float *xs, const int32_t *eidx, const float *ewt, int S, int D, int K,
+                   int world, int per_rank, uint8_t *payload, void *stream);
+int zz_ep_unpack_dev(const uint8_t *rows, int R, int D, int K, int8_t *xq, float *xs, int32_t *eidx, float *ewt,
+                     void *stream);
+
 /* Diagnostic: byte offset inside the zz_moe_ffn_dev workspace (same bank, S, K) of
  *   0 pair_src int32[S*K]  routing slot s*K+k held by each pair row, grouped by expert
  *   1 pair_w   f32[S*K]    its router weight

@@ -181,3 +181,25 @@ def test_gpu_h_surface(orc):
     assert b"gpu_map" in L.gpu_last_error()
     assert L.gpu_unmap(ctypes.c_void_p(base)) == 1
     assert L.gpu_q40_matmul(y.ctypes.data, ctypes.c_void_p(base), y.ctypes.data, 1, 32, 1) == 0
+
+
+def test_ep_pack_unpack_layout():
+    """zz_ep_pack_dev / zz_ep_unpack_dev against the torch construction of the same
+    exchange rows (ep._exchange_torch's layout), with invalid and out-of-range ids."""
+    from zunzuncito_b200 import ep
+    S, D, K, world, per = 37, 2816, 8, 4, 32
+    r = synth.rng(50)
+    xq = torch.from_numpy(r.integers(-127, 128, size=(S, D), dtype=np.int8)).cuda()
+    xs = torch.from_numpy(r.random((S, D // 32), dtype=np.float32)).cuda()
+    e = r.integers(-1, world * per + 3, size=(S, K)).astype(np.int32)
+    eidx = torch.from_numpy(e).cuda()
+    ewt = torch.from_numpy(r.random((S, K), dtype=np.float32)).cuda()
+    pay = zz.ep_pack(xq, xs, eidx, ewt, world, per)
+    assert pay.shape == (world, S, zz.lib.zz_ep_row_bytes(D, K))
+    got = zz.ep_unpack(pay, D, K)
+    for d in range(world):
+        sl = slice(d * S, (d + 1) * S)
+        assert torch.equal(got[0][sl], xq) and torch.equal(got[1][sl], xs)
+        mine = (eidx >= 0) & (torch.div(eidx, per, rounding_mode="floor") == d)
+        assert torch.equal(got[2][sl], torch.where(mine, eidx - d * per, torch.full_like(eidx, -1)))
+        assert torch.equal(got[3][sl], torch.where(mine, ewt, torch.zeros_like(ewt)))

@@ -56,6 +56,10 @@ _PROTOS = [
     ("zz_moe_workspace_offset", c_size_t, [ctypes.POINTER(ExpertBank), c_int, c_int, c_int]),
     ("zz_moe_ffn_q8_dev", c_int, [ctypes.POINTER(ExpertBank), c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
                                   c_int, c_int, c_int, c_float, c_void_p, c_size_t, c_int, c_void_p]),
+    ("zz_ep_row_bytes", c_size_t, [c_int, c_int]),
+    ("zz_ep_pack_dev", c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int, c_void_p,
+                               c_void_p]),
+    ("zz_ep_unpack_dev", c_int, [c_void_p, c_int, c_int, c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p]),
     ("zz_moe_ffn_noalloc_dev", c_int, [ctypes.POINTER(ExpertBank), c_void_p, c_void_p, c_void_p, c_void_p, c_int,
                                        c_int, c_int, c_float, c_void_p]),
     ("zz_prof_enable", c_int, [c_int]),

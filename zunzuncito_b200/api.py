@@ -10,7 +10,8 @@ import torch
 from . import (GPU_FMT_Q40, GPU_FMT_Q80, GPU_FMT_TQ2, ExpertBank, QTensor, check, lib)
 
 __all__ = ["ref_row_bytes", "ref_tensor_bytes", "expert_blob_bytes", "quant_act", "quant_rows",
-           "QTensorDev", "matvec", "blocksums", "ExpertBankDev", "moe_ffn", "moe_ffn_q8", "alloc_aligned"]
+           "QTensorDev", "matvec", "blocksums", "ExpertBankDev", "moe_ffn", "moe_ffn_q8", "alloc_aligned",
+           "ep_pack", "ep_unpack"]
 
 
 def _stream():
@@ -146,3 +147,25 @@ def moe_ffn_q8(bank, xq, xs, eidx, ewt, act, clamp=0.0, out=None, validate=False
     check(lib.zz_moe_ffn_q8_dev(ctypes.byref(bank.b), _p(xq), _p(xs), _p(eidx), _p(ewt), _p(out), S, K, act,
                                 float(clamp), _p(ws), ws.numel(), int(validate), _stream()), "zz_moe_ffn_q8_dev")
     return out
+
+
+def ep_pack(xq, xs, eidx, ewt, world, per_rank):
+    """Expert-parallel dispatch rows [world, S, row] (zz_ep_pack_dev)."""
+    S, D = xq.shape
+    K = eidx.shape[1]
+    out = torch.empty((world, S, lib.zz_ep_row_bytes(D, K)), dtype=torch.uint8, device=xq.device)
+    check(lib.zz_ep_pack_dev(_p(xq), _p(xs), _p(eidx), _p(ewt), S, D, K, world, per_rank, _p(out), _stream()),
+          "zz_ep_pack_dev")
+    return out
+
+
+def ep_unpack(rows, D, K):
+    """Received exchange rows [R, row] -> xq, xs, eidx, ewt (zz_ep_unpack_dev)."""
+    R = rows.numel() // lib.zz_ep_row_bytes(D, K)
+    dev = rows.device
+    xq = torch.empty((R, D), dtype=torch.int8, device=dev)
+    xs = torch.empty((R, D // 32), dtype=torch.float32, device=dev)
+    eidx = torch.empty((R, K), dtype=torch.int32, device=dev)
+    ewt = torch.empty((R, K), dtype=torch.float32, device=dev)
+    check(lib.zz_ep_unpack_dev(_p(rows), R, D, K, _p(xq), _p(xs), _p(eidx), _p(ewt), _stream()), "zz_ep_unpack_dev")
+    return xq, xs, eidx, ewt

@@ -12,8 +12,9 @@ One layer is then
      that rank (local expert ids, -1 elsewhere) -- an NCCL all-to-all
   3. the destination runs the batch-union FFN over everything it received
      (zz_moe_ffn_q8_dev), which already sums that rank's experts per row
-  4. combine: the f32 partial rows go back with the reverse all-to-all and are added
-     into the token's output.
+  4. combine: the f32 partial rows go back and are summed per token -- on GPUs one
+     NCCL reduce-scatter of the slot-major partial rows (the sum happens inside the
+     collective); on CPU ranks the reverse all-to-all and a sum.
 
 The exchange is the only collective; dense weights are replicated. ``ep_moe_layer``
 takes the local FFN as a callable so the exchange logic runs unchanged on CPU ranks
@@ -24,6 +25,30 @@ import os
 import numpy as np
 import torch
 import torch.distributed as dist
+
+
+def _exchange_torch(xq, xs, eidx, ewt, world, per, group):
+    """the dispatch exchange built from torch ops (CPU ranks): the zz_ep_pack_dev layout"""
+    dev = xq.device
+    S, D = xq.shape
+    K = eidx.shape[1]
+    dst = torch.div(eidx, per, rounding_mode="floor").long()                # [S, K]
+    ranks = torch.arange(world, device=dev).view(world, 1, 1)
+    mine = (dst.unsqueeze(0) == ranks) & (eidx.unsqueeze(0) >= 0)           # [world, S, K]
+    loc_e = torch.where(mine, (eidx.unsqueeze(0) - ranks * per).to(torch.int32),
+                        torch.full((), -1, dtype=torch.int32, device=dev))
+    loc_w = torch.where(mine, ewt.unsqueeze(0), torch.zeros((), dtype=ewt.dtype, device=dev))
+    tok = torch.cat([xq.view(torch.uint8), xs.contiguous().view(torch.uint8)], dim=1)  # [S, D + 4 nb]
+    payload = torch.cat([tok.unsqueeze(0).expand(world, S, tok.shape[1]),
+                         loc_e.view(torch.uint8).view(world, S, 4 * K),
+                         loc_w.contiguous().view(torch.uint8).view(world, S, 4 * K)], dim=2).contiguous()
+    recv = torch.empty_like(payload)
+    dist.all_to_all_single(recv.view(world, -1), payload.view(world, -1), group=group)
+    recv = recv.view(world * S, -1)
+    nb = xs.shape[1]
+    return (recv[:, :D].contiguous().view(torch.int8), recv[:, D:D + 4 * nb].contiguous().view(torch.float32),
+            recv[:, D + 4 * nb:D + 4 * nb + 4 * K].contiguous().view(torch.int32),
+            recv[:, D + 4 * nb + 4 * K:].contiguous().view(torch.float32))
 
 
 def ep_moe_layer(xq, xs, eidx, ewt, n_experts, local_ffn, group=None):
@@ -43,26 +68,22 @@ def ep_moe_layer(xq, xs, eidx, ewt, n_experts, local_ffn, group=None):
     S, D = xq.shape
     K = eidx.shape[1]
     per = n_experts // world
-    dst = (eidx // per).long()                                            # [S, K]
-    ranks = torch.arange(world, device=dev).view(world, 1, 1)
-    mine = dst.unsqueeze(0) == ranks                                      # [world, S, K]
-    loc_e = torch.where(mine, (eidx.unsqueeze(0) - ranks * per).to(torch.int32),
-                        torch.full((), -1, dtype=torch.int32, device=dev))
-    loc_w = torch.where(mine, ewt.unsqueeze(0), torch.zeros((), dtype=ewt.dtype, device=dev))
     # one byte row per (destination, token): q8 codes | block scales | local ids | weights
-    tok = torch.cat([xq.view(torch.uint8), xs.contiguous().view(torch.uint8)], dim=1)  # [S, D + 4 nb]
-    payload = torch.cat([tok.unsqueeze(0).expand(world, S, tok.shape[1]),
-                         loc_e.view(torch.uint8).view(world, S, 4 * K),
-                         loc_w.contiguous().view(torch.uint8).view(world, S, 4 * K)], dim=2).contiguous()
-    recv = torch.empty_like(payload)
-    dist.all_to_all_single(recv.view(world, -1), payload.view(world, -1), group=group)
-    recv = recv.view(world * S, -1)
-    nb = xs.shape[1]
-    r_xq = recv[:, :D].contiguous().view(torch.int8)
-    r_xs = recv[:, D:D + 4 * nb].contiguous().view(torch.float32)
-    r_e = recv[:, D + 4 * nb:D + 4 * nb + 4 * K].contiguous().view(torch.int32)
-    r_w = recv[:, D + 4 * nb + 4 * K:].contiguous().view(torch.float32)
+    if dev.type == "cuda":  # one pack and one unpack kernel (zz_ep_pack_dev / zz_ep_unpack_dev)
+        import zunzuncito_b200 as zz
+        payload = zz.ep_pack(xq, xs.contiguous(), eidx.to(torch.int32).contiguous(), ewt.contiguous(), world, per)
+        recv = torch.empty_like(payload)
+        dist.all_to_all_single(recv.view(world, -1), payload.view(world, -1), group=group)
+        r_xq, r_xs, r_e, r_w = zz.ep_unpack(recv, D, K)
+    else:
+        r_xq, r_xs, r_e, r_w = _exchange_torch(xq, xs, eidx, ewt, world, per, group)
     part = local_ffn(r_xq, r_xs, r_e, r_w).contiguous()                  # [world * S, D]
+    # combine: token s of rank r is the sum over destinations of their slot (r, s), i.e. a
+    # reduce-scatter of the slot-major partial rows (summed inside the collective)
+    if dev.type == "cuda":
+        out = torch.empty((S, D), dtype=part.dtype, device=dev)
+        dist.reduce_scatter_tensor(out, part, group=group)
+        return out
     back = torch.empty_like(part)
     dist.all_to_all_single(back.view(world, -1), part.view(world, -1), group=group)
     return back.view(world, S, D).sum(0)
