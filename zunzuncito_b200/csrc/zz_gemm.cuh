@@ -197,14 +197,12 @@ struct GemmSmem {
 // S8: int8 tensor-core path (m16n8k32.s8, int8 activations in shared memory, int32
 // block sums converted to fp32); else the fp16-exact path described above.
 template <int FMT, int BN, int EPI, bool B_HALF, bool S8 = false>
-__global__ void __launch_bounds__(G_THREADS) k_gemm(GemmArgs a) {
+__device__ __forceinline__ void gemm_item(const GemmArgs &a, int item_idx) {
     using T = FmtTraits<FMT>;
     using L = GemmSmem<FMT, BN, B_HALF>;
     extern __shared__ __align__(128) uint8_t smem[];
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, t = lane & 3;
 
-    const int item_idx = blockIdx.y;
-    if (a.n_items && item_idx >= *a.n_items) return;
     WorkItem it;
     if (a.items) {
         it = a.items[item_idx];
@@ -533,6 +531,22 @@ __global__ void __launch_bounds__(G_THREADS) k_gemm(GemmArgs a) {
                         atomicAdd(a.out + (size_t)tok * a.O + o + k, w * v);
                     }
             }
+        }
+    }
+}
+
+// One work item per grid row; with STRIDE the items are strided over grid.y instead (a
+// grid capped below the worst-case item count then launches no CTA that finds no item;
+// the loop costs a few registers, so exact grids use the plain form).
+template <int FMT, int BN, int EPI, bool B_HALF, bool S8 = false, bool STRIDE = false>
+__global__ void __launch_bounds__(G_THREADS) k_gemm(GemmArgs a) {
+    const int n = a.n_items ? *a.n_items : (int)gridDim.y;
+    if constexpr (!STRIDE) {
+        if ((int)blockIdx.y < n) gemm_item<FMT, BN, EPI, B_HALF, S8>(a, blockIdx.y);
+    } else {
+        for (int y = blockIdx.y; y < n; y += gridDim.y) {
+            gemm_item<FMT, BN, EPI, B_HALF, S8>(a, y);
+            __syncthreads();  // shared memory is reused by the next item
         }
     }
 }

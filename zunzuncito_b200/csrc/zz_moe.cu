@@ -69,19 +69,38 @@ constexpr int DENSE_BN = 64;
 
 static inline size_t a256(size_t n) { return (n + 255) & ~(size_t)255; }
 
-template <int FMT, int BN, int EPI, bool BH, bool S8>
-static int launch_gemm_t(const GemmArgs &a, dim3 grid, cudaStream_t st) {
+template <int FMT, int BN, int EPI, bool BH, bool S8, bool STRIDE>
+static int launch_gemm_k(const GemmArgs &a, dim3 grid, cudaStream_t st) {
     constexpr int smem = GemmSmem<FMT, BN, BH>::TOTAL;
     static bool attr_set = false;  // per process; the library drives one device
     if (!attr_set) {
-        if (!check_cuda(cudaFuncSetAttribute(k_gemm<FMT, BN, EPI, BH, S8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             smem),
+        if (!check_cuda(cudaFuncSetAttribute(k_gemm<FMT, BN, EPI, BH, S8, STRIDE>,
+                                             cudaFuncAttributeMaxDynamicSharedMemorySize, smem),
                         "gemm smem attribute"))
             return 0;
         attr_set = true;
     }
-    k_gemm<FMT, BN, EPI, BH, S8><<<grid, G_THREADS, smem, st>>>(a);
+    k_gemm<FMT, BN, EPI, BH, S8, STRIDE><<<grid, G_THREADS, smem, st>>>(a);
     return check_cuda(cudaGetLastError(), "gemm launch");
+}
+
+// grid.y = the worst-case item count, or fewer rows and the striding kernel when that
+// count exceeds about eight waves of 4 CTAs per SM (k_gemm finds the real count on the
+// device; the worst case counts every routing slot, valid or not)
+template <int FMT, int BN, int EPI, bool BH, bool S8>
+static int launch_gemm_t(const GemmArgs &a, dim3 grid, cudaStream_t st) {
+    static int sms = 0;
+    if (!sms) {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms <= 0) sms = 148;
+    }
+    const unsigned cap = (unsigned)(sms * 4 * 8 / (grid.x > 0 ? (int)grid.x : 1));
+    if (a.n_items && cap > 0 && grid.y > cap) {
+        grid.y = cap;
+        return launch_gemm_k<FMT, BN, EPI, BH, S8, true>(a, grid, st);
+    }
+    return launch_gemm_k<FMT, BN, EPI, BH, S8, false>(a, grid, st);
 }
 
 template <int EPI, int BN, bool BH, bool S8 = false>
