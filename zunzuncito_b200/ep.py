@@ -195,12 +195,12 @@ def bench_main(a, rank, world, clock_sampler=None):
                 "scaling": "weak", "vs_baseline": None, "dtype": "int8", "data": "synthetic",
                 "config": {"workload": f"Gemma-4 batch-union MoE stack, {L} layers x 128 q4_0 experts sharded "
                                        f"{per}/GPU, S={S} tokens per GPU per step, top-8 Zipf(1.1), NCCL all-to-all "
-                                       "of q8_0 rows", "tokens_per_gpu": S, "layers": L, "parallelism": f"ep{world}",
+                                       "of q8_0 rows, reduce-scatter combine", "tokens_per_gpu": S, "layers": L, "parallelism": f"ep{world}",
                            "l2": "no flush: per-layer expert reads exceed L2", "timing": mode},
                 "clocks": sampler.summary() if sampler else None,
                 "e2e": {"value": S * world * L / (ems / 1e3), "unit": "token-layers/s",
                         "h2d_bytes_per_step": world * L * (S * D * 4 + S * K * 8),
                         "d2h_bytes_per_step": world * L * S * D * 4},
-                "gpu_launches": a.steps * L * 5}
+                "gpu_launches": a.steps * L * 6}  # quant, pack, unpack, route, gate/up, down
         print(json.dumps(line), flush=True)
     dist.destroy_process_group()
