@@ -356,6 +356,21 @@ extern "C" size_t zz_moe_workspace_offset(const zz_expert_bank *b, int S, int K,
     return (size_t)((const uint8_t *)p - base);
 }
 
+// A side stream (one per host thread) on which the routing kernel runs concurrently with
+// the activation quantization: fork and join by events, so it is stream-ordered with
+// the caller's stream and capturable into a CUDA graph.
+struct SideStream {
+    cudaStream_t s = nullptr;
+    cudaEvent_t fork = nullptr, join = nullptr;
+    bool ok() {
+        if (s) return true;
+        return cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking) == cudaSuccess &&
+               cudaEventCreateWithFlags(&fork, cudaEventDisableTiming) == cudaSuccess &&
+               cudaEventCreateWithFlags(&join, cudaEventDisableTiming) == cudaSuccess;
+    }
+};
+static thread_local SideStream g_side;
+
 // X != NULL: f32 rows quantized here; else xq/xs are q8_0 rows given by the caller.
 static int moe_impl(const zz_expert_bank *b, const float *X, const int8_t *xq_in, const float *xs_in,
                     const int32_t *eidx, const float *ewt, float *OUT, int S, int K, int act, float clamp,
@@ -389,6 +404,15 @@ static int moe_impl(const zz_expert_bank *b, const float *X, const int8_t *xq_in
     const bool tcp = eng == ENG_TC || tcw;  // engines on tcgen05 (pair-ordered fp16 rows)
     const int8_t *xq = xq_in;
     const float *xs = xs_in;
+    // routing (eidx/ewt only) on the side stream, overlapping the quantization
+    if (!g_side.ok()) return fail("zz_moe_ffn: side stream");
+    if (!check_cuda(cudaEventRecord(g_side.fork, st), "fork") || !check_cuda(cudaStreamWaitEvent(g_side.s, g_side.fork, 0), "fork wait"))
+        return 0;
+    k_route<<<1, 1024, 4 * E * sizeof(int), g_side.s>>>(eidx, ewt, P, E,
+                                                        tcw ? TCW_BN : tcp ? TC_BN : eng == ENG_DEC ? DEC_BN : MOE_BN,
+                                                        (int)w.cap, w.pair_src, w.pair_w, w.items, w.n_items, w.tcerr);
+    if (!check_cuda(cudaGetLastError(), "route launch")) return 0;
+    if (!check_cuda(cudaEventRecord(g_side.join, g_side.s), "join")) return 0;
     if (X) {
         const bool want_h = eng == ENG_MMA || tcp;  // engines reading fp16 activations
         if (!launch_quant_act(X, S, D, w.xq, w.xs, fmt == GPU_FMT_TQ2 ? w.xsx : nullptr, want_h ? w.xh : nullptr, st,
@@ -401,9 +425,7 @@ static int moe_impl(const zz_expert_bank *b, const float *X, const int8_t *xq_in
         if (fmt == GPU_FMT_TQ2) k_rows_sx<<<(S + 127) / 128, 128, 0, st>>>(xq, xs, S, D, w.xsx);
         if ((eng == ENG_MMA || tcp) && !launch_s8_to_h(xq, w.xh, (long)S * D, st)) return 0;
     }
-    k_route<<<1, 1024, 4 * E * sizeof(int), st>>>(eidx, ewt, P, E, tcw ? TCW_BN : tcp ? TC_BN : eng == ENG_DEC ? DEC_BN : MOE_BN,
-                                                  (int)w.cap, w.pair_src, w.pair_w, w.items, w.n_items, w.tcerr);
-    if (!check_cuda(cudaGetLastError(), "route launch")) return 0;
+    if (!check_cuda(cudaStreamWaitEvent(st, g_side.join, 0), "join wait")) return 0;
     if (tcp) {
         k_gather_rows<<<(unsigned)w.cap, 128, 0, st>>>(w.pair_src, K, (int)w.cap, w.xh, xs, D, w.xg, w.xsT, (int)w.ldT);
         if (!check_cuda(cudaGetLastError(), "gather launch")) return 0;
