@@ -458,6 +458,58 @@ def sub_benchmarks(zz, torch, synth, stream, banks, hbm_peak):
                                  "ms_per_layer": ms, "tok_per_s": S4 / (ms / 1e3)}
     for b in banks[:2]:
         b._ws = None
+    res.update(maple_tq2(zz, torch, synth, stream, hbm_peak))
+    return res
+
+
+def tq2_bank_dev(zz, torch, E, D, MI, gen):
+    """E Maple-shaped tq2 experts generated on the device: codes uniform in {0,1,2}
+    (weights -1/0/+1, P(0) = 1/3), alpha |N(0,0.02)| + 1e-3, packed as tq2.h:46-51"""
+    def tensor(O, I):
+        c = torch.randint(0, 3, (E, O, I // 64, 4, 16), generator=gen, device="cuda", dtype=torch.uint8)
+        b = c[:, :, :, 0] | (c[:, :, :, 1] << 2) | (c[:, :, :, 2] << 4) | (c[:, :, :, 3] << 6)
+        al = torch.randn((E, O), generator=gen, device="cuda").abs() * 0.02 + 1e-3
+        return torch.cat([al.view(torch.uint8).view(E, -1), b.reshape(E, -1)], dim=1)
+    blobs = torch.cat([tensor(MI, D), tensor(MI, D), tensor(D, MI)], dim=1).contiguous()
+    return zz.ExpertBankDev(zz.GPU_FMT_TQ2, blobs, D, MI)
+
+
+def maple_tq2(zz, torch, synth, stream, hbm_peak):
+    """Maple-shaped ternary MoE layer (256 tq2 experts, D 2048, inter
+    512, top-8, clamped SwiGLU), decode (S=1) and S=512."""
+    D, MI, E, K, CL = synth.MAPLE_D, synth.MAPLE_MI, synth.MAPLE_E, synth.MAPLE_K, synth.MAPLE_CLAMP
+    per_expert = zz.expert_blob_bytes(zz.GPU_FMT_TQ2, D, MI)   # 798,720 B
+    gen = torch.Generator(device="cuda").manual_seed(4321)
+    banks = [tq2_bank_dev(zz, torch, E, D, MI, gen) for _ in range(4)]  # 4 x 204 MB > L2
+    act = zz.ZZ_ACT_SWIGLU_CLAMP
+    res = {}
+    # S=512 on one bank (each layer call reads its ~200 MB of distinct experts)
+    S = 512
+    r = synth.zipf_routing(31, S, E, K)
+    X = torch.from_numpy(synth.gaussian(32, (S, D))).cuda()
+    e, w = torch.from_numpy(r[0]).cuda(), torch.from_numpy(r[1]).cuda()
+    out = torch.empty((S, D), device="cuda")
+    banks[0].workspace(S, K)
+    ms = timed(torch, lambda: zz.moe_ffn(banks[0], X, e, w, act, CL, out=out), 10, 3, stream)
+    distinct = len(np.unique(r[0]))
+    res["maple_tq2_layer_s512"] = {"unit": "ms per layer", "value": ms, "tok_per_s": S / (ms / 1e3),
+                                   "hbm_gbs": distinct * per_expert / (ms / 1e3) / 1e9, "distinct_experts": distinct}
+    # decode: one token, 8 of 256 experts per layer, 4 layers (distinct banks) per graph replay
+    rs = [synth.zipf_routing(40 + l, 1, E, K) for l in range(4)]
+    X1 = torch.from_numpy(synth.gaussian(41, (1, D))).cuda()
+    es = [torch.from_numpy(x[0]).cuda() for x in rs]
+    ws = [torch.from_numpy(x[1]).cuda() for x in rs]
+    o1 = torch.empty((1, D), device="cuda")
+    for b in banks:
+        b.workspace(1, K)
+
+    def four():
+        for l in range(4):
+            zz.moe_ffn(banks[l], X1, es[l], ws[l], act, CL, out=o1)
+    ms1 = graph_timed(torch, four, 20, 3) / 4
+    res["maple_tq2_decode"] = {"unit": "us per layer", "value": ms1 * 1e3,
+                               "hbm_gbs": K * per_expert / (ms1 / 1e3) / 1e9, "launch": "cuda graph of 4 layers"}
+    del banks
     return res
 
 
