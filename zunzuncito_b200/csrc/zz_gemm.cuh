@@ -284,16 +284,20 @@ __device__ __forceinline__ void gemm_item(const GemmArgs &a, int item_idx) {
             const uint8_t *src = xbase + (size_t)col_xrow[n] * xrow_bytes + (size_t)b0 * (B_HALF ? 64 : 32) + p * 16;
             cp_async16_zfill(sb + n * L::B_STRIDE + p * 16, ok ? (const void *)src : (const void *)xbase, ok);
         }
-        // activation scales, stored [block][column] so a column pair is one 8-byte load
+        // activation scales per block: fp16 path [block][column] (a column pair is one
+        // 8-byte load); int8 path [block][t][tile][pair], so the 2*NT scales of the column
+        // pairs (8j + 2t, 8j + 2t + 1) one thread uses in a block are 16-byte loads
         for (int i = tid; i < BN * G_BKB; i += G_THREADS) {
             int n = i / G_BKB, k = i % G_BKB;
             bool ok = n < ncols && k < nbk;
             const float *src = a.xs + (size_t)col_xrow[n] * nb + b0 + k;
-            cp_async4_zfill(sbs + (k * BN + n) * 4, ok ? (const void *)src : (const void *)a.xs, ok);
+            const int pos = S8 ? ((n % 8) / 2) * (2 * (BN / 8)) + (n / 8) * 2 + (n % 2) : n;
+            cp_async4_zfill(sbs + (k * BN + pos) * 4, ok ? (const void *)src : (const void *)a.xs, ok);
         }
     };
 
     constexpr int NT = BN / 8;
+    static_assert(!S8 || NT % 2 == 0, "int8 path pairs n8 tiles");
     float2 acc[NT][2];  // [n8 tile][row g | row g+8] x column pair (2t, 2t+1)
 #pragma unroll
     for (int j = 0; j < NT; j++) acc[j][0] = acc[j][1] = make_float2(0.f, 0.f);
@@ -347,22 +351,37 @@ __device__ __forceinline__ void gemm_item(const GemmArgs &a, int item_idx) {
                 dw0 = make_float2(w0, w0);
                 dw1 = make_float2(w1, w1);
             }
+            // this thread's activation scales of the block: column pairs 8j + 2t (+1)
+            float dxv[2 * NT];
 #pragma unroll
-            for (int j = 0; j < NT; j++) {
-                if (j < jv) {
-                    const uint8_t *pb = sb + (j * 8 + g) * L::B_STRIDE + kb * 32 + 4 * t;
-                    int c[4];
-                    mma_s8(c, a0, a1, a2, a3, *reinterpret_cast<const uint32_t *>(pb),
-                           *reinterpret_cast<const uint32_t *>(pb + 16));
-                    const float2 dx = *reinterpret_cast<const float2 *>(sbs + kb * BN + j * 8 + 2 * t);
-                    const float2 d01 = make_float2((float)c[0], (float)c[1]), d23 = make_float2((float)c[2], (float)c[3]);
-                    if (T::HAS_WSCALE) {
-                        acc[j][0] = ffma2(fmul2(dw0, dx), d01, acc[j][0]);
-                        acc[j][1] = ffma2(fmul2(dw1, dx), d23, acc[j][1]);
-                    } else {
-                        acc[j][0] = ffma2(dx, d01, acc[j][0]);
-                        acc[j][1] = ffma2(dx, d23, acc[j][1]);
-                    }
+            for (int q4 = 0; q4 < NT / 2; q4++) {
+                const float4 v = *reinterpret_cast<const float4 *>(sbs + kb * BN + t * 2 * NT + 4 * q4);
+                dxv[4 * q4] = v.x; dxv[4 * q4 + 1] = v.y; dxv[4 * q4 + 2] = v.z; dxv[4 * q4 + 3] = v.w;
+            }
+            auto tile = [&](int j, uint32_t b0, uint32_t b1) {
+                int c[4];
+                mma_s8(c, a0, a1, a2, a3, b0, b1);
+                const float2 dx = make_float2(dxv[2 * j], dxv[2 * j + 1]);
+                const float2 d01 = make_float2((float)c[0], (float)c[1]), d23 = make_float2((float)c[2], (float)c[3]);
+                if (T::HAS_WSCALE) {
+                    acc[j][0] = ffma2(fmul2(dw0, dx), d01, acc[j][0]);
+                    acc[j][1] = ffma2(fmul2(dw1, dx), d23, acc[j][1]);
+                } else {
+                    acc[j][0] = ffma2(dx, d01, acc[j][0]);
+                    acc[j][1] = ffma2(dx, d23, acc[j][1]);
+                }
+            };
+            // B fragments of two n8 tiles per ldmatrix.x4: matrices (tile jp, k 0-15),
+            // (jp, k 16-31), (jp+1, k 0-15), (jp+1, k 16-31); lane l addresses row l % 8
+            // of matrix l / 8, and receives row g, bytes 4t..4t+3 of each
+#pragma unroll
+            for (int jp = 0; jp < NT; jp += 2) {
+                if (jp < jv) {
+                    uint32_t b0, b1, b2, b3;
+                    const int lrow = (jp + (lane >> 4)) * 8 + (lane & 7);
+                    ldsm_x4(b0, b1, b2, b3, sb + lrow * L::B_STRIDE + kb * 32 + ((lane >> 3) & 1) * 16);
+                    tile(jp, b0, b1);
+                    if (jp + 1 < jv) tile(jp + 1, b2, b3);
                 }
             }
         };
