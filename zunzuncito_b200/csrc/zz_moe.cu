@@ -85,7 +85,7 @@ static int launch_gemm_k(const GemmArgs &a, dim3 grid, cudaStream_t st) {
 }
 
 // grid.y = the worst-case item count, or fewer rows and the striding kernel when that
-// count exceeds about eight waves of 4 CTAs per SM (k_gemm finds the real count on the
+// count exceeds about sixteen waves of 4 CTAs per SM (k_gemm finds the real count on the
 // device; the worst case counts every routing slot, valid or not)
 template <int FMT, int BN, int EPI, bool BH, bool S8>
 static int launch_gemm_t(const GemmArgs &a, dim3 grid, cudaStream_t st) {
@@ -95,7 +95,7 @@ static int launch_gemm_t(const GemmArgs &a, dim3 grid, cudaStream_t st) {
         cudaGetDevice(&dev);
         if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms <= 0) sms = 148;
     }
-    const unsigned cap = (unsigned)(sms * 4 * 8 / (grid.x > 0 ? (int)grid.x : 1));
+    const unsigned cap = (unsigned)(sms * 4 * 16 / (grid.x > 0 ? (int)grid.x : 1));
     if (a.n_items && cap > 0 && grid.y > cap) {
         grid.y = cap;
         return launch_gemm_k<FMT, BN, EPI, BH, S8, true>(a, grid, st);
