@@ -162,18 +162,44 @@ def bench_main(a, rank, world, clock_sampler=None):
     eh = [torch.from_numpy(r[0]).pin_memory() for r in routes]
     wh = [torch.from_numpy(r[1]).pin_memory() for r in routes]
     oh = torch.empty((L, S, D), dtype=torch.float32).pin_memory()
-    Xd = torch.empty((S, D), device="cuda")
-    ed = torch.empty((S, K), dtype=torch.int32, device="cuda")
-    wd = torch.empty((S, K), device="cuda")
+    # two buffer sets: the next layer's inputs copy in and the previous layer's output
+    # copies out on their own streams while a layer computes (every copy in the timed region)
+    Xd = [torch.empty((S, D), device="cuda") for _ in range(2)]
+    ed = [torch.empty((S, K), dtype=torch.int32, device="cuda") for _ in range(2)]
+    wd = [torch.empty((S, K), device="cuda") for _ in range(2)]
+    h2d, d2h = torch.cuda.Stream(), torch.cuda.Stream()
 
     def step_e2e():
+        comp = torch.cuda.current_stream()
+        h2d.wait_stream(comp)
+        d2h.wait_stream(comp)
+        computed, copied_out, outs = [None, None], [None, None], [None, None]
         for l in range(L):
-            Xd.copy_(Xh, non_blocking=True)
-            ed.copy_(eh[l], non_blocking=True)
-            wd.copy_(wh[l], non_blocking=True)
-            xq, xs, _ = zz.quant_act(Xd)
-            ffn = lambda q, s, e, w, b=banks[l]: zz.moe_ffn_q8(b, q, s, e, w, zz.ZZ_ACT_GEGLU_TANH)
-            oh[l].copy_(ep_moe_layer(xq, xs, ed, wd, E, ffn), non_blocking=True)
+            b = l % 2
+            with torch.cuda.stream(h2d):
+                if computed[b] is not None:
+                    h2d.wait_event(computed[b])
+                Xd[b].copy_(Xh, non_blocking=True)
+                ed[b].copy_(eh[l], non_blocking=True)
+                wd[b].copy_(wh[l], non_blocking=True)
+                inp = torch.cuda.Event()
+                inp.record(h2d)
+            comp.wait_event(inp)
+            if copied_out[b] is not None:
+                comp.wait_event(copied_out[b])
+            xq, xs, _ = zz.quant_act(Xd[b])
+            ffn = lambda q, s, e, w, bk=banks[l]: zz.moe_ffn_q8(bk, q, s, e, w, zz.ZZ_ACT_GEGLU_TANH)
+            outs[b] = ep_moe_layer(xq, xs, ed[b], wd[b], E, ffn)
+            computed[b] = torch.cuda.Event()
+            computed[b].record(comp)
+            with torch.cuda.stream(d2h):
+                d2h.wait_event(computed[b])
+                oh[l].copy_(outs[b], non_blocking=True)
+                outs[b].record_stream(d2h)
+                copied_out[b] = torch.cuda.Event()
+                copied_out[b].record(d2h)
+        comp.wait_stream(h2d)
+        comp.wait_stream(d2h)
 
     step_e2e()
     torch.cuda.synchronize()
