@@ -328,11 +328,15 @@ __device__ __forceinline__ void gemm_item(const GemmArgs &a, int item_idx) {
             uint32_t a0, a1, a2, a3;
             const uint8_t *r0 = sa + rA * T::A_STRIDE, *r1 = r0 + 8 * T::A_STRIDE;
             if (FMT == GPU_FMT_Q40) {
-                // the q4_0 byte layout is the fragment split: low nibbles k, high k+16
+                // the q4_0 byte layout is the fragment split: low nibbles k, high k+16.
+                // Each nibble q goes to the high half of its byte xor 8: the signed byte is
+                // then 16 (q - 8) exactly (one op for a high nibble, two for a low one); the
+                // factor 16 leaves through the weight scale dw / 16 (a power of two, so
+                // every product and rounding below is the same as with q - 8 and dw).
                 uint32_t w0 = *reinterpret_cast<const uint32_t *>(r0 + kb * 16 + 4 * t);
                 uint32_t w1 = *reinterpret_cast<const uint32_t *>(r1 + kb * 16 + 4 * t);
-                a0 = nib_to_s8(w0); a2 = nib_to_s8(w0 >> 4);
-                a1 = nib_to_s8(w1); a3 = nib_to_s8(w1 >> 4);
+                a0 = ((w0 << 4) & 0xF0F0F0F0u) ^ 0x80808080u; a2 = (w0 & 0xF0F0F0F0u) ^ 0x80808080u;
+                a1 = ((w1 << 4) & 0xF0F0F0F0u) ^ 0x80808080u; a3 = (w1 & 0xF0F0F0F0u) ^ 0x80808080u;
             } else if (FMT == GPU_FMT_Q80) {
                 const uint8_t *p0 = r0 + kb * 32 + 4 * t, *p1 = r1 + kb * 32 + 4 * t;
                 a0 = *reinterpret_cast<const uint32_t *>(p0); a2 = *reinterpret_cast<const uint32_t *>(p0 + 16);
@@ -348,6 +352,7 @@ __device__ __forceinline__ void gemm_item(const GemmArgs &a, int item_idx) {
             if (T::HAS_WSCALE) {
                 const __half *hs = reinterpret_cast<const __half *>(sas);
                 float w0 = __half2float(hs[rA * G_BKB + kb]), w1 = __half2float(hs[(rA + 8) * G_BKB + kb]);
+                if (FMT == GPU_FMT_Q40) { w0 *= 0.0625f; w1 *= 0.0625f; }  // codes carry 16 (q - 8)
                 dw0 = make_float2(w0, w0);
                 dw1 = make_float2(w1, w1);
             }
