@@ -61,3 +61,20 @@ def test_bad_arguments_decline_before_device_work():
     assert zz.lib.zz_matvec_dev(ctypes.byref(t), None, None, None, None, 1, None) == 0
     assert b"invalid" in zz.lib.gpu_last_error()
     assert zz.lib.zz_quant_act_dev(None, 1, 48, None, None, None, None) == 0
+
+
+def test_ep_exchange_entries_host_checks():
+    """the expert-parallel row layout size, and argument checks that decline before any
+    device work"""
+    assert zz.lib.zz_ep_row_bytes(2816, 8) == 2816 + 88 * 4 + 8 * 8   # 3232
+    assert zz.lib.zz_ep_row_bytes(2048, 8) == 2048 + 64 * 4 + 64
+    p = ctypes.c_void_p(16)
+    assert zz.lib.zz_ep_pack_dev(p, p, p, p, 4, 33, 8, 2, 64, p, None) == 0          # D % 32
+    assert b"bad shape" in zz.lib.gpu_last_error()
+    assert zz.lib.zz_ep_pack_dev(p, p, p, p, 4, 64, 8, 0, 64, p, None) == 0          # world 0
+    assert zz.lib.zz_ep_pack_dev(None, p, p, p, 4, 64, 8, 2, 64, p, None) == 0       # null
+    assert b"null" in zz.lib.gpu_last_error()
+    assert zz.lib.zz_ep_pack_dev(ctypes.c_void_p(18), p, p, p, 4, 64, 8, 2, 64, p, None) == 0  # alignment
+    assert zz.lib.zz_ep_pack_dev(None, None, None, None, 0, 64, 8, 2, 64, None, None) == 1   # S = 0: nothing
+    assert zz.lib.zz_ep_unpack_dev(p, 3, 64, 0, p, p, p, p, None) == 0                # K <= 0
+    assert zz.lib.zz_ep_unpack_dev(p, 0, 64, 8, p, p, p, p, None) == 1                # R = 0: nothing
