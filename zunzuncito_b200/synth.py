@@ -7,7 +7,7 @@ import numpy as np
 
 # Gemma-4 26B-A4B routed experts (tools/convert_gemma4.py:21-23)
 GEMMA_D, GEMMA_MI, GEMMA_E, GEMMA_K = 2816, 704, 128, 8
-# Maple ternary experts (tests/test_metal_sim.c:158-160; README.md:12)
+# Maple ternary experts (reference tests/test_metal_sim.c:158-160 and its README.md:12)
 MAPLE_D, MAPLE_MI, MAPLE_E, MAPLE_K, MAPLE_CLAMP = 2048, 512, 256, 8, 7.0
 
 
