@@ -505,7 +505,7 @@ def tq2_bank_dev(zz, torch, E, D, MI, gen):
 
 
 def maple_tq2(zz, torch, synth, stream, hbm_peak):
-    """BASELINE config 3: Maple-shaped ternary MoE layer (256 tq2 experts, D 2048, inter
+    """BASELINE config 4: Maple-shaped ternary MoE layer (256 tq2 experts, D 2048, inter
     512, top-8, clamped SwiGLU), decode (S=1) and S=512."""
     D, MI, E, K, CL = synth.MAPLE_D, synth.MAPLE_MI, synth.MAPLE_E, synth.MAPLE_K, synth.MAPLE_CLAMP
     per_expert = zz.expert_blob_bytes(zz.GPU_FMT_TQ2, D, MI)   # 798,720 B
