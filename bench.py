@@ -210,8 +210,8 @@ def cpu_baseline_moe(host_blobs, S, seed):
         cores = lib.max_threads()
     else:
         lib, kind, cores = oracle.Oracle(), "port", 1
-    X = synth.gaussian(seed, (S, D))
-    eidx, ewt, _ = synth.zipf_routing(seed + 1, S, E, K)
+    X = synth.gaussian(7, (S, D))
+    eidx, ewt = routing(synth, 1, S, seed=99)[0]     # the timed stack's layer-0 inputs
     lib.moe_layer(0, host_blobs, X, eidx, ewt, D, MI)   # warm-up (threads, pages)
     n, t0 = 0, time.perf_counter()
     while True:   # a bounded sample of about 10 s of CPU work
@@ -247,8 +247,9 @@ def run_reference_arm(a, rank):
     for off, rows, nb in [(0, 2 * MI, D // 32), (2 * MI * (D // 32) * 18, D, MI // 32)]:
         v = blobs[:, off:off + rows * nb * 18].reshape(E, rows * nb, 18)
         v[:, :, 0:2] = np.frombuffer(np.full(E * rows * nb, 0.002, np.float16).tobytes(), np.uint8).reshape(E, -1, 2)
-    X = synth.gaussian(6, (S, D))
-    eidx, ewt, _ = synth.zipf_routing(7, S, E, K)
+    # the GPU arm's layer-0 inputs: the same X (seed 7) and the same seeded routing (seed 99)
+    X = synth.gaussian(7, (S, D))
+    eidx, ewt = routing(synth, 1, S, seed=99)[0]
     times = []
     for i in range(a.warmup + a.steps):
         t = time.perf_counter()

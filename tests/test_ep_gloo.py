@@ -86,3 +86,28 @@ def test_ep_rank_failure_is_reported(tmp_path):
     assert (tmp_path / "err1.txt").exists()
     assert (tmp_path / "err0.txt").exists()
     assert not (tmp_path / "out0.npy").exists()
+
+
+def _uneven_worker(rank, world, port, out_dir):
+    from zunzuncito_b200.ep import ep_moe_layer
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=20))
+    try:
+        xq = torch.zeros((S, D), dtype=torch.int8)
+        xs = torch.zeros((S, D // 32))
+        eidx = torch.zeros((S, K), dtype=torch.int32)
+        ewt = torch.zeros((S, K))
+        ep_moe_layer(xq, xs, eidx, ewt, 7, lambda *a: None)   # 7 experts over 2 ranks
+    except ValueError as e:
+        with open(os.path.join(out_dir, f"val{rank}.txt"), "w") as f:
+            f.write(str(e))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_ep_rejects_uneven_expert_split(tmp_path):
+    """experts that do not divide over the ranks would leave the remainder on no rank
+    (their contributions silently dropped); the layer refuses before any exchange"""
+    mp.start_processes(_uneven_worker, args=(2, _port(), str(tmp_path)), nprocs=2, start_method="fork")
+    for r in range(2):
+        assert "shard evenly" in (tmp_path / f"val{r}.txt").read_text()

@@ -3,8 +3,10 @@
 The product is the C-ABI shared library ``libzz_cuda.so`` built from ``csrc/`` (its
 interface is ``include/zz_gpu.h``). This package only loads it and gives Python callers
 (tests, the benchmark, host-side plumbing such as the expert-parallel exchange) typed
-access to it. There is no CPU fallback: if the library is missing, importing the
-package raises.
+access to it. There is no CPU fallback: the first use of ``lib`` or of any device entry
+point loads the library and raises if it is missing. Importing the package alone (for
+example for ``zunzuncito_b200.synth``, the seeded input generators) loads nothing, so a
+CPU-only process such as the benchmark's reference arm never maps the product library.
 """
 import ctypes
 import os
@@ -81,7 +83,15 @@ def _load():
     return lib
 
 
-lib = _load()
+_lib = None
+
+
+def get_lib():
+    """libzz_cuda.so with every prototype set (loaded on first use)."""
+    global _lib
+    if _lib is None:
+        _lib = _load()
+    return _lib
 
 
 class ZZError(RuntimeError):
@@ -91,9 +101,24 @@ class ZZError(RuntimeError):
 def check(ok, what=""):
     """Raise with gpu_last_error() when an entry point declined (returned 0)."""
     if not ok:
-        msg = lib.gpu_last_error().decode()
+        msg = get_lib().gpu_last_error().decode()
         raise ZZError(f"{what}: {msg}" if what else msg)
     return ok
 
 
-from .api import *  # noqa: E402,F401,F403
+_API = None
+
+
+def __getattr__(name):
+    # PEP 562: `zz.lib` and the typed wrappers of api.py resolve on first use
+    global _API
+    if name == "lib":
+        return get_lib()
+    if name.startswith("__"):
+        raise AttributeError(name)
+    if _API is None:
+        import importlib
+        _API = importlib.import_module(__name__ + ".api")
+    if name in _API.__all__:
+        return getattr(_API, name)
+    raise AttributeError(f"module 'zunzuncito_b200' has no attribute {name!r}")

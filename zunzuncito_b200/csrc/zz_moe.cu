@@ -14,6 +14,7 @@
 //      epilogue (gemma4.c:647-651)
 // Each distinct expert's weights cross HBM once per item; items of one expert are
 // adjacent in the grid so repeated reads of the same expert hit L2.
+#include <atomic>
 #include <cstdlib>
 #include <cstring>
 #include <vector>
@@ -356,9 +357,11 @@ extern "C" size_t zz_moe_workspace_offset(const zz_expert_bank *b, int S, int K,
     return (size_t)((const uint8_t *)p - base);
 }
 
-// A side stream (one per host thread) on which the routing kernel runs concurrently with
-// the activation quantization: fork and join by events, so it is stream-ordered with
-// the caller's stream and capturable into a CUDA graph.
+// A side stream (one per host thread and device) on which the routing kernel runs
+// concurrently with the activation quantization: fork and join by events, so it is
+// stream-ordered with the caller's stream and capturable into a CUDA graph. Streams and
+// events belong to the device that was current when they were created, so each device
+// a thread drives gets its own set.
 struct SideStream {
     cudaStream_t s = nullptr;
     cudaEvent_t fork = nullptr, join = nullptr;
@@ -369,7 +372,23 @@ struct SideStream {
                cudaEventCreateWithFlags(&join, cudaEventDisableTiming) == cudaSuccess;
     }
 };
-static thread_local SideStream g_side;
+constexpr int MAX_DEVICES = 64;
+static thread_local SideStream g_side_dev[MAX_DEVICES];
+// the current device's side stream, or nullptr (error recorded)
+static SideStream *side_stream() {
+    int dev = 0;
+    if (!check_cuda(cudaGetDevice(&dev), "zz_moe_ffn: cudaGetDevice")) return nullptr;
+    if (dev < 0 || dev >= MAX_DEVICES) {
+        fail("zz_moe_ffn: device %d out of range", dev);
+        return nullptr;
+    }
+    SideStream *s = &g_side_dev[dev];
+    if (!s->ok()) {
+        fail("zz_moe_ffn: side stream");
+        return nullptr;
+    }
+    return s;
+}
 
 // X != NULL: f32 rows quantized here; else xq/xs are q8_0 rows given by the caller.
 static int moe_impl(const zz_expert_bank *b, const float *X, const int8_t *xq_in, const float *xs_in,
@@ -405,7 +424,9 @@ static int moe_impl(const zz_expert_bank *b, const float *X, const int8_t *xq_in
     const int8_t *xq = xq_in;
     const float *xs = xs_in;
     // routing (eidx/ewt only) on the side stream, overlapping the quantization
-    if (!g_side.ok()) return fail("zz_moe_ffn: side stream");
+    SideStream *side = side_stream();
+    if (!side) return 0;
+    SideStream &g_side = *side;
     if (!check_cuda(cudaEventRecord(g_side.fork, st), "fork") || !check_cuda(cudaStreamWaitEvent(g_side.s, g_side.fork, 0), "fork wait"))
         return 0;
     k_route<<<1, 1024, 4 * E * sizeof(int), g_side.s>>>(eidx, ewt, P, E,
@@ -515,7 +536,7 @@ static __device__ __align__(256) uint8_t g_noalloc_scratch[ZZ_NOALLOC_SCRATCH_BY
 
 // Device address of g_noalloc_scratch per device. Host code must not pass the symbol
 // itself to a kernel: on the host it is only a stand-in, not a device address.
-static void *g_noalloc_ptr[64];
+static std::atomic<void *> g_noalloc_ptr[MAX_DEVICES];
 
 extern "C" int zz_moe_ffn_noalloc_dev(const zz_expert_bank *b, const float *X, const int32_t *eidx,
                                       const float *ewt, float *OUT, int S, int K, int act, float clamp,
@@ -530,16 +551,18 @@ extern "C" int zz_moe_ffn_noalloc_dev(const zz_expert_bank *b, const float *X, c
                     S, K, need, (unsigned)ZZ_NOALLOC_SCRATCH_BYTES);
     int dev = 0;
     if (!check_cuda(cudaGetDevice(&dev), "zz_moe_ffn_noalloc_dev: cudaGetDevice")) return 0;
-    if (dev < 0 || dev >= 64) return fail("zz_moe_ffn_noalloc_dev: device %d out of range", dev);
-    if (!g_noalloc_ptr[dev]) {  // one-time set-up on this device, with it current
-        void *p = nullptr;
-        if (!check_cuda(cudaGetSymbolAddress(&p, g_noalloc_scratch), "zz_moe_ffn_noalloc_dev: cudaGetSymbolAddress"))
+    if (dev < 0 || dev >= MAX_DEVICES) return fail("zz_moe_ffn_noalloc_dev: device %d out of range", dev);
+    void *scratch = g_noalloc_ptr[dev].load(std::memory_order_acquire);
+    if (!scratch) {  // one-time set-up on this device, with it current
+        // Threads racing here all get the same address, so whichever store wins is right.
+        if (!check_cuda(cudaGetSymbolAddress(&scratch, g_noalloc_scratch),
+                        "zz_moe_ffn_noalloc_dev: cudaGetSymbolAddress"))
             return 0;
-        g_noalloc_ptr[dev] = p;
+        g_noalloc_ptr[dev].store(scratch, std::memory_order_release);
     }
     // Nothing in the scratch needs to start at zero: OUT is cleared by the layer itself
     // and the routing counters live in shared memory.
-    return moe_impl(b, X, nullptr, nullptr, eidx, ewt, OUT, S, K, act, clamp, g_noalloc_ptr[dev],
+    return moe_impl(b, X, nullptr, nullptr, eidx, ewt, OUT, S, K, act, clamp, scratch,
                     ZZ_NOALLOC_SCRATCH_BYTES, 0, stream);
 }
 

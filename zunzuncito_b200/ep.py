@@ -67,6 +67,8 @@ def ep_moe_layer(xq, xs, eidx, ewt, n_experts, local_ffn, group=None):
     dev = xq.device
     S, D = xq.shape
     K = eidx.shape[1]
+    if n_experts % world:
+        raise ValueError(f"{n_experts} experts do not shard evenly over {world} ranks")
     per = n_experts // world
     # one byte row per (destination, token): q8 codes | block scales | local ids | weights
     if dev.type == "cuda":  # one pack and one unpack kernel (zz_ep_pack_dev / zz_ep_unpack_dev)
