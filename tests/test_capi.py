@@ -78,3 +78,17 @@ def test_ep_exchange_entries_host_checks():
     assert zz.lib.zz_ep_pack_dev(None, None, None, None, 0, 64, 8, 2, 64, None, None) == 1   # S = 0: nothing
     assert zz.lib.zz_ep_unpack_dev(p, 3, 64, 0, p, p, p, p, None) == 0                # K <= 0
     assert zz.lib.zz_ep_unpack_dev(p, 0, 64, 8, p, p, p, p, None) == 1                # R = 0: nothing
+
+
+def test_lazy_load_names_match_api():
+    """the package resolves exactly api.__all__ lazily, and importing the package or its
+    CPU-side modules maps no CUDA library (the benchmark's reference arm relies on it)"""
+    import subprocess
+    import sys
+    from zunzuncito_b200 import api
+    assert set(api.__all__) == set(zz._API_NAMES)
+    code = ("import zunzuncito_b200, zunzuncito_b200.synth, zunzuncito_b200.ep; "
+            "print('libzz_cuda' in open('/proc/self/maps').read())")
+    out = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, check=True,
+                         cwd=os.path.dirname(os.path.dirname(HDR)))
+    assert out.stdout.strip() == "False"

@@ -107,6 +107,10 @@ def check(ok, what=""):
 
 
 _API = None
+# the public names of api.py (kept equal to its __all__; a CPU test checks that)
+_API_NAMES = frozenset(["ref_row_bytes", "ref_tensor_bytes", "expert_blob_bytes", "quant_act", "quant_rows",
+                        "QTensorDev", "matvec", "blocksums", "ExpertBankDev", "moe_ffn", "moe_ffn_q8",
+                        "alloc_aligned", "ep_pack", "ep_unpack"])
 
 
 def __getattr__(name):
@@ -114,8 +118,8 @@ def __getattr__(name):
     global _API
     if name == "lib":
         return get_lib()
-    if name.startswith("__"):
-        raise AttributeError(name)
+    if name not in _API_NAMES:   # submodules (synth, ep, ...) are imported by the import system
+        raise AttributeError(f"module 'zunzuncito_b200' has no attribute {name!r}")
     if _API is None:
         import importlib
         _API = importlib.import_module(__name__ + ".api")
