@@ -187,6 +187,31 @@ class Oracle(_Lib):
         return out
 
 
+    def moe_pairs_hidden(self, kind, blobs, X, eidx, D, MI, clamp=7.0):
+        """stage 1 for every routed pair: hq [S*K, MI] int8, hs [S*K, MI/32] f32"""
+        X = np.ascontiguousarray(X, np.float32)
+        S, K = eidx.shape
+        E = blobs.shape[0]
+        hq = np.zeros((S * K, MI), np.int8)
+        hs = np.zeros((S * K, MI // 32), np.float32)
+        ptrs = (_P * E)(*[blobs[e].ctypes.data for e in range(E)])
+        f = self.fn("moe_pairs_hidden", None, [_I, _P, _I, _P, _I, _I, _P, _I, _I, _F, _P, _P])
+        f(kind, ptrs, E, _ptr(X), S, K, _ptr(np.ascontiguousarray(eidx, np.int32)), D, MI, float(clamp),
+          _ptr(hq), _ptr(hs))
+        return hq, hs
+
+    def moe_pairs_combine(self, kind, blobs, hq, hs, eidx, ewt, D, MI):
+        """stage 2 from given per-pair hidden rows (pair p = s*K + k): OUT [S, D]"""
+        S, K = eidx.shape
+        E = blobs.shape[0]
+        out = np.zeros((S, D), np.float32)
+        ptrs = (_P * E)(*[blobs[e].ctypes.data for e in range(E)])
+        f = self.fn("moe_pairs_combine", None, [_I, _P, _I, _P, _P, _I, _I, _P, _P, _I, _I, _P])
+        f(kind, ptrs, E, _ptr(np.ascontiguousarray(hq, np.int8)), _ptr(np.ascontiguousarray(hs, np.float32)), S, K,
+          _ptr(np.ascontiguousarray(eidx, np.int32)), _ptr(np.ascontiguousarray(ewt, np.float32)), D, MI, _ptr(out))
+        return out
+
+
 class Reference(_Lib):
     """The reference's own kernels and engine routines (oracle/_ref/libzzref.so)."""
 

@@ -411,3 +411,86 @@ void orc_moe_layer_q8(int kind, const uint8_t *const *blobs, int E, const int8_t
     }
     free(X); free(xq); free(sx);
 }
+
+/* Stage 1 of the layer for every routed pair (s, k): the requantized hidden row the
+ * expert FFN hands to its down projection (gemma4.c:637-644; maple.c:653-660), hq [S*K][MI]
+ * int8 and hs [S*K][MI/32] (tq2: also the row's Sx sum via orc_tq2_quant_act). Pairs are
+ * independent, so they run in parallel; each pair's arithmetic is the scalar order. */
+void orc_moe_pairs_hidden(int kind, const uint8_t *const *blobs, int E, const float *X, int S, int K,
+                          const int *eidx, int D, int MI, float CL, int8_t *HQ, float *HS) {
+    int nbD = D / ORC_BLK, nbM = MI / ORC_BLK;
+    #pragma omp parallel for schedule(dynamic, 4)
+    for (int p = 0; p < S * K; p++) {
+        int s = p / K, e = eidx[p];
+        int8_t *hq = HQ + (size_t)p * MI;
+        float *hs = HS + (size_t)p * nbM;
+        if (e < 0 || e >= E) { memset(hq, 0, (size_t)MI); memset(hs, 0, sizeof(float) * nbM); continue; }
+        int8_t *xq = malloc((size_t)D);
+        float *sx = malloc(sizeof(float) * nbD), *h = malloc(sizeof(float) * (size_t)MI);
+        const uint8_t *blob = blobs[e];
+        if (kind == 3) {
+            size_t gate_b = (size_t)MI * 4 + (size_t)MI * (D / 4);
+            const uint8_t *G = blob, *U = blob + gate_b;
+            float tx = orc_tq2_quant_act(X + (size_t)s * D, xq, sx, D);
+            for (int o = 0; o < MI; o++) {
+                float g = orc_tq2_dot(G + MI * 4 + (size_t)o * (D / 4), ((const float *)G)[o], xq, sx, tx, D);
+                float u = orc_tq2_dot(U + MI * 4 + (size_t)o * (D / 4), ((const float *)U)[o], xq, sx, tx, D);
+                if (g > CL) g = CL;
+                u = u < -CL ? -CL : (u > CL ? CL : u);
+                h[o] = orc_silu(g) * u;
+            }
+            (void)orc_tq2_quant_act(h, hq, hs, MI);
+        } else {
+            int fmt = kind == 2 ? 2 : 1, bb = fmt == 2 ? ORC_Q80_BB : ORC_Q40_BB;
+            size_t grb = (size_t)nbD * bb, gate_b = grb * MI;
+            const uint8_t *G = blob, *U = blob + gate_b;
+            orc_quant_act(X + (size_t)s * D, xq, sx, D);
+            for (int o = 0; o < MI; o++) {
+                float g = fmt == 2 ? orc_q80_dot(G + o * grb, xq, sx, D) : orc_q40_dot(G + o * grb, xq, sx, D);
+                float u = fmt == 2 ? orc_q80_dot(U + o * grb, xq, sx, D) : orc_q40_dot(U + o * grb, xq, sx, D);
+                h[o] = kind == 0 ? orc_gelu_tanh(g) * u : orc_silu(g) * u;
+            }
+            orc_quant_act(h, hq, hs, MI);
+        }
+        free(xq); free(sx); free(h);
+    }
+}
+
+/* Stage 2 of the layer from given hidden rows: OUT[s] = sum_k ewt[s,k] * Down_e(hq[s*K+k])
+ * (gemma4.c:647-651, 792-806; maple.c:676-690), k in slot order. OUT zeroed first. */
+void orc_moe_pairs_combine(int kind, const uint8_t *const *blobs, int E, const int8_t *HQ, const float *HS,
+                           int S, int K, const int *eidx, const float *ewt, int D, int MI, float *OUT) {
+    int nbM = MI / ORC_BLK;
+    #pragma omp parallel for schedule(dynamic, 4)
+    for (int s = 0; s < S; s++) {
+        float *out = OUT + (size_t)s * D;
+        memset(out, 0, sizeof(float) * (size_t)D);
+        for (int k = 0; k < K; k++) {
+            int p = s * K + k, e = eidx[p];
+            if (e < 0 || e >= E) continue;
+            const int8_t *hq = HQ + (size_t)p * MI;
+            const float *hs = HS + (size_t)p * nbM;
+            float w = ewt[p];
+            const uint8_t *blob = blobs[e];
+            if (kind == 3) {
+                size_t gate_b = (size_t)MI * 4 + (size_t)MI * (D / 4);
+                const uint8_t *Dn = blob + 2 * gate_b;
+                double tot = 0;
+                for (int b = 0; b < nbM; b++) {
+                    int32_t t = 0;
+                    for (int j = 0; j < ORC_BLK; j++) t += hq[b * ORC_BLK + j];
+                    tot += (double)hs[b] * (double)t;
+                }
+                for (int o = 0; o < D; o++)
+                    out[o] += w * orc_tq2_dot(Dn + (size_t)D * 4 + (size_t)o * (MI / 4), ((const float *)Dn)[o], hq, hs,
+                                              (float)tot, MI);
+            } else {
+                int fmt = kind == 2 ? 2 : 1, bb = fmt == 2 ? ORC_Q80_BB : ORC_Q40_BB;
+                size_t grb = (size_t)(D / ORC_BLK) * bb, drb = (size_t)nbM * bb, gate_b = grb * MI;
+                const uint8_t *Dn = blob + 2 * gate_b;
+                for (int o = 0; o < D; o++)
+                    out[o] += w * (fmt == 2 ? orc_q80_dot(Dn + o * drb, hq, hs, MI) : orc_q40_dot(Dn + o * drb, hq, hs, MI));
+            }
+        }
+    }
+}

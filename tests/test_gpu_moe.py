@@ -19,7 +19,6 @@ from zunzuncito_b200 import synth
 
 pytestmark = pytest.mark.gpu
 
-ENGINES = ("mma", "tc")
 KINDS = {0: (zz.GPU_FMT_Q40, zz.ZZ_ACT_GEGLU_TANH), 1: (zz.GPU_FMT_Q40, zz.ZZ_ACT_SWIGLU),
          2: (zz.GPU_FMT_Q80, zz.ZZ_ACT_SWIGLU), 3: (zz.GPU_FMT_TQ2, zz.ZZ_ACT_SWIGLU_CLAMP)}
 CLAMP = 7.0
@@ -123,11 +122,11 @@ def check_pairs(orc, kind, blobs, X, eidx, ewt, out_gpu, bank, pairs=None):
     return flipped_tok
 
 
-@pytest.fixture(params=["auto", "mma", "mma8", "tc", "tcw", "dec"])
+@pytest.fixture(params=["auto", "i8", "mma8"])
 def engine(request, monkeypatch):
-    """every expert engine: auto (GEMV for small S*K, else mma.sync), mma.sync, tcgen05 (32- and 128-token tiles),
-    and the small-batch GEMV kernels forced (ZZ_MOE_KERNEL; calls of more than 64 pairs
-    take the int8 mma.sync engine there)"""
+    """every expert engine: auto (the decode GEMV kernels for calls of <= 64 pairs, else the
+    int8 tcgen05 engine), and the int8 tcgen05 / int8 mma.sync engines forced for every
+    call size (ZZ_MOE_KERNEL)"""
     monkeypatch.setenv("ZZ_MOE_KERNEL", request.param)
     return request.param
 
@@ -145,11 +144,9 @@ def test_moe_small(orc, kind, S, engine):
     flipped = check_pairs(orc, kind, blobs, X, eidx, ewt, out, bank)
     want = orc.moe_layer(kind, blobs, X, eidx, ewt, D, MI, CLAMP)
     scale = np.max(np.abs(want))
-    for s in range(S):
+    for s in range(S):   # a flipped token's combine is checked from the GPU's own hidden rows above
         if s not in flipped:
             assert np.max(np.abs(out[s] - want[s])) <= 1e-4 * scale, s
-        else:
-            assert np.max(np.abs(out[s] - want[s])) <= 1e-2 * scale, s
 
 
 @pytest.mark.parametrize("key,kind", [("g4", 0), ("mp", 3)])
@@ -163,8 +160,8 @@ def test_moe_golden(orc, key, kind, engine):
     flipped = check_pairs(orc, kind, G[key + "_blobs"], G[key + "_X"], G[key + "_eidx"], G[key + "_ewt"], out, bank)
     ref = G[key + "_out"]
     for s in range(S):
-        lim = 1e-2 if s in flipped else 1e-4
-        assert np.max(np.abs(out[s] - ref[s])) <= lim * np.max(np.abs(ref))
+        if s not in flipped:
+            assert np.max(np.abs(out[s] - ref[s])) <= 1e-4 * np.max(np.abs(ref))
 
 
 def test_moe_declines():
@@ -180,48 +177,129 @@ def test_moe_declines():
         zz.moe_ffn(bank, X, bad, w, 7)
 
 
-def _full_layer(seed, S):
-    """Gemma-4 layer shape: 128 q4_0 experts, D 2816, MI 704, top-8,
+def _gemma_blobs(seed, E=synth.GEMMA_E):
+    """Gemma-4 expert blobs (3): 128 q4_0 experts, D 2816, MI 704,
     weights N(0, 0.02) quantized on device by the parity-tested device quantizer."""
-    D, MI, E, K = synth.GEMMA_D, synth.GEMMA_MI, synth.GEMMA_E, synth.GEMMA_K
+    D, MI = synth.GEMMA_D, synth.GEMMA_MI
     stride = zz.expert_blob_bytes(zz.GPU_FMT_Q40, D, MI)
     blobs = torch.empty((E, stride), dtype=torch.uint8, device="cuda")
     g = torch.Generator(device="cuda").manual_seed(seed)
     gb = zz.ref_tensor_bytes(zz.GPU_FMT_Q40, MI, D)
-    for e in range(E):
-        for i, (O, I) in enumerate([(MI, D), (MI, D), (D, MI)]):
-            w = torch.randn((O, I), generator=g, device="cuda") * 0.02
-            blobs[e, i * gb:i * gb + O * I // 32 * 18] = zz.quant_rows(zz.GPU_FMT_Q40, w)
-    X = synth.gaussian(seed + 1, (S, D))
-    eidx, ewt, _ = synth.zipf_routing(seed + 2, S, E, K)
-    return blobs, X, eidx, ewt
+    for i, (O, I) in enumerate([(MI, D), (MI, D), (D, MI)]):
+        w = torch.randn((E * O, I), generator=g, device="cuda") * 0.02
+        blobs[:, i * gb:i * gb + O * I // 32 * 18] = zz.quant_rows(zz.GPU_FMT_Q40, w).view(E, -1)
+    return blobs
+
+
+def _maple_blobs(seed, E=synth.MAPLE_E):
+    """Maple tq2 expert blobs: codes uniform in {0,1,2}, alpha
+    |N(0,0.02)| + 1e-3 per row, packed as tq2.h:46-51, generated on the device"""
+    D, MI = synth.MAPLE_D, synth.MAPLE_MI
+    gen = torch.Generator(device="cuda").manual_seed(seed)
+
+    def tensor(O, I):
+        c = torch.randint(0, 3, (E, O, I // 64, 4, 16), generator=gen, device="cuda", dtype=torch.uint8)
+        b = c[:, :, :, 0] | (c[:, :, :, 1] << 2) | (c[:, :, :, 2] << 4) | (c[:, :, :, 3] << 6)
+        al = torch.randn((E, O), generator=gen, device="cuda").abs() * 0.02 + 1e-3
+        return torch.cat([al.view(torch.uint8).view(E, -1), b.reshape(E, -1)], dim=1)
+    return torch.cat([tensor(MI, D), tensor(MI, D), tensor(D, MI)], dim=1).contiguous()
+
+
+def _full_check(orc, kind, blobs_np, bank, X, eidx, ewt, out, max_flip_frac=0.002):
+    """Every pair and every token: stage 1 (hq equal but for rounding-tie flips of one
+    step, hs within 1e-5), stage 2 (the combine of the GPU's own hidden rows within 1e-5
+    of max|out|), end to end (tokens without a flip within 1e-4). Returns the flip count."""
+    S, K = eidx.shape
+    D, MI = bank.D, bank.MI
+    src, hq, hs = ws_views(bank, S, K)
+    order = np.argsort(src)                       # pair rows -> pair index p = s*K + k
+    hq_g, hs_g = hq[order], hs[order]
+    hq_r, hs_r = orc.moe_pairs_hidden(kind, blobs_np, X, eidx, D, MI, CLAMP)
+    diff = hq_g.astype(np.int32) - hq_r
+    assert np.max(np.abs(diff)) <= 1
+    flips = int(np.count_nonzero(diff))
+    assert flips <= max(3, max_flip_frac * diff.size), (flips, diff.size)
+    assert np.allclose(hs_g, hs_r, rtol=1e-5, atol=0)
+    want2 = orc.moe_pairs_combine(kind, blobs_np, hq_g, hs_g, eidx, ewt, D, MI)
+    assert np.max(np.abs(out - want2)) <= 1e-5 * np.max(np.abs(want2))
+    want = orc.moe_pairs_combine(kind, blobs_np, hq_r, hs_r, eidx, ewt, D, MI)
+    flipped_tok = np.any(diff.reshape(S, K * MI) != 0, axis=1)
+    scale = np.max(np.abs(want))
+    err = np.max(np.abs(out - want), axis=1)
+    assert np.all(err[~flipped_tok] <= 1e-4 * scale), float(np.max(err[~flipped_tok]) / scale)
+    print(f"pairs {S * K}: {flips} requant flips of {diff.size} hidden codes in {int(flipped_tok.sum())} tokens; "
+          f"max err unflipped {float(np.max(err[~flipped_tok]) / scale):.2e}")
+    return flips
 
 
 def test_moe_full_layer_config3(orc, engine):
+    """S = 512, 128 q4_0 experts, Zipf-routed top-8, full output"""
     S = 512
-    blobs, X, eidx, ewt = _full_layer(600, S)
-    D, MI = synth.GEMMA_D, synth.GEMMA_MI
-    bank = zz.ExpertBankDev(zz.GPU_FMT_Q40, blobs, D, MI)
+    blobs = _gemma_blobs(600)
+    X = synth.gaussian(601, (S, synth.GEMMA_D))
+    eidx, ewt, _ = synth.zipf_routing(602, S, synth.GEMMA_E, synth.GEMMA_K)
+    bank = zz.ExpertBankDev(zz.GPU_FMT_Q40, blobs, synth.GEMMA_D, synth.GEMMA_MI)
     out = zz.moe_ffn(bank, dev(X), dev(eidx), dev(ewt), zz.ZZ_ACT_GEGLU_TANH)
     out_np = out.cpu().numpy()
-    # stage 1 on a sample of pair rows
-    pairs = list(synth.rng(7).choice(S * 8, size=24, replace=False))
-    blobs_np = blobs.cpu().numpy()
-    check_pairs(orc, 0, blobs_np, X, eidx, ewt, out_np, bank, pairs=pairs)
-    # stage 2 on a few whole tokens from the GPU's own hidden rows
-    src, hq, hs = ws_views(bank, S, 8)
-    slot = {int(p): r for r, p in enumerate(src)}
-    for s in (0, 17, 511):
-        want = np.zeros(D, np.float32)
-        for k in range(8):
-            r = slot[s * 8 + k]
-            Dn = split_blob(zz.GPU_FMT_Q40, blobs_np[eidx[s, k]], D, MI)[2]
-            want += ewt[s, k] * orc.q40_matvec(Dn.reshape(D, -1), hq[r], hs[r])
-        assert np.max(np.abs(out_np[s] - want)) <= 1e-5 * np.max(np.abs(want))
+    _full_check(orc, 0, blobs.cpu().numpy(), bank, X, eidx, ewt, out_np)
     # linearity in the router weights (an exact power-of-two scaling)
     out2 = zz.moe_ffn(bank, dev(X), dev(eidx), dev(2 * ewt), zz.ZZ_ACT_GEGLU_TANH).cpu().numpy()
     assert np.max(np.abs(out2 - 2 * out_np)) <= 1e-6 * np.max(np.abs(out_np))
     # token permutation: outputs permute with the tokens
     perm = synth.rng(8).permutation(S)
+    out3 = zz.moe_ffn(bank, dev(X[perm]), dev(eidx[perm]), dev(ewt[perm]), zz.ZZ_ACT_GEGLU_TANH).cpu().numpy()
+    assert np.max(np.abs(out3 - out_np[perm])) <= 1e-6 * np.max(np.abs(out_np))
+
+
+@pytest.mark.parametrize("S", [1, 8])
+def test_moe_decode_config2(orc, S):
+    """Gemma-4 experts at decode (S = 1: 8 of 128 experts; S = 8: 64
+    pairs, the largest call the decode kernels take) on the default engine, which routes
+    these calls to the decode kernels; every pair and token checked"""
+    blobs = _gemma_blobs(700)
+    X = synth.gaussian(701 + S, (S, synth.GEMMA_D))
+    eidx, ewt, _ = synth.zipf_routing(702 + S, S, synth.GEMMA_E, synth.GEMMA_K)
+    bank = zz.ExpertBankDev(zz.GPU_FMT_Q40, blobs, synth.GEMMA_D, synth.GEMMA_MI)
+    out = zz.moe_ffn(bank, dev(X), dev(eidx), dev(ewt), zz.ZZ_ACT_GEGLU_TANH).cpu().numpy()
+    _full_check(orc, 0, blobs.cpu().numpy(), bank, X, eidx, ewt, out)
+
+
+@pytest.mark.parametrize("S", [1, 512])
+def test_moe_maple_config4(orc, S, engine):
+    """Maple ternary layer, 256 tq2 experts, D 2048, MI 512, top-8,
+    clamped SwiGLU, decode and S = 512"""
+    blobs = _maple_blobs(800)
+    X = synth.gaussian(801 + S, (S, synth.MAPLE_D))
+    eidx, ewt, _ = synth.zipf_routing(802 + S, S, synth.MAPLE_E, synth.MAPLE_K)
+    bank = zz.ExpertBankDev(zz.GPU_FMT_TQ2, blobs, synth.MAPLE_D, synth.MAPLE_MI)
+    out = zz.moe_ffn(bank, dev(X), dev(eidx), dev(ewt), zz.ZZ_ACT_SWIGLU_CLAMP, CLAMP).cpu().numpy()
+    _full_check(orc, 3, blobs.cpu().numpy(), bank, X, eidx, ewt, out)
+
+
+def test_moe_prefill_4096(orc, engine):
+    """S = 4096 (BASELINE config 5's largest batch): many full 128-row items per expert
+    on the tcgen05 engine, the capped-grid item striding on the mma.sync engine; sampled
+    pairs (stage 1), sampled tokens (stage 2) and the size-independent properties"""
+    S, K, D, MI = 4096, synth.GEMMA_K, synth.GEMMA_D, synth.GEMMA_MI
+    blobs = _gemma_blobs(900)
+    X = synth.gaussian(901, (S, D))
+    eidx, ewt, _ = synth.zipf_routing(902, S, synth.GEMMA_E, K)
+    bank = zz.ExpertBankDev(zz.GPU_FMT_Q40, blobs, D, MI)
+    out = zz.moe_ffn(bank, dev(X), dev(eidx), dev(ewt), zz.ZZ_ACT_GEGLU_TANH)
+    out_np = out.cpu().numpy()
+    blobs_np = blobs.cpu().numpy()
+    src, hq, hs = ws_views(bank, S, K)
+    slot = {int(p): r for r, p in enumerate(src)}
+    toks = [0, 1, 777, 2048, 4095] + list(synth.rng(9).choice(S, size=11, replace=False))
+    sub_e, sub_w = eidx[toks], ewt[toks]
+    hq_r, hs_r = orc.moe_pairs_hidden(0, blobs_np, X[toks], sub_e, D, MI)
+    rows = [slot[s * K + k] for s in toks for k in range(K)]
+    diff = hq[rows].astype(np.int32) - hq_r
+    assert np.max(np.abs(diff)) <= 1 and np.count_nonzero(diff) <= max(3, diff.size // 500)
+    want2 = orc.moe_pairs_combine(0, blobs_np, hq[rows], hs[rows], sub_e, sub_w, D, MI)
+    assert np.max(np.abs(out_np[toks] - want2)) <= 1e-5 * np.max(np.abs(want2))
+    out2 = zz.moe_ffn(bank, dev(X), dev(eidx), dev(0.5 * ewt), zz.ZZ_ACT_GEGLU_TANH).cpu().numpy()
+    assert np.max(np.abs(2 * out2 - out_np)) <= 1e-6 * np.max(np.abs(out_np))
+    perm = synth.rng(10).permutation(S)
     out3 = zz.moe_ffn(bank, dev(X[perm]), dev(eidx[perm]), dev(ewt[perm]), zz.ZZ_ACT_GEGLU_TANH).cpu().numpy()
     assert np.max(np.abs(out3 - out_np[perm])) <= 1e-6 * np.max(np.abs(out_np))

@@ -88,6 +88,7 @@ struct GemmArgs {
     int K;
     // tensor-core path: B rows in pair order and transposed block scales
     const __half *xg;        // [rows_cap][I] fp16
+    const int8_t *xg8;       // [rows_cap][I] int8 (the int8 tensor-core engine's B rows)
     const float *xsT;        // [I/32][ldT]
     int ldT, rows_cap;
     float *hsT;              // gate/up: transposed hidden scales [O/64][ldT]

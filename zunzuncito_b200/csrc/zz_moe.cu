@@ -37,34 +37,32 @@ int launch_quant_act(const float *x, int S, int I, int8_t *xq, float *sx, float 
 int launch_s8_to_h(const int8_t *q, __half *h, long n, cudaStream_t st);
 __global__ void k_rows_sx(const int8_t *__restrict__ xq, const float *__restrict__ xs, int S, int I,
                           float *__restrict__ xsx);
-int launch_moe_tc(int fmt, int epi, const GemmArgs &a, int n_groups, int *err, cudaStream_t st);
-int launch_moe_tcw(int fmt, int epi, const GemmArgs &a, int n_groups, int *err, cudaStream_t st);
+int launch_moe_i8(int fmt, int epi, const GemmArgs &a, int n_groups, int *err, cudaStream_t st);
+bool moe_i8_supported(int fmt, int D, int MI);
 int launch_moe_dec(int fmt, const GemmArgs &gu, const GemmArgs &dn, int P, float *hbuf, cudaStream_t st);
 
 // Expert engine. Default ("auto"): the small-batch GEMV kernels (zz_moe_dec.cu) when
-// S*K <= DEC_MAX_PAIRS, else the int8 mma.sync GEMM (k_gemm<..., S8>), the fastest
-// measured. ZZ_MOE_KERNEL=dec|mma8|mma|tc forces one (mma = the fp16-exact mma.sync
-// variant, tc = the tcgen05 kernel k_moe_tc). All are exact per block.
-enum { ENG_DEC = 0, ENG_MMA = 1, ENG_TC = 2, ENG_MMA8 = 3, ENG_TCW = 4 };
+// S*K <= DEC_MAX_PAIRS, else the int8 tcgen05 engine (zz_moe_i8.cu) where the layer's
+// shape allows it, else the int8 mma.sync GEMM (k_gemm<..., S8>).
+// ZZ_MOE_KERNEL=dec|i8|mma8 forces one where it applies. All are exact per block.
+enum { ENG_DEC = 0, ENG_MMA8 = 3, ENG_I8 = 5 };
 constexpr int DEC_MAX_PAIRS = 64;
-static int moe_engine(int P) {
+static int moe_engine(int P, const zz_expert_bank *b) {
     const char *e = getenv("ZZ_MOE_KERNEL");
-    if (e && !strcmp(e, "tc")) return ENG_TC;
-    if (e && !strcmp(e, "tcw")) return ENG_TCW;
-    if (e && !strcmp(e, "mma")) return ENG_MMA;
+    const bool i8_ok = moe_i8_supported(b->fmt, b->hidden, b->inter);
     if (e && !strcmp(e, "mma8")) return ENG_MMA8;
-    // the decode kernels take calls of up to DEC_MAX_PAIRS pairs; larger ones go to mma8
-    if (e && !strcmp(e, "dec")) return P <= DEC_MAX_PAIRS ? ENG_DEC : ENG_MMA8;
-    return P <= DEC_MAX_PAIRS ? ENG_DEC : ENG_MMA8;
+    if (e && !strcmp(e, "i8")) return i8_ok ? ENG_I8 : ENG_MMA8;
+    // the decode kernels take calls of up to DEC_MAX_PAIRS pairs
+    if (P <= DEC_MAX_PAIRS) return ENG_DEC;
+    return i8_ok ? ENG_I8 : ENG_MMA8;
 }
-constexpr int TC_BN = 32;
-constexpr int TCW_BN = 128;
+constexpr int I8_BN = 128;
 
 #ifndef ZZ_MOE_BN
 #define ZZ_MOE_BN 32
 #endif
 constexpr int MOE_BN = ZZ_MOE_BN;
-constexpr int ROW_ALIGN = 16;
+constexpr int ROW_ALIGN = 4;
 constexpr int DEC_BN = 2;      // rows per work item of the small-batch kernels (DEC_C)
 constexpr int DENSE_BN = 64;
 
@@ -147,13 +145,17 @@ __device__ __forceinline__ int block_excl_scan(int v, int *warp_tot, int &total)
 // (rank order inside an expert is arbitrary: each pair's result is independent of its
 // row); each expert's rows start on a ROW_ALIGN boundary and padding rows get src -1.
 // Also clears the tensor-core error word of the call. E <= 2048.
+// With `sorted`, the items are listed in decreasing row count (full items first, then
+// the partial ones by size), so a grid striding over them hands every CTA a similar mix
+// of large and small tiles; BN <= 1024 then.
 __global__ void __launch_bounds__(1024) k_route(const int32_t *__restrict__ eidx, const float *__restrict__ ewt,
                                                 int P, int E, int BN, int cap, int *__restrict__ pair_src,
                                                 float *__restrict__ pair_w, WorkItem *__restrict__ items,
-                                                int *__restrict__ n_items, int *__restrict__ tcerr) {
+                                                int *__restrict__ n_items, int *__restrict__ tcerr, int sorted) {
     extern __shared__ int sh[];
     int *cnt = sh, *off = sh + E, *ioff = sh + 2 * E, *cur = sh + 3 * E;
     __shared__ int warp_tot[33];
+    __shared__ int bin_start[1025], bin_cur[1025];
     for (int e = threadIdx.x; e < E; e += blockDim.x) { cnt[e] = 0; cur[e] = 0; }
     if (threadIdx.x == 0) *tcerr = 0;
     __syncthreads();
@@ -182,9 +184,36 @@ __global__ void __launch_bounds__(1024) k_route(const int32_t *__restrict__ eidx
             pair_w[pos] = ewt[p];
         }
     }
+    if (!sorted) {
+        for (int e = threadIdx.x; e < E; e += blockDim.x) {
+            int c = cnt[e], ni = (c + BN - 1) / BN;
+            for (int i = 0; i < ni; i++) items[ioff[e] + i] = WorkItem{e, off[e] + i * BN, min(BN, c - i * BN), 0};
+        }
+    } else {
+        // full items (BN rows) first, at an exclusive scan of the experts' full counts;
+        // then one bin per remainder size r = BN-1 .. 1
+        const int f0 = e0 < E ? cnt[e0] / BN : 0, f1 = e1 < E ? cnt[e1] / BN : 0;
+        int n_full;
+        const int fo = block_excl_scan(f0 + f1, warp_tot, n_full);
+        for (int r = threadIdx.x; r <= BN; r += blockDim.x) bin_cur[r] = 0;
+        __syncthreads();
+        for (int e = threadIdx.x; e < E; e += blockDim.x)
+            if (cnt[e] % BN) atomicAdd(&bin_cur[cnt[e] % BN], 1);
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            int o = n_full;
+            for (int r = BN - 1; r >= 1; r--) { bin_start[r] = o; o += bin_cur[r]; bin_cur[r] = 0; }
+        }
+        __syncthreads();
+        if (e0 < E) for (int i = 0; i < f0; i++) items[fo + i] = WorkItem{e0, off[e0] + i * BN, BN, 0};
+        if (e1 < E) for (int i = 0; i < f1; i++) items[fo + f0 + i] = WorkItem{e1, off[e1] + i * BN, BN, 0};
+        for (int e = threadIdx.x; e < E; e += blockDim.x) {
+            const int c = cnt[e], rem = c % BN;
+            if (rem) items[bin_start[rem] + atomicAdd(&bin_cur[rem], 1)] = WorkItem{e, off[e] + (c / BN) * BN, rem, 0};
+        }
+    }
     for (int e = threadIdx.x; e < E; e += blockDim.x) {
-        int c = cnt[e], ni = (c + BN - 1) / BN;
-        for (int i = 0; i < ni; i++) items[ioff[e] + i] = WorkItem{e, off[e] + i * BN, min(BN, c - i * BN), 0};
+        int c = cnt[e];
         int pad_end = off[e] + (c + ROW_ALIGN - 1) / ROW_ALIGN * ROW_ALIGN;
         for (int r = off[e] + c; r < pad_end; r++) pair_src[r] = -1;
     }
@@ -199,32 +228,37 @@ __global__ void k_count_bad(const int32_t *eidx, int P, int E, int *bad) {
 // pair rows incl. alignment padding; a multiple of ROW_ALIGN
 static inline size_t pair_cap(size_t P, int E) { return (P + (size_t)ROW_ALIGN * E + 15) / 16 * 16; }
 
-// routed rows in pair order: xg[r] = xh[token(r)] (fp16) and the block scales
-// transposed, xsT[b][r] = xs[token(r)][b], for the tensor-core path's bulk copies
-__global__ void k_gather_rows(const int *__restrict__ pair_src, int K, int cap, const __half *__restrict__ xh,
-                              const float *__restrict__ xs, int D, __half *__restrict__ xg, float *__restrict__ xsT,
-                              int ldT) {
+// routed rows in pair order for the int8 tensor-core engine: xg8[r] = xq[token(r)] and the
+// block scales transposed, xsT[b][r] = xs[token(r)][b] (bulk-copy friendly)
+__global__ void k_gather_rows8(const int *__restrict__ pair_src, int K, const int8_t *__restrict__ xq,
+                               const float *__restrict__ xs, int D, int8_t *__restrict__ xg8, float *__restrict__ xsT,
+                               int ldT) {
     const int r = blockIdx.x;
     const int src = pair_src[r];
     if (src < 0) return;
     const int tok = src / K, nb = D / 32;
-    const uint4 *a = reinterpret_cast<const uint4 *>(xh + (size_t)tok * D);
-    uint4 *b = reinterpret_cast<uint4 *>(xg + (size_t)r * D);
-    for (int i = threadIdx.x; i < D / 8; i += blockDim.x) b[i] = a[i];
+    const uint4 *a = reinterpret_cast<const uint4 *>(xq + (size_t)tok * D);
+    uint4 *b = reinterpret_cast<uint4 *>(xg8 + (size_t)r * D);
+    for (int i = threadIdx.x; i < D / 16; i += blockDim.x) b[i] = a[i];
     for (int i = threadIdx.x; i < nb; i += blockDim.x) xsT[(size_t)i * ldT + r] = xs[(size_t)tok * nb + i];
 }
 
 struct MoeWs {
-    int8_t *xq; float *xs, *xsx; __half *xh;
+    int8_t *xq; float *xs, *xsx;
     int *pair_src; float *pair_w;
-    __half *xg; float *xsT, *hsT; size_t cap, ldT;
+    int8_t *xg8; float *xsT, *hsT; size_t cap, ldT;
     WorkItem *items; int *n_items;
-    int8_t *hq; float *hs; int *hblk; __half *hh; float *hf;
+    int8_t *hq; float *hs; int *hblk; float *hf;
     int *bad;
     int *tcerr;
     size_t total;
 };
 
+// Scratch of one layer call. Pair rows (cap) count every routed (token, expert) pair
+// plus each expert's padding to ROW_ALIGN rows; per pair row: the gathered int8
+// activation row (D), its block scales transposed (D/32 f32), the requantized hidden
+// row (MI int8 + MI/32 f32 scales, also transposed, + MI/32 int block sums for tq2).
+// The decode engine's f32 hidden rows exist only for calls it takes (S*K <= 64 pairs).
 static MoeWs moe_layout(const zz_expert_bank *b, int S, int K, uint8_t *base) {
     MoeWs w{};
     const int D = b->hidden, MI = b->inter, E = b->n_experts;
@@ -238,10 +272,9 @@ static MoeWs moe_layout(const zz_expert_bank *b, int S, int K, uint8_t *base) {
     w.xq = (int8_t *)take((size_t)S * D);
     w.xs = (float *)take((size_t)S * (D / 32) * 4);
     w.xsx = (float *)take((size_t)S * 4);
-    w.xh = (__half *)take((size_t)S * D * 2);
     w.pair_src = (int *)take(cap * 4);
     w.pair_w = (float *)take(cap * 4);
-    w.xg = (__half *)take(cap * D * 2);
+    w.xg8 = (int8_t *)take(cap * D);
     w.xsT = (float *)take((size_t)(D / 32) * ldT * 4);
     w.hsT = (float *)take((size_t)(MI / 32) * ldT * 4);
     w.items = (WorkItem *)take(maxit * sizeof(WorkItem));
@@ -249,8 +282,7 @@ static MoeWs moe_layout(const zz_expert_bank *b, int S, int K, uint8_t *base) {
     w.hq = (int8_t *)take(cap * MI);
     w.hs = (float *)take(cap * (MI / 32) * 4);
     w.hblk = (int *)take(cap * (MI / 32) * 4);
-    w.hh = (__half *)take(cap * MI * 2);
-    w.hf = (float *)take(cap * MI * 4);
+    w.hf = (float *)take(P <= (size_t)DEC_MAX_PAIRS ? cap * MI * 4 : 0);
     w.bad = (int *)take(4);
     w.tcerr = (int *)take(4);
     w.total = o;
@@ -418,37 +450,33 @@ static int moe_impl(const zz_expert_bank *b, const float *X, const int8_t *xq_in
         if (bad) return fail("zz_moe_ffn: %d expert ids outside [0, %d)", bad, E);
     }
     prof_mark(st);
-    const int eng = moe_engine(P);
-    const bool tcw = eng == ENG_TCW;
-    const bool tcp = eng == ENG_TC || tcw;  // engines on tcgen05 (pair-ordered fp16 rows)
+    const int eng = moe_engine(P, b);
+    const bool i8 = eng == ENG_I8;
     const int8_t *xq = xq_in;
     const float *xs = xs_in;
     // routing (eidx/ewt only) on the side stream, overlapping the quantization
     SideStream *side = side_stream();
     if (!side) return 0;
-    SideStream &g_side = *side;
-    if (!check_cuda(cudaEventRecord(g_side.fork, st), "fork") || !check_cuda(cudaStreamWaitEvent(g_side.s, g_side.fork, 0), "fork wait"))
+    if (!check_cuda(cudaEventRecord(side->fork, st), "fork") ||
+        !check_cuda(cudaStreamWaitEvent(side->s, side->fork, 0), "fork wait"))
         return 0;
-    k_route<<<1, 1024, 4 * E * sizeof(int), g_side.s>>>(eidx, ewt, P, E,
-                                                        tcw ? TCW_BN : tcp ? TC_BN : eng == ENG_DEC ? DEC_BN : MOE_BN,
-                                                        (int)w.cap, w.pair_src, w.pair_w, w.items, w.n_items, w.tcerr);
+    k_route<<<1, 1024, 4 * E * sizeof(int), side->s>>>(eidx, ewt, P, E, i8 ? I8_BN : eng == ENG_DEC ? DEC_BN : MOE_BN,
+                                                      (int)w.cap, w.pair_src, w.pair_w, w.items, w.n_items, w.tcerr,
+                                                      i8 ? 1 : 0);
     if (!check_cuda(cudaGetLastError(), "route launch")) return 0;
-    if (!check_cuda(cudaEventRecord(g_side.join, g_side.s), "join")) return 0;
+    if (!check_cuda(cudaEventRecord(side->join, side->s), "join")) return 0;
     if (X) {
-        const bool want_h = eng == ENG_MMA || tcp;  // engines reading fp16 activations
-        if (!launch_quant_act(X, S, D, w.xq, w.xs, fmt == GPU_FMT_TQ2 ? w.xsx : nullptr, want_h ? w.xh : nullptr, st,
-                              OUT, D))
+        if (!launch_quant_act(X, S, D, w.xq, w.xs, fmt == GPU_FMT_TQ2 ? w.xsx : nullptr, nullptr, st, OUT, D))
             return 0;
         xq = w.xq;
         xs = w.xs;
     } else {
         if (!check_cuda(cudaMemsetAsync(OUT, 0, (size_t)S * D * 4, st), "memset OUT")) return 0;
         if (fmt == GPU_FMT_TQ2) k_rows_sx<<<(S + 127) / 128, 128, 0, st>>>(xq, xs, S, D, w.xsx);
-        if ((eng == ENG_MMA || tcp) && !launch_s8_to_h(xq, w.xh, (long)S * D, st)) return 0;
     }
-    if (!check_cuda(cudaStreamWaitEvent(st, g_side.join, 0), "join wait")) return 0;
-    if (tcp) {
-        k_gather_rows<<<(unsigned)w.cap, 128, 0, st>>>(w.pair_src, K, (int)w.cap, w.xh, xs, D, w.xg, w.xsT, (int)w.ldT);
+    if (!check_cuda(cudaStreamWaitEvent(st, side->join, 0), "join wait")) return 0;
+    if (i8) {
+        k_gather_rows8<<<(unsigned)w.cap, 128, 0, st>>>(w.pair_src, K, xq, xs, D, w.xg8, w.xsT, (int)w.ldT);
         if (!check_cuda(cudaGetLastError(), "gather launch")) return 0;
     }
 
@@ -478,18 +506,16 @@ static int moe_impl(const zz_expert_bank *b, const float *X, const int8_t *xq_in
     g.codes_gstride = (long)codes_bytes(fmt, 2 * MI, D);
     g.scale_gstride = (long)scales_bytes(fmt, 2 * MI, D);
     g.O = 2 * MI; g.I = D;
-    g.xq = w.xh; g.xs = xs; g.xsx = w.xsx; g.xblk = nullptr; g.gather = w.pair_src; g.gather_div = K;
+    g.xq = xq; g.xs = xs; g.xsx = w.xsx; g.xblk = nullptr; g.gather = w.pair_src; g.gather_div = K;
     g.items = w.items; g.n_items = w.n_items;
     g.act = act; g.clamp = clamp;
-    g.hq = w.hq; g.hs = w.hs; g.hblk = w.hblk; g.hh = (eng == ENG_MMA || tcp) ? w.hh : nullptr;
-    g.xg = w.xg; g.xsT = w.xsT; g.ldT = (int)w.ldT; g.hsT = w.hsT; g.rows_cap = (int)w.cap;
+    g.hq = w.hq; g.hs = w.hs; g.hblk = w.hblk; g.hh = nullptr;
+    g.pair_src = w.pair_src; g.K = K;
+    g.xg8 = w.xg8; g.xsT = w.xsT; g.ldT = (int)w.ldT; g.hsT = w.hsT; g.rows_cap = (int)w.cap;
     prof_mark(st);
-    if (tcp) {
-        if (!(tcw ? launch_moe_tcw : launch_moe_tc)(fmt, EPI_GATEUP, g, E, w.tcerr, st)) return 0;
-    } else if (eng == ENG_MMA8) {
-        g.xq = xq;  // int8 rows
-        if (!launch_gemm<EPI_GATEUP, MOE_BN, false, true>(fmt, g, dim3((2 * MI) / G_BM, maxit), st)) return 0;
-    } else if (!launch_gemm<EPI_GATEUP, MOE_BN, true>(fmt, g, dim3((2 * MI) / G_BM, maxit), st)) {
+    if (i8) {
+        if (!launch_moe_i8(fmt, EPI_GATEUP, g, E, w.tcerr, st)) return 0;
+    } else if (!launch_gemm<EPI_GATEUP, MOE_BN, false, true>(fmt, g, dim3((2 * MI) / G_BM, maxit), st)) {
         return 0;
     }
     prof_mark(st);
@@ -499,14 +525,12 @@ static int moe_impl(const zz_expert_bank *b, const float *X, const int8_t *xq_in
     d.codes_gstride = (long)codes_bytes(fmt, D, MI);
     d.scale_gstride = (long)scales_bytes(fmt, D, MI);
     d.O = D; d.I = MI;
-    d.xq = w.hh; d.xs = w.hs; d.xsx = nullptr; d.xblk = fmt == GPU_FMT_TQ2 ? w.hblk : nullptr; d.gather = nullptr;
+    d.xq = w.hq; d.xs = w.hs; d.xsx = nullptr; d.xblk = fmt == GPU_FMT_TQ2 ? w.hblk : nullptr; d.gather = nullptr;
     d.items = w.items; d.n_items = w.n_items;
     d.out = OUT; d.pair_w = w.pair_w; d.pair_src = w.pair_src; d.K = K;
-    d.xg = w.hh; d.xsT = w.hsT; d.ldT = (int)w.ldT; d.rows_cap = (int)w.cap;
-    if (eng == ENG_MMA8) d.xq = w.hq;
-    int ok = tcp ? (tcw ? launch_moe_tcw : launch_moe_tc)(fmt, EPI_DOWN, d, E, w.tcerr, st)
-             : eng == ENG_MMA8 ? launch_gemm<EPI_DOWN, MOE_BN, false, true>(fmt, d, dim3((D + G_BM - 1) / G_BM, maxit), st)
-                               : launch_gemm<EPI_DOWN, MOE_BN, true>(fmt, d, dim3((D + G_BM - 1) / G_BM, maxit), st);
+    d.xg8 = w.hq; d.xsT = w.hsT; d.ldT = (int)w.ldT; d.rows_cap = (int)w.cap;
+    int ok = i8 ? launch_moe_i8(fmt, EPI_DOWN, d, E, w.tcerr, st)
+                : launch_gemm<EPI_DOWN, MOE_BN, false, true>(fmt, d, dim3((D + G_BM - 1) / G_BM, maxit), st);
     prof_mark(st);
     return ok;
 }
