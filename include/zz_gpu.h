@@ -157,13 +157,16 @@ int zz_moe_ffn_q8_dev(const zz_expert_bank *bank, const int8_t *xq, const float 
 
 /* zz_moe_ffn_dev for callers that cannot allocate device memory (no counterpart in
  * the reference, which has no device memory of its own). Same arguments minus the
- * workspace: the scratch is a fixed 32 MiB array inside the library, held by every GPU
- * that loads it until the process exits. Declines when S and K need more than that
- * (about S = 1200 at top-8 for the Gemma-4 shape). It calls no allocator.
+ * workspace: the scratch is a fixed ZZ_NOALLOC_SCRATCH_BYTES (32 MiB) array inside the
+ * library, held by every GPU that loads it until the process exits. Declines when
+ * zz_moe_workspace_bytes(bank, S, K) exceeds it: at top-8 that is S > 862 for the
+ * Gemma-4 shape (hidden 2816, inter 704, 128 experts) and S > 1147 for Maple's (2048,
+ * 512, 256 experts). It calls no allocator.
  *  - The first call on each device looks up the array's device address with that
  *    device current; make that first call before any stream capture.
  *  - All calls share the one array and it keeps the previous call's contents; calls
  *    that overlap on the GPU (two streams, or two host threads) race on it. */
+#define ZZ_NOALLOC_SCRATCH_BYTES (32u << 20)
 int zz_moe_ffn_noalloc_dev(const zz_expert_bank *bank, const float *X, const int32_t *eidx,
                            const float *ewt, float *OUT, int S, int K, int act, float clamp,
                            void *stream);

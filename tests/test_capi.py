@@ -92,3 +92,15 @@ def test_lazy_load_names_match_api():
     out = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, check=True,
                          cwd=os.path.dirname(os.path.dirname(HDR)))
     assert out.stdout.strip() == "False"
+
+
+@pytest.mark.parametrize("fmt,E,D,MI,smax", [(zz.GPU_FMT_Q40, 128, 2816, 704, 862), (zz.GPU_FMT_TQ2, 256, 2048, 512, 1147)])
+def test_noalloc_capacity_matches_header(fmt, E, D, MI, smax):
+    """the largest S the allocation-free entry point takes at top-8, as its header states:
+    the workspace of S fits the fixed scratch array, that of S + 1 does not"""
+    cap = int(re.search(r"#define ZZ_NOALLOC_SCRATCH_BYTES \((\d+)u << (\d+)\)", open(HDR).read()).group(1)) << 20
+    assert cap == 32 << 20
+    b = zz.ExpertBank(fmt, E, D, MI, None, None, None, None)
+    assert zz.lib.zz_moe_workspace_bytes(ctypes.byref(b), smax, 8) <= cap
+    assert zz.lib.zz_moe_workspace_bytes(ctypes.byref(b), smax + 1, 8) > cap
+    assert f"S > {smax}" in open(HDR).read()

@@ -61,3 +61,31 @@ def test_noalloc_rejects_oversize():
     out = torch.zeros((S, D), device="cuda")
     assert _noalloc(bank, X, eidx, ewt, out) == 0
     assert b"scratch" in zz.lib.gpu_last_error()
+
+
+def test_noalloc_gemma_shape_at_capacity():
+    """Gemma-4 layer shape (128 q4_0 experts, hidden 2816, inter 704, top-8) at the largest
+    batch the fixed scratch holds, S = 862: matches the workspace entry point; S = 863
+    declines with a reason instead of running."""
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    D, MI, E, K = synth.GEMMA_D, synth.GEMMA_MI, synth.GEMMA_E, synth.GEMMA_K
+    stride = zz.expert_blob_bytes(zz.GPU_FMT_Q40, D, MI)
+    g = torch.Generator(device="cuda").manual_seed(990)
+    gb = zz.ref_tensor_bytes(zz.GPU_FMT_Q40, MI, D)
+    blobs = torch.empty((E, stride), dtype=torch.uint8, device="cuda")
+    for i, (O, I) in enumerate([(MI, D), (MI, D), (D, MI)]):
+        w = torch.randn((E * O, I), generator=g, device="cuda") * 0.02
+        blobs[:, i * gb:i * gb + O * I // 32 * 18] = zz.quant_rows(zz.GPU_FMT_Q40, w).view(E, -1)
+    bank = zz.ExpertBankDev(zz.GPU_FMT_Q40, blobs, D, MI)
+    S = 862
+    X = torch.from_numpy(synth.gaussian(991, (S + 1, D))).cuda()
+    ei, ew, _ = synth.zipf_routing(992, S + 1, E, K)
+    eidx, ewt = torch.from_numpy(ei).cuda(), torch.from_numpy(ew).cuda()
+    want = zz.moe_ffn(bank, X[:S], eidx[:S], ewt[:S], zz.ZZ_ACT_GEGLU_TANH).cpu().numpy()
+    out = torch.full((S + 1, D), float("nan"), device="cuda")
+    assert _noalloc(bank, X[:S], eidx[:S], ewt[:S], out[:S]) == 1, zz.lib.gpu_last_error()
+    got = out[:S].cpu().numpy()
+    assert np.max(np.abs(got - want)) <= TOL * np.max(np.abs(want))
+    assert _noalloc(bank, X, eidx, ewt, out) == 0
+    assert b"scratch" in zz.lib.gpu_last_error()

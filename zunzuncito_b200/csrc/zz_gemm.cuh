@@ -103,36 +103,28 @@ __device__ __forceinline__ void mma_f16(float d[4], uint32_t a0, uint32_t a1, ui
         : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
         : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "f"(c0), "f"(c1), "f"(c2), "f"(c3));
 }
+// int8 MMA onto the accumulator preset 0x4B400000 (fp32 1.5 * 2^23): for a block sum
+// |I| < 2^22 the s32 result 0x4B400000 + I, read as fp32, is exactly 12582912 + I, so the
+// block integer reaches fp32 without a conversion instruction
+constexpr uint32_t S8_BIAS = 0x4B400000u;
+constexpr float S8_BIAS_F = 12582912.0f;
 __device__ __forceinline__ void mma_s8(int c[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
                                        uint32_t b1) {
     asm volatile(
         "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-        "{%10,%11,%12,%13};"
+        "{%10,%10,%10,%10};"
         : "=r"(c[0]), "=r"(c[1]), "=r"(c[2]), "=r"(c[3])
-        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(0), "r"(0), "r"(0), "r"(0));
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(S8_BIAS));
 }
 __device__ __forceinline__ void ldsm_x4(uint32_t &r0, uint32_t &r1, uint32_t &r2, uint32_t &r3, const void *p) {
     uint32_t s = (uint32_t)__cvta_generic_to_shared(p);
     asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
                  : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3) : "r"(s));
 }
-// packed fp32 pair ops (sm_100): d = a*b + c and d = a*b on two lanes at once
-__device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
-    float2 d;
-    asm("{.reg .b64 ra, rb, rc, rd;\n\t"
-        "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\tmov.b64 rc, {%6, %7};\n\t"
-        "fma.rn.f32x2 rd, ra, rb, rc;\n\tmov.b64 {%0, %1}, rd;}"
-        : "=f"(d.x), "=f"(d.y) : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
-    return d;
-}
-__device__ __forceinline__ float2 fmul2(float2 a, float2 b) {
-    float2 d;
-    asm("{.reg .b64 ra, rb, rd;\n\t"
-        "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
-        "mul.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;}"
-        : "=f"(d.x), "=f"(d.y) : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
-    return d;
-}
+// packed fp32 pair ops (sm_100 fma.rn.f32x2 / mul.rn.f32x2 through the compiler's own
+// intrinsics, so operand pairs are allocated as register pairs with no packing moves)
+__device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) { return __ffma2_rn(a, b, c); }
+__device__ __forceinline__ float2 fmul2(float2 a, float2 b) { return __fmul2_rn(a, b); }
 __device__ __forceinline__ void cp_async4_zfill(void *smem, const void *gmem, bool valid) {
     uint32_t s = (uint32_t)__cvta_generic_to_shared(smem);
     int n = valid ? 4 : 0;
@@ -349,14 +341,17 @@ __device__ __forceinline__ void gemm_item(const GemmArgs &a, int item_idx) {
                 a0 = (w0 >> sh) & 0x03030303u; a2 = (w0 >> (sh + 2)) & 0x03030303u;
                 a1 = (w1 >> sh) & 0x03030303u; a3 = (w1 >> (sh + 2)) & 0x03030303u;
             }
-            float2 dw0 = make_float2(1.f, 1.f), dw1 = make_float2(1.f, 1.f);
+            // per row: dw and -M*dw (exact: dw has 11 significant bits), so that
+            // fma(F, dw, -M*dw) = dw * I rounded once for F = M + I
+            float w0 = 1.f, w1 = 1.f;
             if (T::HAS_WSCALE) {
                 const __half *hs = reinterpret_cast<const __half *>(sas);
-                float w0 = __half2float(hs[rA * G_BKB + kb]), w1 = __half2float(hs[(rA + 8) * G_BKB + kb]);
+                w0 = __half2float(hs[rA * G_BKB + kb]);
+                w1 = __half2float(hs[(rA + 8) * G_BKB + kb]);
                 if (FMT == GPU_FMT_Q40) { w0 *= 0.0625f; w1 *= 0.0625f; }  // codes carry 16 (q - 8)
-                dw0 = make_float2(w0, w0);
-                dw1 = make_float2(w1, w1);
             }
+            const float2 dw0 = make_float2(w0, w0), dw1 = make_float2(w1, w1);
+            const float2 cm0 = make_float2(-S8_BIAS_F * w0, -S8_BIAS_F * w0), cm1 = make_float2(-S8_BIAS_F * w1, -S8_BIAS_F * w1);
             // this thread's activation scales of the block: column pairs 8j + 2t (+1)
             float dxv[2 * NT];
 #pragma unroll
@@ -368,14 +363,11 @@ __device__ __forceinline__ void gemm_item(const GemmArgs &a, int item_idx) {
                 int c[4];
                 mma_s8(c, a0, a1, a2, a3, b0, b1);
                 const float2 dx = make_float2(dxv[2 * j], dxv[2 * j + 1]);
-                const float2 d01 = make_float2((float)c[0], (float)c[1]), d23 = make_float2((float)c[2], (float)c[3]);
-                if (T::HAS_WSCALE) {
-                    acc[j][0] = ffma2(fmul2(dw0, dx), d01, acc[j][0]);
-                    acc[j][1] = ffma2(fmul2(dw1, dx), d23, acc[j][1]);
-                } else {
-                    acc[j][0] = ffma2(dx, d01, acc[j][0]);
-                    acc[j][1] = ffma2(dx, d23, acc[j][1]);
-                }
+                const float2 f01 = make_float2(__int_as_float(c[0]), __int_as_float(c[1]));
+                const float2 f23 = make_float2(__int_as_float(c[2]), __int_as_float(c[3]));
+                // dw * I (one rounding), then + dx * (dw * I)
+                acc[j][0] = ffma2(ffma2(f01, dw0, cm0), dx, acc[j][0]);
+                acc[j][1] = ffma2(ffma2(f23, dw1, cm1), dx, acc[j][1]);
             };
             // B fragments of two n8 tiles per ldmatrix.x4: matrices (tile jp, k 0-15),
             // (jp, k 16-31), (jp+1, k 0-15), (jp+1, k 16-31); lane l addresses row l % 8

@@ -42,9 +42,10 @@ bool moe_i8_supported(int fmt, int D, int MI);
 int launch_moe_dec(int fmt, const GemmArgs &gu, const GemmArgs &dn, int P, float *hbuf, cudaStream_t st);
 
 // Expert engine. Default ("auto"): the small-batch GEMV kernels (zz_moe_dec.cu) when
-// S*K <= DEC_MAX_PAIRS, else the int8 tcgen05 engine (zz_moe_i8.cu) where the layer's
-// shape allows it, else the int8 mma.sync GEMM (k_gemm<..., S8>).
-// ZZ_MOE_KERNEL=dec|i8|mma8 forces one where it applies. All are exact per block.
+// S*K <= DEC_MAX_PAIRS, else the int8 mma.sync GEMM (k_gemm<..., S8>), the fastest
+// measured. ZZ_MOE_KERNEL=i8 selects the int8 tcgen05 engine (zz_moe_i8.cu) where the
+// layer's shape allows it, =mma8 the mma.sync GEMM for every call size. All are exact
+// per block.
 enum { ENG_DEC = 0, ENG_MMA8 = 3, ENG_I8 = 5 };
 constexpr int DEC_MAX_PAIRS = 64;
 static int moe_engine(int P, const zz_expert_bank *b) {
@@ -54,7 +55,7 @@ static int moe_engine(int P, const zz_expert_bank *b) {
     if (e && !strcmp(e, "i8")) return i8_ok ? ENG_I8 : ENG_MMA8;
     // the decode kernels take calls of up to DEC_MAX_PAIRS pairs
     if (P <= DEC_MAX_PAIRS) return ENG_DEC;
-    return i8_ok ? ENG_I8 : ENG_MMA8;
+    return ENG_MMA8;
 }
 constexpr int I8_BN = 128;
 
@@ -555,7 +556,6 @@ extern "C" int zz_moe_ffn_q8_dev(const zz_expert_bank *b, const int8_t *xq, cons
 // running where an allocation could stall or fail mid-request. For them the layer's
 // scratch lives in this file-scope array instead of a caller workspace. It is part of
 // the library image, so every GPU that loads the library holds these bytes until exit.
-#define ZZ_NOALLOC_SCRATCH_BYTES (32u << 20)
 static __device__ __align__(256) uint8_t g_noalloc_scratch[ZZ_NOALLOC_SCRATCH_BYTES];
 
 // Device address of g_noalloc_scratch per device. Host code must not pass the symbol

@@ -69,8 +69,8 @@ constexpr int ND = 4;
 constexpr int DX_STAGE = KB * BN * 4;
 constexpr int NW = 4;
 constexpr int W_SLOT = 128 * KB * 2;
-constexpr int CTG = BN + 4;          // gate/up exchange: 64 up rows x 128 columns
-constexpr int CT_BYTES = 64 * CTG * 4;
+constexpr int CTX = 64 + 1;          // tile-end exchange: 128 rows x 64 columns
+constexpr int CT_BYTES = 128 * CTX * 4;
 constexpr int OFF_A = 0;             // 1 KB aligned (swizzled destinations)
 constexpr int OFF_B = OFF_A + NS * A_STAGE;
 constexpr int OFF_RING = OFF_B + RB * B_STAGE;
@@ -104,6 +104,22 @@ __device__ __forceinline__ void tmem_st16_bias(uint32_t taddr) {
         "r"(b)
         : "memory");
 }
+// tcgen05.wait::ld that also names the loaded registers, so no use of them can be
+// scheduled before the wait
+__device__ __forceinline__ void tmem_ld_wait_regs(uint32_t (&v)[4][16]) {
+    asm volatile("tcgen05.wait::ld.sync.aligned;"
+                 : "+r"(v[0][0]), "+r"(v[0][1]), "+r"(v[0][2]), "+r"(v[0][3]), "+r"(v[0][4]), "+r"(v[0][5]), "+r"(v[0][6]), "+r"(v[0][7]), "+r"(v[0][8]), "+r"(v[0][9]), "+r"(v[0][10]), "+r"(v[0][11]), "+r"(v[0][12]), "+r"(v[0][13]), "+r"(v[0][14]), "+r"(v[0][15]), "+r"(v[1][0]), "+r"(v[1][1]), "+r"(v[1][2]), "+r"(v[1][3]), "+r"(v[1][4]), "+r"(v[1][5]), "+r"(v[1][6]), "+r"(v[1][7]), "+r"(v[1][8]), "+r"(v[1][9]), "+r"(v[1][10]), "+r"(v[1][11]), "+r"(v[1][12]), "+r"(v[1][13]), "+r"(v[1][14]), "+r"(v[1][15]), "+r"(v[2][0]), "+r"(v[2][1]), "+r"(v[2][2]), "+r"(v[2][3]), "+r"(v[2][4]), "+r"(v[2][5]), "+r"(v[2][6]), "+r"(v[2][7]), "+r"(v[2][8]), "+r"(v[2][9]), "+r"(v[2][10]), "+r"(v[2][11]), "+r"(v[2][12]), "+r"(v[2][13]), "+r"(v[2][14]), "+r"(v[2][15]), "+r"(v[3][0]), "+r"(v[3][1]), "+r"(v[3][2]), "+r"(v[3][3]), "+r"(v[3][4]), "+r"(v[3][5]), "+r"(v[3][6]), "+r"(v[3][7]), "+r"(v[3][8]), "+r"(v[3][9]), "+r"(v[3][10]), "+r"(v[3][11]), "+r"(v[3][12]), "+r"(v[3][13]), "+r"(v[3][14]), "+r"(v[3][15])
+                 :
+                 : "memory");
+}
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(
+            taddr),
+        "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
+        "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+        : "memory");
+}
 __device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
 // K-major operand in 128-byte-swizzled atoms (8 rows x 128 bytes, 1024 bytes apart):
@@ -122,10 +138,19 @@ __device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t addr) {
 __host__ __device__ constexpr uint32_t idesc_i8(int M, int N) {
     return (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
 }
+#ifndef ZZ_I8_PRESET
+#define ZZ_I8_PRESET 1
+#endif
 __device__ __forceinline__ void mma_i8_acc(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc) {
+#if ZZ_I8_PRESET
     asm volatile("tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, 1;" ::"r"(tmem_d), "l"(adesc), "l"(bdesc),
                  "r"(idesc)
                  : "memory");
+#else
+    asm volatile("tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, 0;" ::"r"(tmem_d), "l"(adesc), "l"(bdesc),
+                 "r"(idesc)
+                 : "memory");
+#endif
 }
 
 __device__ __forceinline__ int np2_of(int count) {
@@ -175,11 +200,27 @@ __device__ __forceinline__ int colw_of(int count) { return max(32, np2_of(count)
 // dx * (dw * I) of one slot's 16 columns into the sums `s` (fp32 pairs)
 __device__ __forceinline__ void scale_slot(float2 (&s)[8], const uint32_t (&v)[16], float2 dw2, float2 c2,
                                            const float *dxb) {
+#ifdef ZZ_SCALE_SCALAR
 #pragma unroll
     for (int k4 = 0; k4 < 4; k4++) {
         const float4 d4 = *reinterpret_cast<const float4 *>(dxb + 4 * k4);
+        s[2 * k4].x = fmaf(fmaf(__uint_as_float(v[4 * k4]), dw2.x, c2.x), d4.x, s[2 * k4].x);
+        s[2 * k4].y = fmaf(fmaf(__uint_as_float(v[4 * k4 + 1]), dw2.x, c2.x), d4.y, s[2 * k4].y);
+        s[2 * k4 + 1].x = fmaf(fmaf(__uint_as_float(v[4 * k4 + 2]), dw2.x, c2.x), d4.z, s[2 * k4 + 1].x);
+        s[2 * k4 + 1].y = fmaf(fmaf(__uint_as_float(v[4 * k4 + 3]), dw2.x, c2.x), d4.w, s[2 * k4 + 1].y);
+    }
+    return;
+#endif
+#pragma unroll
+    for (int k4 = 0; k4 < 4; k4++) {
+        const float4 d4 = *reinterpret_cast<const float4 *>(dxb + 4 * k4);
+#if ZZ_I8_PRESET
         const float2 f0 = make_float2(__uint_as_float(v[4 * k4]), __uint_as_float(v[4 * k4 + 1]));
         const float2 f1 = make_float2(__uint_as_float(v[4 * k4 + 2]), __uint_as_float(v[4 * k4 + 3]));
+#else
+        const float2 f0 = make_float2(__uint_as_float(v[4 * k4] + i8k::BIAS), __uint_as_float(v[4 * k4 + 1] + i8k::BIAS));
+        const float2 f1 = make_float2(__uint_as_float(v[4 * k4 + 2] + i8k::BIAS), __uint_as_float(v[4 * k4 + 3] + i8k::BIAS));
+#endif
         // fma(F, dw, -M*dw) = dw * I rounded once; then + dx * (dw * I)
         s[2 * k4] = ffma2(ffma2(f0, dw2, c2), make_float2(d4.x, d4.y), s[2 * k4]);
         s[2 * k4 + 1] = ffma2(ffma2(f1, dw2, c2), make_float2(d4.z, d4.w), s[2 * k4 + 1]);
@@ -196,6 +237,24 @@ __device__ __forceinline__ void epi_tile(const GemmArgs &a, const I8Ctx &c, cons
     const uint32_t lane_base = (uint32_t)(q * 32) << 16;
     const int ncols = it.count;
     const int cw = colw_of(ncols), G = BN / cw, cpw = cw / 32;
+    const int lg_cpw = cpw == 4 ? 2 : cpw == 2 ? 1 : 0, lg_g = G == 4 ? 2 : G == 2 ? 1 : 0;
+    // per slot (fixed for the tile): block within the group, chunk, column offset, and
+    // whether any of the chunk's columns holds a row -- shifts only, no division
+    int s_sub[4], s_col[4];
+    bool s_live[4];
+#pragma unroll
+    for (int sl = 0; sl < 4; sl++) {
+        const int ch = sl & (cpw - 1);
+        s_sub[sl] = sl >> lg_cpw;
+        s_col[sl] = s_sub[sl] * cw + 16 * ch;
+        s_live[sl] = h * (cw / 2) + 16 * ch < ncols;
+    }
+    float4 *dwtab = reinterpret_cast<float4 *>(c.smem + OFF_CT);
+    static_assert(KB * 256 * 16 <= CT_BYTES, "dw table");
+    // the TMEM preset held in 16 registers (one tcgen05.st operand vector)
+    uint32_t bz[16];
+#pragma unroll
+    for (int i = 0; i < 16; i++) asm volatile("mov.b32 %0, %1;" : "=r"(bz[i]) : "n"(BIAS));
     float2 acc[4][8];
 #pragma unroll
     for (int i = 0; i < 4; i++)
@@ -204,6 +263,7 @@ __device__ __forceinline__ void epi_tile(const GemmArgs &a, const I8Ctx &c, cons
 
 #pragma unroll 1
     for (int ss = 0; ss < c.nss; ss++, g++) {
+        TC_PROF_T(p_pro);
         const int ds = g % ND, ws = g % NW;
         const int nbl = min(KB, c.nb - ss * KB);
         uint4 dwr = make_uint4(0, 0, 0, 0);
@@ -216,132 +276,184 @@ __device__ __forceinline__ void epi_tile(const GemmArgs &a, const I8Ctx &c, cons
             __syncwarp();
             if (lane == 0) tc::mbar_arrive(&c.wempty[ws]);
         }
+        // this thread's (dw, dw, -M dw, -M dw) of the stage's 8 blocks, read back per slot
+        // as the packed operands (a thread-private table in the tile-end exchange area)
+#pragma unroll
+        for (int jb = 0; jb < KB; jb++) {
+            float dw = 1.f;
+            if (HAS_DW) {
+                const uint32_t wv = jb < 2 ? dwr.x : jb < 4 ? dwr.y : jb < 6 ? dwr.z : dwr.w;
+                const __half2 hw = *reinterpret_cast<const __half2 *>(&wv);
+                dw = (jb & 1) ? __high2float(hw) : __low2float(hw);
+                if (FMT == GPU_FMT_Q40) dw *= 0.0625f;  // codes carry 16 (q - 8)
+            }
+            dwtab[jb * 256 + tid] = make_float4(dw, dw, -BIAS_F * dw, -BIAS_F * dw);  // exact
+        }
+        TC_PROF_ADD(44, p_pro);
         const bool dok = tc::mbar_wait(&c.dfull[ds], (g / ND) & 1, c.abort_flag, err, 9);
         const float *dxs = reinterpret_cast<const float *>(c.smem + OFF_DX + ds * DX_STAGE);
-        const int ngr = (nbl + G - 1) / G;
+        const int ngr = (nbl + G - 1) >> lg_g;
 #pragma unroll 1
         for (int gi = 0; gi < ngr; gi++, gg++) {
+            TC_PROF_T(p_grp);
+            TC_PROF_T(p_tf);
             const int p = gg % NGRP;
             bool ok = tc::mbar_wait(&c.tfull[p], (gg / NGRP) & 1, c.abort_flag, err, 8) && dok;
             ok = __all_sync(0xffffffffu, ok);  // tcgen05.ld / st are warp-collective
             tc::tc_fence_after();
+            TC_PROF_ADD(48, p_tf);
             const uint32_t gcol = c.tbase + lane_base + (uint32_t)(p * BN + h * (cw / 2));
+            // the group's 4 slots: load all, one wait, preset the columns again and release
+            // the group to the MMA, then scale into the sums while the next MMAs run
+            uint32_t v[4][16];
+            bool val[4];
+            int jbs[4];
+            TC_PROF_T(p_ldi);
 #pragma unroll
-            for (int half = 0; half < 2; half++) {
-                uint32_t v[2][16];
-                bool val[2];
-                int jbs[2];
-                uint32_t col[2];
-#pragma unroll
-                for (int u = 0; u < 2; u++) {
-                    const int sl = 2 * half + u, sub = sl / cpw, ch = sl % cpw;
-                    jbs[u] = gi * G + sub;
-                    col[u] = (uint32_t)(sub * cw + 16 * ch);
-                    val[u] = ok && jbs[u] < nbl && h * (cw / 2) + 16 * ch < ncols;
-                    if (val[u]) tmem_ld16(gcol + col[u], v[u]);
-                }
-                tc::tmem_ld_wait();
-#pragma unroll
-                for (int u = 0; u < 2; u++) {
-                    if (!val[u]) continue;
-                    const int sl = 2 * half + u, jb = jbs[u];
-                    tmem_st16_bias(gcol + col[u]);
-                    float dw = 1.f;
-                    if (HAS_DW) {
-                        const uint32_t wv = jb < 4 ? (jb < 2 ? dwr.x : dwr.y) : (jb < 6 ? dwr.z : dwr.w);
-                        const __half2 hw = *reinterpret_cast<const __half2 *>(&wv);
-                        dw = (jb & 1) ? __high2float(hw) : __low2float(hw);
-                        if (FMT == GPU_FMT_Q40) dw *= 0.0625f;  // codes carry 16 (q - 8)
-                    }
-                    const float2 dw2 = make_float2(dw, dw);
-                    const float2 c2 = make_float2(-BIAS_F * dw, -BIAS_F * dw);  // exact
-                    const float *dxb = dxs + jb * BN + h * (cw / 2) + 16 * (sl % cpw);
-                    // chunk sl % cpw of the warp's columns, with register indices fixed per branch
-                    if (sl == 0) scale_slot(acc[0], v[u], dw2, c2, dxb);
-                    else if (sl == 1) { if (cpw == 1) scale_slot(acc[0], v[u], dw2, c2, dxb); else scale_slot(acc[1], v[u], dw2, c2, dxb); }
-                    else if (sl == 2) { if (cpw == 4) scale_slot(acc[2], v[u], dw2, c2, dxb); else scale_slot(acc[0], v[u], dw2, c2, dxb); }
-                    else { if (cpw == 4) scale_slot(acc[3], v[u], dw2, c2, dxb); else if (cpw == 2) scale_slot(acc[1], v[u], dw2, c2, dxb); else scale_slot(acc[0], v[u], dw2, c2, dxb); }
-                }
+            for (int sl = 0; sl < 4; sl++) {
+                jbs[sl] = (gi << lg_g) + s_sub[sl];
+                val[sl] = ok && jbs[sl] < nbl && s_live[sl];
+                if (val[sl]) tmem_ld16(gcol + (uint32_t)s_col[sl], v[sl]);
             }
+            TC_PROF_ADD(46, p_ldi);
+            TC_PROF_T(p_ld);
+            tmem_ld_wait_regs(v);
+            TC_PROF_ADD(40, p_ld);
+            TC_PROF_T(p_sti);
+#pragma unroll
+            for (int sl = 0; sl < 4; sl++)
+                if (ZZ_I8_PRESET && val[sl]) tmem_st16(gcol + (uint32_t)s_col[sl], bz);
+            TC_PROF_ADD(47, p_sti);
+            TC_PROF_T(p_st);
             tmem_st_wait();
+            TC_PROF_ADD(42, p_st);
+            TC_PROF_T(p_arr);
             tc::tc_fence_before();
             __syncwarp();
             if (lane == 0) tc::mbar_arrive(&c.tempty[p]);  // the group's columns are read and preset again
+            TC_PROF_ADD(49, p_arr);
+            TC_PROF_T(p_cmp);
+#pragma unroll
+            for (int sl = 0; sl < 4; sl++) {
+                if (!val[sl]) continue;
+                const int jb = jbs[sl];
+                const float4 t4 = dwtab[jb * 256 + tid];
+                const float2 dw2 = make_float2(t4.x, t4.y), c2 = make_float2(t4.z, t4.w);
+                const float *dxb = dxs + jb * BN + h * (cw / 2) + 16 * (sl & (cpw - 1));
+                // chunk sl % cpw of the warp's columns, with register indices fixed per branch
+                if (sl == 0) scale_slot(acc[0], v[sl], dw2, c2, dxb);
+                else if (sl == 1) { if (cpw == 1) scale_slot(acc[0], v[sl], dw2, c2, dxb); else scale_slot(acc[1], v[sl], dw2, c2, dxb); }
+                else if (sl == 2) { if (cpw == 4) scale_slot(acc[2], v[sl], dw2, c2, dxb); else scale_slot(acc[0], v[sl], dw2, c2, dxb); }
+                else { if (cpw == 4) scale_slot(acc[3], v[sl], dw2, c2, dxb); else if (cpw == 2) scale_slot(acc[1], v[sl], dw2, c2, dxb); else scale_slot(acc[0], v[sl], dw2, c2, dxb); }
+            }
+            TC_PROF_ADD(41, p_cmp);
+            TC_PROF_ADD(45, p_grp);
         }
         __syncwarp();
         if (lane == 0) tc::mbar_arrive(&c.dempty[ds]);
     }
 
+    TC_PROF_T(p_end);
     // ---------------- tile end: this thread holds columns cbase .. cbase + cw/2 - 1 ----------------
+    // Both outputs go through shared memory in halves of 64 columns (CTX = 65 floats per
+    // row: writes along rows and reads along columns are both bank-conflict free), so all
+    // 256 epilogue threads take part: gate/up requantizes one (32-feature block, token)
+    // per thread, down adds 4 output rows per float4 reduction.
     float *ct = reinterpret_cast<float *>(c.smem + OFF_CT);
     const bool live = !*c.abort_flag;
     const int cbase = h * (cw / 2), cend = min(ncols, cbase + cw / 2);
     const float *alpha = FMT == GPU_FMT_TQ2 ? reinterpret_cast<const float *>(reinterpret_cast<const uint8_t *>(a.scale) +
                                                                               (long)it.group * a.scale_gstride)
                                             : nullptr;
-    if (EPI == EPI_GATEUP) {
-        // rows 0-63 are the gate rows and 64-127 the up rows of the same 64 features
-        const int MI = a.O / 2, nbh = MI / 32, f0 = (m0 / 128) * 64;
-        if (q >= 2) {
+    const int nhalf = ncols > 64 ? 2 : 1;
+    tc::named_sync(1, 256);  // every thread is past its last read of the dw table
+    for (int hc = 0; hc < nhalf; hc++) {
+        // this thread's sums of columns [64 hc, 64 hc + 64) into the tile [row][column]
 #pragma unroll
-            for (int i = 0; i < 32; i++)
-                if (cbase + 2 * i < cend)
-                    *reinterpret_cast<float2 *>(ct + ((q - 2) * 32 + lane) * CTG + cbase + 2 * i) = acc[i >> 3][i & 7];
+        for (int i = 0; i < 32; i++) {
+            const int col = cbase + 2 * i;
+            if (col >= 64 * hc && col < 64 * hc + 64 && col < cend) {
+                const float2 v = acc[i >> 3][i & 7];
+                ct[(q * 32 + lane) * CTX + col - 64 * hc] = v.x;
+                ct[(q * 32 + lane) * CTX + col + 1 - 64 * hc] = v.y;
+            }
         }
         tc::named_sync(1, 256);
-        if (q < 2 && live) {
-            const int fl = q * 32 + lane;  // feature within the tile
-            const float ag = FMT == GPU_FMT_TQ2 ? alpha[m0 + fl] : 0.f, au = FMT == GPU_FMT_TQ2 ? alpha[m0 + 64 + fl] : 0.f;
-            const int blk = f0 / 32 + q;
+        if (live) {
+            if (EPI == EPI_GATEUP) {
+                // rows 0-63 gate and 64-127 up of the same 64 features; thread = (block qb of
+                // 32 features, column): h = act(gate, up), then the q8_0 block (q40.h:124-138)
+                const int MI = a.O / 2, nbh = MI / 32, f0 = (m0 / 128) * 64;
+                const int n = tid & 63, qb = tid >> 6, col = 64 * hc + n;
+                if (qb < 2 && col < ncols) {
+                    const size_t pr = (size_t)(it.row0 + col);
+                    const float tot = FMT == GPU_FMT_TQ2 ? a.xsx[a.pair_src[pr] / a.K] : 0.f;
+                    float hv[32];
+                    float amax = 0.f;
 #pragma unroll
-            for (int k = 0; k < 64; k++) {
-                const int col = cbase + k;
-                if (col >= cend) break;  // warp-uniform
-                const size_t pr = (size_t)(it.row0 + col);
-                float gv = (k & 1) ? acc[k >> 4][(k >> 1) & 7].y : acc[k >> 4][(k >> 1) & 7].x;
-                float uv = ct[fl * CTG + col];
-                if (FMT == GPU_FMT_TQ2) {
-                    const float tot = a.xsx[a.pair_src[pr] / a.K];
-                    gv = ag * (gv - tot);
-                    uv = au * (uv - tot);
-                }
-                float d;
-                const int8_t qv = quant_lane(gated_act(a.act, gv, uv, a.clamp), d);
-                a.hq[pr * MI + f0 + fl] = qv;
-                if (FMT == GPU_FMT_TQ2) {
-                    int s = qv;
+                    for (int j = 0; j < 32; j++) {
+                        const int fl = 32 * qb + j;
+                        float gv = ct[fl * CTX + n], uv = ct[(64 + fl) * CTX + n];
+                        if (FMT == GPU_FMT_TQ2) {
+                            gv = alpha[m0 + fl] * (gv - tot);
+                            uv = alpha[m0 + 64 + fl] * (uv - tot);
+                        }
+                        hv[j] = gated_act(a.act, gv, uv, a.clamp);
+                        amax = fmaxf(amax, fabsf(hv[j]));
+                    }
+                    const float d = __fdiv_rn(amax, 127.0f);
+                    const float id = d != 0.f ? __fdiv_rn(1.0f, d) : 0.0f;
+                    uint32_t w[8];
+                    int qs = 0;
 #pragma unroll
-                    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-                    if (lane == 0) a.hblk[pr * nbh + blk] = s;
-                }
-                if (lane == 0) {
+                    for (int j4 = 0; j4 < 8; j4++) {
+                        uint32_t word = 0;
+#pragma unroll
+                        for (int k = 0; k < 4; k++) {
+                            int qv = __float2int_rn(__fmul_rn(hv[4 * j4 + k], id));
+                            qv = qv < -127 ? -127 : (qv > 127 ? 127 : qv);
+                            qs += qv;
+                            word |= (uint32_t)(qv & 0xFF) << (8 * k);
+                        }
+                        w[j4] = word;
+                    }
+                    uint4 *dst = reinterpret_cast<uint4 *>(a.hq + pr * MI + f0 + 32 * qb);
+                    dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
+                    dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
+                    const int blk = f0 / 32 + qb;
                     a.hs[pr * nbh + blk] = d;
                     a.hsT[(size_t)blk * a.ldT + pr] = d;
+                    if (FMT == GPU_FMT_TQ2) a.hblk[pr * nbh + blk] = qs;
+                }
+            } else {
+                // OUT[token, m0 + 4 o4 .. + 3] += w * C, lanes along the rows (each warp
+                // instruction covers 512 contiguous bytes of one token's output row)
+                const int nbh = a.I / 32;
+                for (int task = tid; task < 32 * 64; task += 256) {
+                    const int o4 = task & 31, n = task >> 5, col = 64 * hc + n;
+                    if (col >= ncols) break;  // n grows with task
+                    const int pr = it.row0 + col;
+                    float4 v = make_float4(ct[(4 * o4) * CTX + n], ct[(4 * o4 + 1) * CTX + n], ct[(4 * o4 + 2) * CTX + n],
+                                           ct[(4 * o4 + 3) * CTX + n]);
+                    const int o = m0 + 4 * o4;
+                    if (FMT == GPU_FMT_TQ2) {
+                        // Sx of the requantized hidden row, summed as tq2_quant_act does (tq2.h:103-107)
+                        double t = 0;
+                        for (int b = 0; b < nbh; b++)
+                            t += (double)a.xs[(size_t)pr * nbh + b] * (double)a.xblk[(size_t)pr * nbh + b];
+                        const float tot = (float)t;
+                        v.x = alpha[o] * (v.x - tot); v.y = alpha[o + 1] * (v.y - tot);
+                        v.z = alpha[o + 2] * (v.z - tot); v.w = alpha[o + 3] * (v.w - tot);
+                    }
+                    const float wgt = a.pair_w[pr];
+                    v.x *= wgt; v.y *= wgt; v.z *= wgt; v.w *= wgt;
+                    atomicAdd(reinterpret_cast<float4 *>(a.out + (size_t)(a.pair_src[pr] / a.K) * a.O + o), v);
                 }
             }
         }
         tc::named_sync(1, 256);
-    } else if (live) {  // EPI_DOWN: OUT[token, o] += w * C, lanes along o (coalesced reductions)
-        const int o = m0 + q * 32 + lane;
-        const float al = FMT == GPU_FMT_TQ2 ? alpha[o] : 0.f;
-        const int nbh = a.I / 32;
-#pragma unroll
-        for (int k = 0; k < 64; k++) {
-            const int col = cbase + k;
-            if (col >= cend) break;
-            const int pr = it.row0 + col;
-            float v = (k & 1) ? acc[k >> 4][(k >> 1) & 7].y : acc[k >> 4][(k >> 1) & 7].x;
-            if (FMT == GPU_FMT_TQ2) {
-                // Sx of the requantized hidden row, summed as tq2_quant_act does (tq2.h:103-107)
-                double t = 0;
-                for (int b = 0; b < nbh; b++)
-                    t += (double)a.xs[(size_t)pr * nbh + b] * (double)a.xblk[(size_t)pr * nbh + b];
-                v = al * (v - (float)t);
-            }
-            const int tok = a.pair_src[pr] / a.K;
-            atomicAdd(a.out + (size_t)tok * a.O + o, a.pair_w[pr] * v);
-        }
     }
+    TC_PROF_ADD(43, p_end);
 }
 
 template <int FMT, int EPI>
@@ -404,6 +516,7 @@ __global__ void __launch_bounds__(i8k::NTHREADS, 1)
     tc::tc_fence_before();
     __syncthreads();
     tc::tc_fence_after();
+    TC_PROF_T(prof_t0);
     if (warp >= 12) {
       asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(REG_COPY));
       if (warp == 12) {
@@ -506,7 +619,7 @@ __global__ void __launch_bounds__(i8k::NTHREADS, 1)
                     const uint32_t sa = tc::smem_u32(smem + OFF_A + st * A_STAGE);
                     const uint32_t sb = tc::smem_u32(smem + OFF_B + bs * B_STAGE);
                     for (int jb = 0; jb < nbl; jb++) {
-                        const int sub = jb % G, p = gg % NGRP;
+                        const int sub = jb & (G - 1), p = gg % NGRP;
                         if (sub == 0 && gg >= NGRP &&
                             !tc::mbar_wait(&c.tempty[p], ((gg / NGRP) - 1) & 1, c.abort_flag, err, 6)) {
                             ok = false;
@@ -585,6 +698,12 @@ __global__ void __launch_bounds__(i8k::NTHREADS, 1)
             epi_tile<FMT, EPI>(a, c, it, m0, g, gg, err);
         }
     }
+#ifdef ZZ_TC_PROF
+    // per-role span from set-up to here: 32 epilogue, 33 producers, 34 code TMA, 35 B TMA, 36 MMA
+    if (blockIdx.x == 0 && lane == 0 && warp < 15)
+        atomicAdd(&tc::g_tc_prof[32 + (warp < 8 ? 0 : warp < 12 ? 1 : warp - 10)],
+                  (unsigned long long)(clock64() - prof_t0));
+#endif
     tc::tc_fence_before();
     __syncthreads();
     if (warp == 14) {
@@ -694,3 +813,15 @@ int launch_moe_i8(int fmt, int epi, const GemmArgs &a, int n_groups, int *err, c
 }
 
 }  // namespace zz
+
+#ifdef ZZ_TC_PROF
+// diagnostic build only: this translation unit's wait-site cycle totals (block 0), read
+// and cleared
+extern "C" int zz_i8_prof_read(unsigned long long *out) {
+    cudaDeviceSynchronize();
+    cudaMemcpyFromSymbol(out, zz::tc::g_tc_prof, sizeof(unsigned long long) * 128);
+    unsigned long long z[128] = {0};
+    cudaMemcpyToSymbol(zz::tc::g_tc_prof, z, sizeof z);
+    return 1;
+}
+#endif

@@ -84,11 +84,20 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, volati
 #endif
     if (mbar_try(bar, parity)) return true;
     const unsigned long long w0 = global_ns();
+    // try_wait with a short back-off: a waiting warp sleeps between tries instead of
+    // taking issue slots from the warps doing the work (a suspend-time hint on the try
+    // itself can sleep well past the phase change); the sleep grows from 32 to 256 ns.
+    // The clock and the abort flag are read every 16 tries.
+    uint32_t ns = 32;
     for (;;) {
 #ifdef ZZ_TC_PROF
         if (blockIdx.x == 0 && (threadIdx.x & 31) == 0) atomicAdd(&g_tc_prof[64 + code], 1ull);
 #endif
-        if (mbar_try_suspend(bar, parity, SUSPEND_NS)) return true;
+        for (int i = 0; i < 16; i++) {
+            __nanosleep(ns);
+            if (mbar_try(bar, parity)) return true;
+            ns = ns < 256 ? 2 * ns : 256;
+        }
         if (*abort) return false;
         if (global_ns() - w0 > WAIT_LIMIT_NS) break;
     }
