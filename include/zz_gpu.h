@@ -4,10 +4,14 @@
  * Two layers:
  *  1. The reference's backend surface, unchanged in name, signature and 1/0 decline
  *     convention (reference gpu.h:61-84), so an engine built against gpu.h links this
- *     library in place of metal.o. Activations cross it as host f32 and are quantized
- *     ON DEVICE exactly like q40_quant_act (q40.h:124-138); the dots are the integer
- *     q40_dot / q80_dot / tq2_dot (q40.h:188, 374; tq2.h:134), so results match the
- *     engines' default int8-activation CPU build.
+ *     library in place of metal.o. Activations cross it as host f32. By default the
+ *     matmuls keep them f32, as the reference's GPU backend does (gpu.h:25-30), so they
+ *     match q40_dot_f32 / q80_dot_f32 / tq2_dot_f32 / q4a_dot_f32 and the engines'
+ *     --check-gpu (gemma4.c:2315-2361) passes; zz_gpu_set_act_quant(1) switches to
+ *     quantizing them ON DEVICE exactly like q40_quant_act (q40.h:124-138) and the
+ *     integer dots q40_dot / q80_dot / tq2_dot / q4a_dot (q40.h:188, 374; tq2.h:134,
+ *     395), the engines' default int8-activation CPU build. The q8_0-activation
+ *     kernel signatures of q40.h / tq2.h are added as gpu_*_matvec.
  *  2. Device-pointer entry points (zz_*) for callers that keep weights, activations and
  *     outputs resident in HBM: no host copies, explicit caller-provided workspace, an
  *     explicit stream (a cudaStream_t passed as void*; NULL = legacy default stream).
@@ -59,11 +63,29 @@ int gpu_map(const void *p, size_t n);
 int gpu_unmap(const void *p);
 /* replaces gpu_q40_matmul (gpu.h:75): y[S,O] = W[O,I] (q4_0) x[S,I]; host y and x */
 int gpu_q40_matmul(float *y, const uint8_t *W, const float *x, int O, int I, int S);
-/* replaces gpu_matmul (gpu.h:84) for GPU_FMT_Q40, Q80 and TQ2 (W is the whole tq2
- * tensor, alphas first). GPU_FMT_Q4A declines. I % 32 (q4_0/q8_0) or I % 64 (tq2). */
+/* replaces gpu_matmul (gpu.h:84) for GPU_FMT_Q40, Q80, TQ2 (W is the whole tq2 tensor,
+ * alphas first) and Q4A (tq2.h:268-283). I % 32 (q4_0/q8_0) or I % 64 (tq2, q4a). */
 int gpu_matmul(int fmt, float *y, const uint8_t *W, const float *x, int O, int I, int S);
 /* added: why the last call declined ("" if it did not). */
 const char *gpu_last_error(void);
+/* added: numerics of gpu_q40_matmul / gpu_matmul. 0 (default): f32 activations, the
+ * reference GPU backend's (gpu.h:25-30; metal.mm:43-45); 1: activations quantized to
+ * q8_0 on device and the integer dots, bit-for-bit the engines' CPU kernels per block.
+ * No reference counterpart (the Metal backend has only the first). */
+int zz_gpu_set_act_quant(int on);
+
+/* q8_0-activation matvecs on host buffers, W inside a gpu_map'd region: the kernel-level
+ * signatures an engine's matvec calls, y[o] = dot(W row o, xq, sx) for o < O.
+ *   gpu_q40_matvec replaces q40_matvec (q40.h:308-312); gpu_q80_matvec replaces
+ *   q80_matvec (q40.h:456-460); gpu_tq2_matvec is the row loop maple runs through
+ *   tq2_dot (maple.c:387-398, tq2.h:134) with W the whole tq2 tensor (tq2.h:85-91) and
+ *   sxtot = tq2_quant_act's return; gpu_q4a_matvec is the same loop over q4a_dot
+ *   (tq2.h:395). The names carry a gpu_ prefix because the reference's own are static
+ *   inline in its headers. */
+int gpu_q40_matvec(float *y, const uint8_t *W, const int8_t *xq, const float *sx, int O, int I);
+int gpu_q80_matvec(float *y, const uint8_t *W, const int8_t *xq, const float *sx, int O, int I);
+int gpu_tq2_matvec(float *y, const uint8_t *W, const int8_t *xq, const float *sx, float sxtot, int O, int I);
+int gpu_q4a_matvec(float *y, const uint8_t *W, const int8_t *xq, const float *sx, int O, int I);
 
 /* ---------- 2. device-resident entry points ---------- */
 
@@ -72,6 +94,8 @@ const char *gpu_last_error(void);
  *         order), scale = O x I/32 fp16 block scales
  *   q8_0: codes = O rows of I int8,  scale = O x I/32 fp16
  *   tq2 : codes = O rows of I/4 bytes (the reference packing), scale = O f32 alphas
+ *   q4a : codes = O rows of I/2 bytes (each 64-weight group's two 16-byte nibble
+ *         blocks), scale = O x I/64 (fp16 d, fp16 m) pairs (tq2.h:268-283)
  * Row strides are exactly those widths; planes start 256-byte aligned. */
 typedef struct zz_qtensor {
     int fmt, O, I;
@@ -100,11 +124,17 @@ int zz_quant_rows_dev(int fmt, const float *w, int O, int I, uint8_t *dst, void 
 int zz_quant_act_dev(const float *x, int S, int I, int8_t *xq, float *sx, float *sxtot,
                      void *stream);
 
-/* replaces q40_matvec / q80_matvec (q40.h:308, 456) and the tq2 row loop that maple
- * runs through w_dot (maple.c:387-398): y[S, O] = W . (xq, sx) for S quantized rows.
- * sxtot is required for tq2 and ignored otherwise. */
+/* replaces q40_matvec / q80_matvec (q40.h:308, 456), the tq2 row loop that maple
+ * runs through w_dot (maple.c:387-398) and its q4a counterpart (q4a_dot, tq2.h:395):
+ * y[S, O] = W . (xq, sx) for S quantized rows. sxtot is required for tq2 and ignored
+ * otherwise. */
 int zz_matvec_dev(const zz_qtensor *W, const int8_t *xq, const float *sx, const float *sxtot,
                   float *y, int S, void *stream);
+
+/* the f32-activation matvec (q40_dot_f32 q40.h:290-305, q80_dot_f32, tq2_dot_f32
+ * tq2.h:235-252, q4a_dot_f32 tq2.h:410-432): y[S, O] = W . x for S f32 rows x [S, I]
+ * (I <= 51200). Each 32-weight block is summed in fp32 (the reference sums in double). */
+int zz_matvec_f32_dev(const zz_qtensor *W, const float *x, float *y, int S, void *stream);
 
 /* per-block integer sums for the bit-exact parity check: out[o, b] = <q_w - 8, q_x>
  * (q4_0), <q_w, q_x> (q8_0), <c, q_x> with unsigned codes (tq2), for one activation

@@ -187,6 +187,21 @@ class Oracle(_Lib):
         return out
 
 
+    def matvec_f32(self, fmt, T, O, I, x):
+        """exact-activation matvec (q40_dot_f32 / q80_dot_f32 / tq2_dot_f32 / q4a_dot_f32)"""
+        y = np.zeros(O, np.float32)
+        self.fn("matvec_f32", None, [_I, _P, _P, _P, _I, _I])(fmt, _ptr(y), _ptr(np.ascontiguousarray(T)),
+                                                              _ptr(np.ascontiguousarray(x, np.float32)), O, I)
+        return y
+
+    def q4a_matvec(self, T, O, xq, sx):
+        I = xq.shape[-1]
+        y = np.zeros(O, np.float32)
+        self.fn("q4a_matvec", None, [_P, _P, _P, _P, _I, _I])(_ptr(y), _ptr(np.ascontiguousarray(T)),
+                                                              _ptr(np.ascontiguousarray(xq)),
+                                                              _ptr(np.ascontiguousarray(sx, np.float32)), O, I)
+        return y
+
     def moe_pairs_hidden(self, kind, blobs, X, eidx, D, MI, clamp=7.0):
         """stage 1 for every routed pair: hq [S*K, MI] int8, hs [S*K, MI/32] f32"""
         X = np.ascontiguousarray(X, np.float32)

@@ -92,3 +92,6 @@ void ref_gemma4_moe_layer(const uint8_t *const *blobs, const float *X, float *OU
     }
     free(uniq); free(rows); free(wr);
 }
+
+/* exact-activation q8_0 dot (q40.h:443-455), for pinning the restatement */
+float ref_q80_dot_f32(const uint8_t *w, const float *x, int I) { return q80_dot_f32(w, x, I); }

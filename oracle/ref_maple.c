@@ -72,3 +72,9 @@ void ref_maple_moe_layer(const uint8_t *const *blobs, const float *X, float *OUT
     }
     free(uniq); free(rows); free(wr);
 }
+
+/* exact-activation tq2 and q4a dots and the q8_0-activation q4a dot (tq2.h:235-252,
+ * 390-432), for pinning the restatement */
+float ref_tq2_dot_f32(const uint8_t *codes, float alpha, const float *x, int I) { return tq2_dot_f32(codes, alpha, x, I); }
+float ref_q4a_dot_f32(const uint8_t *w, const float *x, int I) { return q4a_dot_f32(w, x, I); }
+float ref_q4a_dot(const uint8_t *w, const int8_t *xq, const float *sx, int I) { return q4a_dot(w, xq, sx, I); }

@@ -494,3 +494,113 @@ void orc_moe_pairs_combine(int kind, const uint8_t *const *blobs, int E, const i
         }
     }
 }
+
+/* ---- exact-activation dots (f32 x, double sums): what the reference's GPU backend is
+ * checked against (gemma4.c:2315-2361, maple.c:1756-1800) ---- */
+
+/* q40_dot_f32 (q40.h:290-305) */
+float orc_q40_dot_f32(const uint8_t *w, const float *x, int I) {
+    double acc = 0;
+    for (int b = 0; b < I / ORC_BLK; b++) {
+        const uint8_t *blk = w + (size_t)b * ORC_Q40_BB;
+        uint16_t hd; memcpy(&hd, blk, 2);
+        const float *v = x + b * ORC_BLK;
+        double s = 0;
+        for (int j = 0; j < 16; j++) {
+            s += (double)((int)(blk[2 + j] & 15) - 8) * v[j];
+            s += (double)((int)(blk[2 + j] >> 4) - 8) * v[j + 16];
+        }
+        acc += (double)orc_fp16_to_f32(hd) * s;
+    }
+    return (float)acc;
+}
+
+/* q80_dot_f32 (q40.h:443-455) */
+float orc_q80_dot_f32(const uint8_t *w, const float *x, int I) {
+    double acc = 0;
+    for (int b = 0; b < I / ORC_BLK; b++) {
+        const uint8_t *blk = w + (size_t)b * ORC_Q80_BB;
+        uint16_t hd; memcpy(&hd, blk, 2);
+        const int8_t *a = (const int8_t *)(blk + 2);
+        double s = 0;
+        for (int j = 0; j < ORC_BLK; j++) s += (double)a[j] * x[b * ORC_BLK + j];
+        acc += (double)orc_fp16_to_f32(hd) * s;
+    }
+    return (float)acc;
+}
+
+/* tq2_dot_f32 (tq2.h:235-252): codes of one row, 16 bytes per 64-weight group */
+float orc_tq2_dot_f32(const uint8_t *codes, float alpha, const float *x, int I) {
+    double acc = 0;
+    for (int g = 0; g < I / 64; g++) {
+        const uint8_t *c = codes + (size_t)g * 16;
+        const float *v = x + (size_t)g * 64;
+        double s = 0;
+        for (int k = 0; k < 16; k++) {
+            s += (double)((int)(c[k] & 3) - 1) * v[k];
+            s += (double)((int)((c[k] >> 2) & 3) - 1) * v[k + 16];
+            s += (double)((int)((c[k] >> 4) & 3) - 1) * v[k + 32];
+            s += (double)((int)(c[k] >> 6) - 1) * v[k + 48];
+        }
+        acc += s;
+    }
+    return (float)((double)alpha * acc);
+}
+
+/* q4a: 64-weight groups of 36 bytes, fp16 d, fp16 m, two 16-byte nibble blocks;
+ * w = d*q + m (tq2.h:268-283). q4a_dot_f32 (tq2.h:410-432) */
+float orc_q4a_dot_f32(const uint8_t *w, const float *x, int I) {
+    double acc = 0;
+    for (int g = 0; g < I / 64; g++) {
+        const uint8_t *grp = w + (size_t)g * 36;
+        uint16_t hd, hm; memcpy(&hd, grp, 2); memcpy(&hm, grp + 2, 2);
+        double d = orc_fp16_to_f32(hd), m = orc_fp16_to_f32(hm);
+        for (int h = 0; h < 2; h++) {
+            const uint8_t *nib = grp + 4 + h * 16;
+            const float *u = x + (size_t)g * 64 + h * 32;
+            double s = 0, t = 0;
+            for (int j = 0; j < 16; j++) {
+                s += (double)(nib[j] & 15) * u[j];
+                s += (double)(nib[j] >> 4) * u[j + 16];
+                t += (double)u[j] + (double)u[j + 16];
+            }
+            acc += d * s + m * t;
+        }
+    }
+    return (float)acc;
+}
+
+/* q4a_dot with q8_0 activations, the scalar form (tq2.h:390-408) */
+float orc_q4a_dot(const uint8_t *w, const int8_t *xq, const float *sx, int I) {
+    double acc = 0;
+    for (int g = 0; g < I / 64; g++) {
+        const uint8_t *grp = w + (size_t)g * 36;
+        uint16_t hd, hm; memcpy(&hd, grp, 2); memcpy(&hm, grp + 2, 2);
+        float d = orc_fp16_to_f32(hd), m = orc_fp16_to_f32(hm);
+        for (int h = 0; h < 2; h++) {
+            const uint8_t *nib = grp + 4 + h * 16;
+            const int8_t *v = xq + (size_t)g * 64 + h * 32;
+            int32_t dp = 0, sv = 0;
+            for (int j = 0; j < 16; j++) {
+                dp += (int)(nib[j] & 15) * (int)v[j];
+                dp += (int)(nib[j] >> 4) * (int)v[j + 16];
+                sv += (int)v[j] + (int)v[j + 16];
+            }
+            acc += (double)sx[2 * g + h] * ((double)d * dp + (double)m * sv);
+        }
+    }
+    return (float)acc;
+}
+
+/* y[o] for a whole tensor: fmt 1 q4_0, 2 q8_0, 3 tq2 (T = alphas then codes), 4 q4a */
+void orc_matvec_f32(int fmt, float *y, const uint8_t *T, const float *x, int O, int I) {
+    for (int o = 0; o < O; o++) {
+        if (fmt == 1) y[o] = orc_q40_dot_f32(T + (size_t)o * (I / ORC_BLK) * ORC_Q40_BB, x, I);
+        else if (fmt == 2) y[o] = orc_q80_dot_f32(T + (size_t)o * (I / ORC_BLK) * ORC_Q80_BB, x, I);
+        else if (fmt == 3) y[o] = orc_tq2_dot_f32(T + (size_t)O * 4 + (size_t)o * (I / 4), ((const float *)T)[o], x, I);
+        else y[o] = orc_q4a_dot_f32(T + (size_t)o * (I / 64) * 36, x, I);
+    }
+}
+void orc_q4a_matvec(float *y, const uint8_t *T, const int8_t *xq, const float *sx, int O, int I) {
+    for (int o = 0; o < O; o++) y[o] = orc_q4a_dot(T + (size_t)o * (I / 64) * 36, xq, sx, I);
+}

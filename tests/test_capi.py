@@ -49,7 +49,8 @@ def test_declines_without_device():
 def test_size_queries_host_only():
     assert zz.lib.zz_qtensor_bytes(zz.GPU_FMT_Q40, 2816, 2816) >= 2816 * 1408 + 2816 * 88 * 2
     assert zz.lib.zz_qtensor_bytes(zz.GPU_FMT_TQ2, 10, 96) == 0   # tq2 needs I % 64
-    assert zz.lib.zz_qtensor_bytes(zz.GPU_FMT_Q4A, 10, 64) == 0
+    assert zz.lib.zz_qtensor_bytes(zz.GPU_FMT_Q4A, 10, 64) == 512 + 256  # q4a planes, each 256-aligned
+    assert zz.lib.zz_qtensor_bytes(zz.GPU_FMT_Q4A, 10, 96) == 0   # q4a needs I % 64
     assert zz.lib.zz_expert_bank_bytes(zz.GPU_FMT_Q40, 128, 2816, 704) > 128 * 3345408 * 0.99
     assert zz.lib.zz_expert_bank_bytes(zz.GPU_FMT_Q40, 128, 2816, 700) == 0  # inter % 64
     b = zz.ExpertBank(zz.GPU_FMT_Q40, 128, 2816, 704, None, None, None, None)

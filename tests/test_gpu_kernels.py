@@ -35,11 +35,15 @@ def rel(a, b):
 def q_weights(orc, fmt, seed, O, I):
     if fmt == zz.GPU_FMT_TQ2:
         return synth.tq2_tensor(seed, O, I)
+    if fmt == zz.GPU_FMT_Q4A:
+        return synth.q4a_tensor(seed, O, I)
     w = synth.gaussian(seed, (O, I), 0.02)
     return (orc.q40_quant_rows(w) if fmt == zz.GPU_FMT_Q40 else orc.q80_quant_rows(w)).reshape(-1)
 
 
 def oracle_matvec(orc, fmt, Wb, O, I, xq, sx, tot):
+    if fmt == zz.GPU_FMT_Q4A:
+        return orc.q4a_matvec(Wb, O, xq, sx)
     if fmt == zz.GPU_FMT_Q40:
         return orc.q40_matvec(Wb.reshape(O, -1), xq, sx)
     if fmt == zz.GPU_FMT_Q80:
@@ -138,49 +142,121 @@ def test_matvec_streamed(orc, fmt, reps):
 
 
 def test_gpu_h_surface(orc):
-    """gpu_init / gpu_map / gpu_matmul exactly as an engine calls them (gemma4.c:445)."""
+    """gpu_init / gpu_map / gpu_matmul exactly as an engine calls them (gemma4.c:445):
+    by default f32 activations (the reference GPU backend's numerics, checked against
+    q40_dot_f32 & co. at 1e-4 like --check-gpu), with zz_gpu_set_act_quant(1) the q8_0
+    integer dots; and the q8_0-activation kernel signatures gpu_*_matvec."""
     L = zz.lib
     assert L.gpu_init() == 1, L.gpu_last_error()
     assert L.gpu_ready() == 1
     assert b"B200" in L.gpu_name() or b"sm_10" in L.gpu_name()
-    O, I = 300, 2816
-    W4 = q_weights(orc, zz.GPU_FMT_Q40, 30, O, I)
-    W8 = q_weights(orc, zz.GPU_FMT_Q80, 31, O, I)
-    T2 = q_weights(orc, zz.GPU_FMT_TQ2, 32, O, 2048)
-    # one page-aligned region holding all three tensors, like the dense blob
-    region = np.zeros(((W4.size + W8.size + T2.size) // 4096 + 2) * 4096, np.uint8)
-    region[:W4.size] = W4
-    region[W4.size:W4.size + W8.size] = W8
-    o2 = W4.size + W8.size
-    region[o2:o2 + T2.size] = T2
-    base = region.ctypes.data
+    O, I, It = 300, 2816, 2048
+    tens = {zz.GPU_FMT_Q40: (q_weights(orc, zz.GPU_FMT_Q40, 30, O, I), I),
+            zz.GPU_FMT_Q80: (q_weights(orc, zz.GPU_FMT_Q80, 31, O, I), I),
+            zz.GPU_FMT_TQ2: (q_weights(orc, zz.GPU_FMT_TQ2, 32, O, It), It),
+            zz.GPU_FMT_Q4A: (q_weights(orc, zz.GPU_FMT_Q4A, 33, O, It), It)}
+    # one page-aligned region holding all four tensors, like the dense blob
+    total = sum(w.size for w, _ in tens.values())
+    region = np.zeros((total // 4096 + 2) * 4096, np.uint8)
+    base, off, where = region.ctypes.data, 0, {}
+    for fmt, (w, _) in tens.items():
+        region[off:off + w.size] = w
+        where[fmt] = off
+        off += (w.size + 15) // 16 * 16
     assert L.gpu_map(ctypes.c_void_p(base), region.size) == 1, L.gpu_last_error()
-    for S in (1, 3):
-        x = synth.gaussian(33 + S, (S, I))
-        y = np.zeros((S, O), np.float32)
-        assert L.gpu_q40_matmul(y.ctypes.data, ctypes.c_void_p(base), x.ctypes.data, O, I, S) == 1, L.gpu_last_error()
-        xq, sx = orc.quant_act(x)
-        for s in range(S):
-            assert rel(y[s], orc.q40_matvec(W4.reshape(O, -1), xq[s], sx[s])) < TOL
-        y8 = np.zeros((S, O), np.float32)
-        assert L.gpu_matmul(zz.GPU_FMT_Q80, y8.ctypes.data, ctypes.c_void_p(base + W4.size), x.ctypes.data, O, I, S) == 1
-        for s in range(S):
-            assert rel(y8[s], orc.q80_matvec(W8.reshape(O, -1), xq[s], sx[s])) < TOL
-        xt = synth.gaussian(40 + S, (S, 2048))
-        yt = np.zeros((S, O), np.float32)
-        assert L.gpu_matmul(zz.GPU_FMT_TQ2, yt.ctypes.data, ctypes.c_void_p(base + o2), xt.ctypes.data, O, 2048, S) == 1
-        tq, ts, tt = orc.tq2_quant_act(xt)
-        for s in range(S):
-            assert rel(yt[s], orc.tq2_matvec(T2, O, tq[s], ts[s], tt[s])) < TOL
-    # declines: q4a, bad shape, unmapped pointer
-    y = np.zeros(8, np.float32)
-    assert L.gpu_matmul(zz.GPU_FMT_Q4A, y.ctypes.data, ctypes.c_void_p(base), y.ctypes.data, 8, 64, 1) == 0
-    assert L.gpu_matmul(zz.GPU_FMT_Q40, y.ctypes.data, ctypes.c_void_p(base), y.ctypes.data, 8, 48, 1) == 0
-    other = np.zeros(4096, np.uint8)
-    assert L.gpu_q40_matmul(y.ctypes.data, other.ctypes.data, y.ctypes.data, 1, 32, 1) == 0
-    assert b"gpu_map" in L.gpu_last_error()
-    assert L.gpu_unmap(ctypes.c_void_p(base)) == 1
+    try:
+        for S in (1, 3):
+            for fmt, (w, In) in tens.items():
+                x = synth.gaussian(33 + S + fmt, (S, In))
+                Wp = ctypes.c_void_p(base + where[fmt])
+                y = np.zeros((S, O), np.float32)
+                assert L.zz_gpu_set_act_quant(0) == 1
+                call = (L.gpu_q40_matmul(y.ctypes.data, Wp, x.ctypes.data, O, In, S) if fmt == zz.GPU_FMT_Q40
+                        else L.gpu_matmul(fmt, y.ctypes.data, Wp, x.ctypes.data, O, In, S))
+                assert call == 1, L.gpu_last_error()
+                for s in range(S):
+                    assert rel(y[s], orc.matvec_f32(fmt, w, O, In, x[s])) < TOL, (fmt, s)
+                assert L.zz_gpu_set_act_quant(1) == 1
+                y8 = np.zeros((S, O), np.float32)
+                assert L.gpu_matmul(fmt, y8.ctypes.data, Wp, x.ctypes.data, O, In, S) == 1, L.gpu_last_error()
+                xq, sx, tot = orc.tq2_quant_act(x)
+                for s in range(S):
+                    assert rel(y8[s], oracle_matvec(orc, fmt, w, O, In, xq[s], sx[s], tot[s])) < TOL, (fmt, s)
+                # the kernel-level signatures (q40.h:308, 456; tq2.h:134, 395) on host buffers
+                y1 = np.zeros(O, np.float32)
+                if fmt == zz.GPU_FMT_TQ2:
+                    ok = L.gpu_tq2_matvec(y1.ctypes.data, Wp, xq[0].ctypes.data, sx[0].ctypes.data, float(tot[0]), O, In)
+                else:
+                    f = {zz.GPU_FMT_Q40: L.gpu_q40_matvec, zz.GPU_FMT_Q80: L.gpu_q80_matvec,
+                         zz.GPU_FMT_Q4A: L.gpu_q4a_matvec}[fmt]
+                    ok = f(y1.ctypes.data, Wp, xq[0].ctypes.data, sx[0].ctypes.data, O, In)
+                assert ok == 1, L.gpu_last_error()
+                assert rel(y1, oracle_matvec(orc, fmt, w, O, In, xq[0], sx[0], tot[0])) < TOL, fmt
+        L.zz_gpu_set_act_quant(0)
+        # declines: bad shape, unmapped pointer
+        y = np.zeros(8, np.float32)
+        assert L.gpu_matmul(zz.GPU_FMT_Q4A, y.ctypes.data, ctypes.c_void_p(base), y.ctypes.data, 8, 96, 1) == 0
+        assert L.gpu_matmul(zz.GPU_FMT_Q40, y.ctypes.data, ctypes.c_void_p(base), y.ctypes.data, 8, 48, 1) == 0
+        other = np.zeros(4096, np.uint8)
+        assert L.gpu_q40_matmul(y.ctypes.data, other.ctypes.data, y.ctypes.data, 1, 32, 1) == 0
+        assert b"gpu_map" in L.gpu_last_error()
+    finally:
+        L.zz_gpu_set_act_quant(0)
+        assert L.gpu_unmap(ctypes.c_void_p(base)) == 1
     assert L.gpu_q40_matmul(y.ctypes.data, ctypes.c_void_p(base), y.ctypes.data, 1, 32, 1) == 0
+
+
+@pytest.mark.parametrize("fmt,O,I", [(zz.GPU_FMT_Q40, 2816, 2816), (zz.GPU_FMT_Q80, 64, 704), (zz.GPU_FMT_TQ2, 512, 2048),
+                                     (zz.GPU_FMT_Q4A, 4096, 2048), (zz.GPU_FMT_Q40, 7, 32 * 1599)])
+def test_matvec_f32_activations(orc, fmt, O, I):
+    """zz_matvec_f32_dev against q40_dot_f32 / q80_dot_f32 / tq2_dot_f32 / q4a_dot_f32,
+    two rows"""
+    Wb = q_weights(orc, fmt, 70, O, I)
+    x = synth.gaussian(71, (2, I))
+    t = zz.QTensorDev(fmt, dev(Wb), O, I)
+    y = torch.empty((2, O), device="cuda")
+    zz.check(zz.lib.zz_matvec_f32_dev(ctypes.byref(t.t), ctypes.c_void_p(dev(x).data_ptr()),
+                                      ctypes.c_void_p(y.data_ptr()), 2, None), "zz_matvec_f32_dev")
+    y = y.cpu().numpy()
+    for s in range(2):
+        assert rel(y[s], orc.matvec_f32(fmt, Wb, O, I, x[s])) < TOL, s
+
+
+@pytest.mark.parametrize("O,I", [(4096, 2048), (37, 128)])
+def test_q4a_repack_and_matvec(orc, O, I):
+    """q4a planes round-trip to the reference layout; the q8_0-activation matvec matches
+    q4a_dot (tq2.h:390-408) at 1e-4 for 1 and 3 rows"""
+    Wb = q_weights(orc, zz.GPU_FMT_Q4A, 72, O, I)
+    t = zz.QTensorDev(zz.GPU_FMT_Q4A, dev(Wb), O, I)
+    assert np.array_equal(t.unpack().cpu().numpy(), Wb)
+    for S in (1, 3):
+        x = synth.gaussian(73 + S, (S, I))
+        xq, sx = orc.quant_act(x)
+        y = zz.matvec(t, dev(xq), dev(sx)).cpu().numpy()
+        for s in range(S):
+            assert rel(y[s], orc.q4a_matvec(Wb, O, xq[s], sx[s])) < TOL
+
+
+@pytest.mark.parametrize("engine", ["gemma4_zz", "maple_zz"])
+def test_reference_engine_check_gpu(engine):
+    """The reference engines' own source, built with the GPU backend on (-DCOLI_METAL)
+    and linked against libzz_cuda.so in place of metal.o (oracle/Makefile), run their
+    own --check-gpu: six shapes each (gemma4.c:2315-2361: q4_0 projections and experts;
+    maple.c:1756-1800: tq2 projections / experts and the q4a lm_head / centroids), every
+    one within their 1e-4 of the exact-activation dot."""
+    import os
+    import subprocess
+    import tempfile
+    exe = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "oracle", "_ref", engine)
+    if not os.path.exists(exe):
+        pytest.skip(f"{exe} not built (the reference tree is needed to build it)")
+    with tempfile.TemporaryDirectory() as d:
+        r = subprocess.run([exe, d, "--check-gpu"], capture_output=True, text=True, timeout=300)
+    print(r.stdout)
+    lines = [ln for ln in r.stdout.splitlines() if "max rel err" in ln]
+    assert len(lines) == 6, r.stdout + r.stderr
+    assert all(ln.rstrip().endswith(" ok") for ln in lines), r.stdout
+    assert r.returncode == 0, r.stdout + r.stderr
 
 
 def test_ep_pack_unpack_layout():

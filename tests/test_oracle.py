@@ -150,3 +150,43 @@ def test_moe_layer_maple_matches_engine(orc, ref, S):
     a = orc.moe_layer(3, blobs, X, eidx, ewt, D, MI, 7.0)
     b = ref.moe_layer(3, blobs, X, eidx, ewt, D, MI, 7.0)
     assert np.max(np.abs(a - b)) <= 1e-4 * np.max(np.abs(b))
+
+
+def test_f32_activation_dots_match_reference(orc, ref):
+    """the exact-activation dots the GPU backend is checked against (q40_dot_f32,
+    q80_dot_f32, tq2_dot_f32, q4a_dot_f32): the same double arithmetic, so equal"""
+    import ctypes
+    I = 2048
+    x = synth.gaussian(60, (I,))
+    W4 = orc.q40_quant_rows(synth.gaussian(61, (5, I), 0.02))
+    W8 = orc.q80_quant_rows(synth.gaussian(62, (5, I), 0.02))
+    T2 = synth.tq2_tensor(63, 5, I)
+    A4 = synth.q4a_tensor(64, 5, I)
+    P, F, Ii = ctypes.c_void_p, ctypes.c_float, ctypes.c_int
+    p = lambda a: np.ascontiguousarray(a).ctypes.data_as(P)  # noqa: E731
+    for o in range(5):
+        for name, row in [("q40_dot_f32", W4[o]), ("q80_dot_f32", W8[o]), ("q4a_dot_f32", A4.reshape(5, -1)[o])]:
+            a = orc.fn(name, F, [P, P, Ii])(p(row), p(x), I)
+            b = ref.fn(name, F, [P, P, Ii])(p(row), p(x), I)
+            assert a == b, (name, o)
+        al = T2[:20].view(np.float32)[o]
+        codes = T2[20:].reshape(5, -1)[o]
+        a = orc.fn("tq2_dot_f32", F, [P, F, P, Ii])(p(codes), float(al), p(x), I)
+        b = ref.fn("tq2_dot_f32", F, [P, F, P, Ii])(p(codes), float(al), p(x), I)
+        assert a == b, o
+
+
+def test_q4a_dot_matches_reference(orc, ref):
+    """q4a_dot with q8_0 activations: the restatement (scalar, double) against the
+    reference build's AVX2 path (f32 lanes) within 1e-5 of the summand magnitude"""
+    import ctypes
+    I = 2048
+    xq, sx = orc.quant_act(synth.gaussian(65, (1, I)))
+    A4 = synth.q4a_tensor(66, 8, I).reshape(8, -1)
+    P, F, Ii = ctypes.c_void_p, ctypes.c_float, ctypes.c_int
+    p = lambda a: np.ascontiguousarray(a).ctypes.data_as(P)  # noqa: E731
+    for o in range(8):
+        a = orc.fn("q4a_dot", F, [P, P, P, Ii])(p(A4[o]), p(xq[0]), p(sx[0]), I)
+        b = ref.fn("q4a_dot", F, [P, P, P, Ii])(p(A4[o]), p(xq[0]), p(sx[0]), I)
+        scale = float(np.sum(np.abs(xq[0].astype(np.float64) * np.repeat(sx[0], 32)))) * 0.1
+        assert abs(a - b) <= 1e-5 * scale, o

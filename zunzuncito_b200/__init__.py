@@ -44,6 +44,12 @@ _PROTOS = [
     ("gpu_q40_matmul", c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int, c_int]),
     ("gpu_matmul", c_int, [c_int, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int]),
     ("gpu_last_error", ctypes.c_char_p, []),
+    ("zz_gpu_set_act_quant", c_int, [c_int]),
+    ("gpu_q40_matvec", c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int]),
+    ("gpu_q80_matvec", c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int]),
+    ("gpu_tq2_matvec", c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_float, c_int, c_int]),
+    ("gpu_q4a_matvec", c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int]),
+    ("zz_matvec_f32_dev", c_int, [ctypes.POINTER(QTensor), c_void_p, c_void_p, c_int, c_void_p]),
     ("zz_qtensor_bytes", c_size_t, [c_int, c_int, c_int]),
     ("zz_repack_dev", c_int, [c_int, c_void_p, c_int, c_int, c_void_p, ctypes.POINTER(QTensor), c_void_p]),
     ("zz_unpack_dev", c_int, [ctypes.POINTER(QTensor), c_void_p, c_void_p]),

@@ -7,7 +7,7 @@ import ctypes
 
 import torch
 
-from . import (GPU_FMT_Q40, GPU_FMT_Q80, GPU_FMT_TQ2, ExpertBank, QTensor, check, lib)
+from . import (GPU_FMT_Q40, GPU_FMT_Q4A, GPU_FMT_Q80, GPU_FMT_TQ2, ExpertBank, QTensor, check, lib)
 
 __all__ = ["ref_row_bytes", "ref_tensor_bytes", "expert_blob_bytes", "quant_act", "quant_rows",
            "QTensorDev", "matvec", "blocksums", "ExpertBankDev", "moe_ffn", "moe_ffn_q8", "alloc_aligned",
@@ -23,8 +23,8 @@ def _p(t):
 
 
 def ref_row_bytes(fmt, I):
-    """Bytes of one row in the reference layout (q40.h:313, 460; tq2.h:81)."""
-    return {GPU_FMT_Q40: I // 32 * 18, GPU_FMT_Q80: I // 32 * 34, GPU_FMT_TQ2: I // 4}[fmt]
+    """Bytes of one row in the reference layout (q40.h:313, 460; tq2.h:81, 286)."""
+    return {GPU_FMT_Q40: I // 32 * 18, GPU_FMT_Q80: I // 32 * 34, GPU_FMT_TQ2: I // 4, GPU_FMT_Q4A: I // 64 * 36}[fmt]
 
 
 def ref_tensor_bytes(fmt, O, I):

@@ -392,6 +392,7 @@ int launch_gemv1(const zz_qtensor *W, const int8_t *xq, const float *sx, const f
 }
 
 int launch_blocksums(const zz_qtensor *W, const int8_t *xq, int32_t *out, cudaStream_t st) {
+    if (W->fmt == GPU_FMT_Q4A) return fail("zz_blocksums_dev: q4a has no per-block integer check");
     long n = (long)W->O * (W->I / ZZ_BLK);
     unsigned grid = (unsigned)((n + 255) / 256);
     if (W->fmt == GPU_FMT_Q40) k_blocksums<GPU_FMT_Q40><<<grid, 256, 0, st>>>(W->codes, W->O, W->I, xq, out);

@@ -594,8 +594,10 @@ extern "C" int zz_moe_ffn_noalloc_dev(const zz_expert_bank *b, const float *X, c
 namespace zz {
 // y[S, O] for S quantized rows; S == 1 takes the register-resident GEMV, larger S the
 // tensor-core GEMM with work items derived from the grid (no device scratch).
+int launch_gemv_q4a(const zz_qtensor *W, const int8_t *xq, const float *sx, int S, float *y, cudaStream_t st);
 int matvec_impl(const zz_qtensor *W, const int8_t *xq, const float *sx, const float *sxtot, float *y, int S,
                 cudaStream_t st) {
+    if (W->fmt == GPU_FMT_Q4A) return launch_gemv_q4a(W, xq, sx, S, y, st);
     if (S == 1) {
         int r = launch_gemv1(W, xq, sx, sxtot, y, st);
         if (r != 0) return r > 0;

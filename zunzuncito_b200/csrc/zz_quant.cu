@@ -10,17 +10,18 @@ namespace zz {
 static inline size_t align256(size_t n) { return (n + 255) & ~(size_t)255; }
 
 size_t code_row_bytes(int fmt, int I) {
-    return fmt == GPU_FMT_Q40 ? (size_t)I / 2 : fmt == GPU_FMT_Q80 ? (size_t)I : (size_t)I / 4;
+    return fmt == GPU_FMT_Q40 || fmt == GPU_FMT_Q4A ? (size_t)I / 2 : fmt == GPU_FMT_Q80 ? (size_t)I : (size_t)I / 4;
 }
 // fp16 block-scale rows are padded to a multiple of 8 blocks (16 bytes) so a K-chunk
 // of scales is always one aligned piece; tq2 has one f32 alpha per row
 int scale_ld(int I) { return ((I / ZZ_BLK) + 7) & ~7; }
 size_t scale_row_bytes(int fmt, int I) {
-    return fmt == GPU_FMT_TQ2 ? 4 : (size_t)scale_ld(I) * 2;
+    // q4a: one (fp16 d, fp16 m) pair per 64-weight group
+    return fmt == GPU_FMT_TQ2 ? 4 : fmt == GPU_FMT_Q4A ? (size_t)(I / 64) * 4 : (size_t)scale_ld(I) * 2;
 }
 size_t ref_row_bytes(int fmt, int I) {  // bytes of one row in the reference layout
     return fmt == GPU_FMT_Q40 ? (size_t)(I / ZZ_BLK) * 18 : fmt == GPU_FMT_Q80 ? (size_t)(I / ZZ_BLK) * 34
-                                                                              : (size_t)I / 4;
+         : fmt == GPU_FMT_Q4A ? (size_t)(I / 64) * 36 : (size_t)I / 4;
 }
 size_t ref_tensor_bytes(int fmt, int O, int I) {
     return fmt == GPU_FMT_TQ2 ? (size_t)O * 4 + (size_t)O * (I / 4) : (size_t)O * ref_row_bytes(fmt, I);
@@ -208,8 +209,12 @@ using namespace zz;
 
 static bool fmt_ok(int fmt, int I) {
     if (fmt == GPU_FMT_Q40 || fmt == GPU_FMT_Q80) return I > 0 && I % 32 == 0;
-    if (fmt == GPU_FMT_TQ2) return I > 0 && I % 64 == 0;
+    if (fmt == GPU_FMT_TQ2 || fmt == GPU_FMT_Q4A) return I > 0 && I % 64 == 0;
     return false;
+}
+namespace zz {
+int launch_repack_q4a(const uint8_t *src, int O, int I, uint8_t *codes, void *scale, cudaStream_t st);
+int launch_unpack_q4a(const zz_qtensor *t, uint8_t *dst, cudaStream_t st);
 }
 
 extern "C" size_t zz_qtensor_bytes(int fmt, int O, int I) {
@@ -224,6 +229,11 @@ extern "C" int zz_repack_dev(int fmt, const uint8_t *src, int O, int I, void *ds
     if ((uintptr_t)dst & 255) return fail("zz_repack_dev: dst must be 256-byte aligned");
     uint8_t *codes = (uint8_t *)dst;
     void *scale = codes + codes_bytes(fmt, O, I);
+    if (fmt == GPU_FMT_Q4A) {
+        if (!launch_repack_q4a(src, O, I, codes, scale, (cudaStream_t)stream)) return 0;
+        out->fmt = fmt; out->O = O; out->I = I; out->codes = codes; out->scale = scale;
+        return 1;
+    }
     RowMap m{0, 0, 0};
     if (fmt != GPU_FMT_TQ2 &&
         !check_cuda(cudaMemsetAsync(scale, 0, scales_bytes(fmt, O, I), (cudaStream_t)stream), "repack memset"))
@@ -236,6 +246,7 @@ extern "C" int zz_repack_dev(int fmt, const uint8_t *src, int O, int I, void *ds
 extern "C" int zz_unpack_dev(const zz_qtensor *t, uint8_t *dst, void *stream) {
     if (!t || !dst || !fmt_ok(t->fmt, t->I)) return fail("zz_unpack_dev: bad tensor");
     cudaStream_t st = (cudaStream_t)stream;
+    if (t->fmt == GPU_FMT_Q4A) return launch_unpack_q4a(t, dst, st);
     if (t->fmt == GPU_FMT_TQ2) {
         if (!check_cuda(cudaMemcpyAsync(dst, t->scale, (size_t)t->O * 4, cudaMemcpyDeviceToDevice, st), "unpack"))
             return 0;

@@ -51,3 +51,16 @@ def zipf_routing(seed, S, E, K, s=1.1):
     w = np.exp(top - top[:, :1])
     w = (w / w.sum(axis=1, keepdims=True)).astype(np.float32)
     return idx, w, logits
+
+
+def q4a_tensor(seed, O, I):
+    """one q4a tensor [O, I] in the reference layout (tq2.h:268-283): per 64-weight group
+    fp16 d = |N(0,1)| * 0.01 + 0.002, fp16 m = N(0,1) * 0.05, uniform 4-bit codes"""
+    r = rng(seed)
+    g = np.zeros((O, I // 64, 36), np.uint8)
+    g[:, :, 4:] = r.integers(0, 256, size=(O, I // 64, 32), dtype=np.uint8)
+    d = (np.abs(r.standard_normal((O, I // 64))) * 0.01 + 0.002).astype(np.float16)
+    m = (r.standard_normal((O, I // 64)) * 0.05).astype(np.float16)
+    g[:, :, 0:2] = d.view(np.uint8).reshape(O, I // 64, 2)
+    g[:, :, 2:4] = m.view(np.uint8).reshape(O, I // 64, 2)
+    return g.reshape(-1)
