@@ -141,6 +141,25 @@ int zz_matvec_f32_dev(const zz_qtensor *W, const float *x, float *y, int S, void
  * row (q40.h:162-187, 359-372; tq2.h:116-133). out is [O, I/32] int32. */
 int zz_blocksums_dev(const zz_qtensor *W, const int8_t *xq, int32_t *out, void *stream);
 
+/* ---- routers: token rows -> (eidx, ewt) [S][K] in device memory, the inputs of
+ * zz_moe_ffn_dev; no host round trip. Selection is the reference's exactly (scores in
+ * its operation order; descending score, ties to the lower expert index). K <= 16. */
+
+/* replaces gemma4's route_row (gemma4.c:581-613): rmsnorm(res) * router_scale * D^-1/2,
+ * f32 logits = router_proj [E][D] . xn, top-K, softmax over the K, times the per-expert
+ * scale pes [E]. res [S][D] is the residual row before the pre-FFN norm. */
+int zz_route_gemma4_dev(const float *res, int S, int D, int E, int K, const float *proj,
+                        const float *scale, const float *pes, float eps, int32_t *idx, float *wts,
+                        void *stream);
+/* replaces ling's grouped route_row (ling.c:705-789): sigmoid scores of router [E][D]
+ * against the normalized rows xn [S][D], biased by bias [E] for selection only; the E
+ * experts in n_group contiguous groups ranked by the sum of their two best biased
+ * scores, the best topk_group kept; top-K of those; weights the unbiased scores,
+ * renormalised when norm_topk_prob, times routed_scale. E <= 1024, n_group <= 32. */
+int zz_route_ling_dev(const float *xn, int S, int D, int E, int K, int n_group, int topk_group,
+                      int norm_topk_prob, float routed_scale, const float *router, const float *bias,
+                      int32_t *idx, float *wts, void *stream);
+
 /* The routed experts of one MoE layer, packed for the batch-union FFN.
  *   gu: gate and up stacked per expert as a [2*inter, hidden] tensor whose rows are
  *       interleaved in groups of 64 (64 gate rows, then the 64 up rows of the same

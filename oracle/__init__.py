@@ -110,6 +110,47 @@ class _Lib:
         return idx, wts
 
 
+    def gemma4_route(self, res, proj, scale, pes, K, eps=1e-6):
+        """gemma4 route_row over rows res [S, D] -> idx, wts [S, K]"""
+        res = np.ascontiguousarray(np.atleast_2d(res), np.float32)
+        S, D = res.shape
+        E = proj.shape[0]
+        idx = np.zeros((S, K), np.int32)
+        wts = np.zeros((S, K), np.float32)
+        if self.prefix == "ref_":
+            self.fn("gemma4_route", None, [_P, _I, _I, _I, _I, _P, _P, _P, _F, _P, _P])(
+                _ptr(res), S, D, E, K, _ptr(np.ascontiguousarray(proj, np.float32)),
+                _ptr(np.ascontiguousarray(scale, np.float32)), _ptr(np.ascontiguousarray(pes, np.float32)),
+                float(eps), _ptr(idx), _ptr(wts))
+        else:
+            f = self.fn("gemma4_route", None, [_P, _I, _I, _I, _P, _P, _P, _F, _P, _P])
+            for s in range(S):
+                f(_ptr(res[s]), D, E, K, _ptr(np.ascontiguousarray(proj, np.float32)),
+                  _ptr(np.ascontiguousarray(scale, np.float32)), _ptr(np.ascontiguousarray(pes, np.float32)),
+                  float(eps), _ptr(idx[s]), _ptr(wts[s]))
+        return idx, wts
+
+    def ling_route(self, xn, router, bias, K, n_group, topk_group, norm_topk=1, routed_scale=1.0):
+        """ling grouped route_row over normalized rows xn [S, D] -> idx, wts [S, K]"""
+        xn = np.ascontiguousarray(np.atleast_2d(xn), np.float32)
+        S, D = xn.shape
+        E = router.shape[0]
+        idx = np.zeros((S, K), np.int32)
+        wts = np.zeros((S, K), np.float32)
+        rt = np.ascontiguousarray(router, np.float32)
+        bi = np.ascontiguousarray(bias, np.float32)
+        if self.prefix == "ref_":
+            self.fn("ling_route", None, [_P, _I, _I, _I, _I, _I, _I, _I, _F, _P, _P, _P, _P])(
+                _ptr(xn), S, D, E, K, n_group, topk_group, norm_topk, float(routed_scale), _ptr(rt), _ptr(bi),
+                _ptr(idx), _ptr(wts))
+        else:
+            f = self.fn("ling_route", None, [_P, _I, _I, _I, _I, _I, _I, _F, _P, _P, _P, _P])
+            for s in range(S):
+                f(_ptr(xn[s]), D, E, K, n_group, topk_group, norm_topk, float(routed_scale), _ptr(rt), _ptr(bi),
+                  _ptr(idx[s]), _ptr(wts[s]))
+        return idx, wts
+
+
 class Oracle(_Lib):
     """The restatement (zz_oracle.c)."""
 

@@ -95,3 +95,18 @@ void ref_gemma4_moe_layer(const uint8_t *const *blobs, const float *X, float *OU
 
 /* exact-activation q8_0 dot (q40.h:443-455), for pinning the restatement */
 float ref_q80_dot_f32(const uint8_t *w, const float *x, int I) { return q80_dot_f32(w, x, I); }
+
+/* the engine's own router (gemma4.c:581-613) over S residual rows, layer 0 of a model
+ * holding only the router tensors: idx / wts [S][K] */
+void ref_gemma4_route(const float *res, int S, int D, int E, int K, const float *proj, const float *scale,
+                      const float *pes, float eps, int *idx, float *wts) {
+    static M m;
+    memset(&m, 0, sizeof m);
+    m.c.hidden = D; m.c.n_experts = E; m.c.topk = K; m.c.eps = eps;
+    m.L[0].router_proj.f = proj; m.L[0].router_scale.f = scale; m.L[0].router_pes.f = pes;
+    Buf b;
+    memset(&b, 0, sizeof b);
+    b.xn = malloc(sizeof(float) * (size_t)D);
+    for (int s = 0; s < S; s++) route_row(&m, 0, res + (size_t)s * D, idx + (size_t)s * K, wts + (size_t)s * K, &b);
+    free(b.xn);
+}

@@ -604,3 +604,98 @@ void orc_matvec_f32(int fmt, float *y, const uint8_t *T, const float *x, int O, 
 void orc_q4a_matvec(float *y, const uint8_t *T, const int8_t *xq, const float *sx, int O, int I) {
     for (int o = 0; o < O; o++) y[o] = orc_q4a_dot(T + (size_t)o * (I / 64) * 36, xq, sx, I);
 }
+
+/* ---- routers ---- */
+
+/* gemma4 route_row (gemma4.c:581-613) for one residual row: rmsnorm without weight
+ * (double sum of squares, gemma4.c:425-431), times router_scale * D^-1/2, f32 logits
+ * as a sequential fused multiply-add chain (the reference is built with -mfma and the
+ * default contraction, so `v += RP * xn` is one fma per term), top-K by insertion in
+ * expert order (ties keep the lower index), softmax over the K, times the per-expert
+ * scale. */
+void orc_gemma4_route(const float *res, int D, int E, int K, const float *proj, const float *scale,
+                      const float *pes, float eps, int *idx, float *wts) {
+    float *xn = malloc(sizeof(float) * (size_t)D);
+    double s = 0;
+    for (int i = 0; i < D; i++) s += (double)res[i] * res[i];
+    float r = 1.0f / sqrtf((float)(s / D) + eps);
+    float rs = 1.0f / sqrtf((float)D);
+    for (int i = 0; i < D; i++) {
+        xn[i] = res[i] * r;
+        xn[i] *= scale[i] * rs;
+    }
+    float topv[64];
+    for (int j = 0; j < K; j++) { idx[j] = -1; topv[j] = -INFINITY; }
+    for (int e = 0; e < E; e++) {
+        float v = 0.0f;
+        for (int i = 0; i < D; i++) v += proj[(size_t)e * D + i] * xn[i];
+        int j = K;
+        while (j > 0 && v > topv[j - 1]) j--;
+        if (j == K) continue;
+        for (int t = K - 1; t > j; t--) { topv[t] = topv[t - 1]; idx[t] = idx[t - 1]; }
+        topv[j] = v; idx[j] = e;
+    }
+    float sum = 0.0f, mx = topv[0];
+    for (int j = 0; j < K; j++) { wts[j] = expf(topv[j] - mx); sum += wts[j]; }
+    for (int j = 0; j < K; j++) wts[j] = (wts[j] / sum) * pes[idx[j]];
+    free(xn);
+}
+
+/* ling route_row (ling.c:705-789) for one normalized row: per expert the double dot
+ * with 8 interleaved accumulators, sigmoid score, biased selection score; groups of
+ * E/NG ranked by the sum of their two best biased scores, the best TG kept (ties keep
+ * the lower index); top-K of the kept experts by biased score in expert order; weights
+ * the unbiased scores, renormalised over the K when norm_topk, times routed_scale. */
+void orc_ling_route(const float *xn, int D, int E, int K, int NG, int TG, int norm_topk, float routed_scale,
+                    const float *router, const float *bias, int *idx, float *wts) {
+    float *rwt = malloc(sizeof(float) * (size_t)E), *rsel = malloc(sizeof(float) * (size_t)E);
+    int EG = E / NG;
+    for (int e = 0; e < E; e++) {
+        const float *r = router + (size_t)e * D;
+        double s[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+        int i = 0;
+        for (; i + 8 <= D; i += 8)
+            for (int k = 0; k < 8; k++) s[k] += (double)r[i + k] * xn[i + k];
+        for (; i < D; i++) s[0] += (double)r[i] * xn[i];
+        double v = ((s[0] + s[1]) + (s[2] + s[3])) + ((s[4] + s[5]) + (s[6] + s[7]));
+        rwt[e] = 1.0f / (1.0f + expf(-(float)v));
+        rsel[e] = rwt[e] + bias[e];
+    }
+    float gs[64], topg[64], topv[64];
+    int keep[64];
+    for (int g = 0; g < NG; g++) {
+        float a = -INFINITY, bb = -INFINITY;
+        for (int i = 0; i < EG; i++) {
+            float v = rsel[g * EG + i];
+            if (v > a) { bb = a; a = v; }
+            else if (v > bb) bb = v;
+        }
+        gs[g] = EG > 1 ? a + bb : a;
+    }
+    for (int j = 0; j < TG; j++) { keep[j] = -1; topg[j] = -INFINITY; }
+    for (int g = 0; g < NG; g++) {
+        int j = TG;
+        while (j > 0 && gs[g] > topg[j - 1]) j--;
+        if (j == TG) continue;
+        for (int t = TG - 1; t > j; t--) { topg[t] = topg[t - 1]; keep[t] = keep[t - 1]; }
+        topg[j] = gs[g]; keep[j] = g;
+    }
+    unsigned char live[64] = {0};
+    for (int j = 0; j < TG; j++) if (keep[j] >= 0) live[keep[j]] = 1;
+    for (int j = 0; j < K; j++) { idx[j] = -1; topv[j] = -INFINITY; }
+    for (int e = 0; e < E; e++) {
+        if (!live[e / EG]) continue;
+        float v = rsel[e];
+        int j = K;
+        while (j > 0 && v > topv[j - 1]) j--;
+        if (j == K) continue;
+        for (int t = K - 1; t > j; t--) { topv[t] = topv[t - 1]; idx[t] = idx[t - 1]; }
+        topv[j] = v; idx[j] = e;
+    }
+    float sum = 0.0f;
+    for (int j = 0; j < K; j++) { wts[j] = rwt[idx[j]]; sum += wts[j]; }
+    if (norm_topk && K > 1)
+        for (int j = 0; j < K; j++) wts[j] /= (sum + 1e-20f);
+    for (int j = 0; j < K; j++) wts[j] *= routed_scale;
+    free(rwt); free(rsel);
+}

@@ -190,3 +190,25 @@ def test_q4a_dot_matches_reference(orc, ref):
         b = ref.fn("q4a_dot", F, [P, P, P, Ii])(p(A4[o]), p(xq[0]), p(sx[0]), I)
         scale = float(np.sum(np.abs(xq[0].astype(np.float64) * np.repeat(sx[0], 32)))) * 0.1
         assert abs(a - b) <= 1e-5 * scale, o
+
+
+def test_gemma4_router_matches_reference(orc, ref):
+    """route_row (gemma4.c:581-613): identical experts and weights"""
+    S, D, E, K = 64, 2816, 128, 8
+    res = synth.gaussian(1, (S, D))
+    proj, sc = synth.gaussian(2, (E, D), 0.02), synth.gaussian(3, (D,))
+    pes = np.abs(synth.gaussian(4, (E,)))
+    a, b = orc.gemma4_route(res, proj, sc, pes, K), ref.gemma4_route(res, proj, sc, pes, K)
+    assert np.array_equal(a[0], b[0]) and np.array_equal(a[1], b[1])
+
+
+@pytest.mark.parametrize("E,NG,TG,K", [(256, 8, 4, 8), (128, 8, 4, 8), (64, 1, 1, 6)])
+def test_ling_router_matches_reference(orc, ref, E, NG, TG, K):
+    """ling's grouped route_row (ling.c:705-789): identical experts and weights"""
+    S, D = 48, 1536
+    xn = synth.gaussian(5, (S, D))
+    rt, bi = synth.gaussian(6, (E, D), 0.05), synth.gaussian(7, (E,), 0.01)
+    for norm in (0, 1):
+        a = orc.ling_route(xn, rt, bi, K, NG, TG, norm, 2.5)
+        b = ref.ling_route(xn, rt, bi, K, NG, TG, norm, 2.5)
+        assert np.array_equal(a[0], b[0]) and np.array_equal(a[1], b[1])

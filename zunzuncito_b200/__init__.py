@@ -57,6 +57,10 @@ _PROTOS = [
     ("zz_quant_act_dev", c_int, [c_void_p, c_int, c_int, c_void_p, c_void_p, c_void_p, c_void_p]),
     ("zz_matvec_dev", c_int, [ctypes.POINTER(QTensor), c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_void_p]),
     ("zz_blocksums_dev", c_int, [ctypes.POINTER(QTensor), c_void_p, c_void_p, c_void_p]),
+    ("zz_route_gemma4_dev", c_int, [c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_void_p, c_void_p, c_float,
+                                    c_void_p, c_void_p, c_void_p]),
+    ("zz_route_ling_dev", c_int, [c_void_p, c_int, c_int, c_int, c_int, c_int, c_int, c_int, c_float, c_void_p,
+                                  c_void_p, c_void_p, c_void_p, c_void_p]),
     ("zz_expert_bank_bytes", c_size_t, [c_int, c_int, c_int, c_int]),
     ("zz_expert_bank_pack_dev", c_int, [c_int, c_int, c_int, c_int, c_void_p, c_int64, c_void_p,
                                         ctypes.POINTER(ExpertBank), c_void_p]),
@@ -116,7 +120,7 @@ _API = None
 # the public names of api.py (kept equal to its __all__; a CPU test checks that)
 _API_NAMES = frozenset(["ref_row_bytes", "ref_tensor_bytes", "expert_blob_bytes", "quant_act", "quant_rows",
                         "QTensorDev", "matvec", "blocksums", "ExpertBankDev", "moe_ffn", "moe_ffn_q8",
-                        "alloc_aligned", "ep_pack", "ep_unpack"])
+                        "alloc_aligned", "ep_pack", "ep_unpack", "route_gemma4", "route_ling"])
 
 
 def __getattr__(name):

@@ -11,7 +11,7 @@ from . import (GPU_FMT_Q40, GPU_FMT_Q4A, GPU_FMT_Q80, GPU_FMT_TQ2, ExpertBank, Q
 
 __all__ = ["ref_row_bytes", "ref_tensor_bytes", "expert_blob_bytes", "quant_act", "quant_rows",
            "QTensorDev", "matvec", "blocksums", "ExpertBankDev", "moe_ffn", "moe_ffn_q8", "alloc_aligned",
-           "ep_pack", "ep_unpack"]
+           "ep_pack", "ep_unpack", "route_gemma4", "route_ling"]
 
 
 def _stream():
@@ -169,3 +169,28 @@ def ep_unpack(rows, D, K):
     ewt = torch.empty((R, K), dtype=torch.float32, device=dev)
     check(lib.zz_ep_unpack_dev(_p(rows), R, D, K, _p(xq), _p(xs), _p(eidx), _p(ewt), _stream()), "zz_ep_unpack_dev")
     return xq, xs, eidx, ewt
+
+
+def route_gemma4(res, proj, scale, pes, K, eps=1e-6):
+    """gemma4 router on device (zz_route_gemma4_dev): res [S, D] -> eidx, ewt [S, K]"""
+    res = res.contiguous()
+    S, D = res.shape
+    E = proj.shape[0]
+    idx = torch.empty((S, K), dtype=torch.int32, device=res.device)
+    wts = torch.empty((S, K), dtype=torch.float32, device=res.device)
+    check(lib.zz_route_gemma4_dev(_p(res), S, D, E, K, _p(proj.contiguous()), _p(scale.contiguous()),
+                                  _p(pes.contiguous()), float(eps), _p(idx), _p(wts), _stream()), "zz_route_gemma4_dev")
+    return idx, wts
+
+
+def route_ling(xn, router, bias, K, n_group, topk_group, norm_topk_prob=1, routed_scale=1.0):
+    """ling grouped router on device (zz_route_ling_dev): xn [S, D] -> eidx, ewt [S, K]"""
+    xn = xn.contiguous()
+    S, D = xn.shape
+    E = router.shape[0]
+    idx = torch.empty((S, K), dtype=torch.int32, device=xn.device)
+    wts = torch.empty((S, K), dtype=torch.float32, device=xn.device)
+    check(lib.zz_route_ling_dev(_p(xn), S, D, E, K, n_group, topk_group, int(norm_topk_prob), float(routed_scale),
+                                _p(router.contiguous()), _p(bias.contiguous()), _p(idx), _p(wts), _stream()),
+          "zz_route_ling_dev")
+    return idx, wts
