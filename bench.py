@@ -347,7 +347,7 @@ def main():
         "layer_hbm_gbs": layer_bytes / (ms / L / 1e3) / 1e9,
         "layer_int8_tops": 2 * S * K * MACS_PER_PAIR / (ms / L / 1e3) / 1e12,
         "stage_ms_per_layer": {"quant_route": stage_ms[0], "gate_up": stage_ms[1], "down": stage_ms[2]},
-        "roofline": {"kernel": "k_moe_i8<q4_0, EPI_GATEUP> (tcgen05 kind::i8 gate/up GEMM + GeGLU + requant)",
+        "roofline": {"kernel": "k_gemm<q4_0, BN=32, EPI_GATEUP, int8 mma.sync, preset accumulators> (gate/up GEMM + GeGLU + requant)",
                      "bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s", "frac": achieved / hbm_peak,
                      "peak_source": peak_src, "traffic": traffic,
                      "traffic_source": "ncu dram bytes of the same kernel (profile case moe), scaled by algorithmic bytes",
@@ -451,6 +451,28 @@ def sub_benchmarks(zz, torch, synth, stream, banks, hbm_peak):
     res["q40_gemv_2816_single"] = {"unit": "GB/s", "value": GEMV_BYTES / (ms1 / 1e3) / 1e9,
                                    "us_per_gemv": ms1 * 1e3, "launch": "cuda graph, 64 distinct matrices"}
     del T, subs
+    # tied lm_head of a Gemma-4 decode step: 262144 x 2816 q4_0 (415 MiB) + softcap 30
+    # (gemma4.c:1270-1274), one launch per token, graph-replayed
+    V = 262144
+    Wl = torch.empty(V * 2816 // 32 * 18, dtype=torch.uint8, device="cuda")
+    for c0 in range(0, V, 32768):
+        w = torch.randn((32768, 2816), device="cuda") * 0.02
+        Wl[c0 * 1584:(c0 + 32768) * 1584] = zz.quant_rows(zz.GPU_FMT_Q40, w)
+        del w
+    TL = zz.QTensorDev(zz.GPU_FMT_Q40, Wl, V, 2816)
+    del Wl
+    yl = torch.empty(V, device="cuda")
+
+    def lm_head():
+        zz.check(zz.lib.zz_lm_head_dev(ctypes.byref(TL.t), ctypes.c_void_p(xq.data_ptr()), ctypes.c_void_p(sx.data_ptr()),
+                                       None, 30.0, ctypes.c_void_p(yl.data_ptr()),
+                                       ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)), "lm_head")
+    msl = graph_timed(torch, lm_head, 20, 3)
+    lbytes = V * 1584 + 2816 + 88 * 4 + V * 4
+    res["lm_head_262144x2816"] = {"unit": "GB/s", "value": lbytes / (msl / 1e3) / 1e9,
+                                  "frac_hbm": lbytes / (msl / 1e3) / 1e9 / hbm_peak, "us_per_launch": msl * 1e3,
+                                  "bytes": lbytes, "softcap": 30.0}
+    del TL
     # config 2: decode, M=1, 8 routed experts per layer, over the 30 resident layers
     L = len(banks)
     r1 = [synth.zipf_routing(300 + l, 1, E, K)[:2] for l in range(L)]

@@ -131,6 +131,13 @@ int zz_quant_act_dev(const float *x, int S, int I, int8_t *xq, float *sx, float 
 int zz_matvec_dev(const zz_qtensor *W, const int8_t *xq, const float *sx, const float *sxtot,
                   float *y, int S, void *stream);
 
+/* the tied lm_head of a decode step (gemma4.c:1270-1274): y[o] = W row o . (xq, sx) for
+ * the whole vocabulary (e.g. 262144 x 2816 q4_0), then, when softcap > 0, the final-logit
+ * softcap y = tanhf(y / softcap) * softcap. One activation row; tall tensors stream
+ * through the bulk-copy GEMV with the softcap fused into its epilogue. */
+int zz_lm_head_dev(const zz_qtensor *W, const int8_t *xq, const float *sx, const float *sxtot,
+                   float softcap, float *y, void *stream);
+
 /* the f32-activation matvec (q40_dot_f32 q40.h:290-305, q80_dot_f32, tq2_dot_f32
  * tq2.h:235-252, q4a_dot_f32 tq2.h:410-432): y[S, O] = W . x for S f32 rows x [S, I]
  * (I <= 51200). Each 32-weight block is summed in fp32 (the reference sums in double). */

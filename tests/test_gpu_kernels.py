@@ -215,7 +215,8 @@ def test_matvec_f32_activations(orc, fmt, O, I):
     x = synth.gaussian(71, (2, I))
     t = zz.QTensorDev(fmt, dev(Wb), O, I)
     y = torch.empty((2, O), device="cuda")
-    zz.check(zz.lib.zz_matvec_f32_dev(ctypes.byref(t.t), ctypes.c_void_p(dev(x).data_ptr()),
+    x_d = dev(x)   # held for the call
+    zz.check(zz.lib.zz_matvec_f32_dev(ctypes.byref(t.t), ctypes.c_void_p(x_d.data_ptr()),
                                       ctypes.c_void_p(y.data_ptr()), 2, None), "zz_matvec_f32_dev")
     y = y.cpu().numpy()
     for s in range(2):
@@ -279,3 +280,27 @@ def test_ep_pack_unpack_layout():
         mine = (eidx >= 0) & (torch.div(eidx, per, rounding_mode="floor") == d)
         assert torch.equal(got[2][sl], torch.where(mine, eidx - d * per, torch.full_like(eidx, -1)))
         assert torch.equal(got[3][sl], torch.where(mine, ewt, torch.zeros_like(ewt)))
+
+
+@pytest.mark.parametrize("O,cap", [(65536, 30.0), (1000, 0.0), (4099, 30.0)])
+def test_lm_head_softcap(orc, O, cap):
+    """tied lm_head + final-logit softcap (gemma4.c:1270-1274); 65536 x 2816 q4_0 (104 MB)
+    takes the streamed kernel with the softcap in its epilogue, the small ones the
+    register kernel and a separate pass"""
+    I = 2816
+    g = torch.Generator(device="cuda").manual_seed(80)
+    w = torch.randn((O, I), generator=g, device="cuda") * 0.02
+    Wq = zz.quant_rows(zz.GPU_FMT_Q40, w)
+    del w
+    t = zz.QTensorDev(zz.GPU_FMT_Q40, Wq, O, I)
+    x = synth.gaussian(81, (1, I)) * 4
+    xq, sx = orc.quant_act(x)
+    y = torch.empty(O, device="cuda")
+    xq_d, sx_d = dev(xq), dev(sx)   # held for the call
+    zz.check(zz.lib.zz_lm_head_dev(ctypes.byref(t.t), ctypes.c_void_p(xq_d.data_ptr()),
+                                   ctypes.c_void_p(sx_d.data_ptr()), None, float(cap),
+                                   ctypes.c_void_p(y.data_ptr()), None), "zz_lm_head_dev")
+    want = orc.q40_matvec(Wq.cpu().numpy().reshape(O, -1), xq[0], sx[0]).astype(np.float64)
+    if cap > 0:
+        want = np.tanh(want / cap) * cap
+    assert rel(y.cpu().numpy(), want) < TOL

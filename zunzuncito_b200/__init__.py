@@ -56,6 +56,7 @@ _PROTOS = [
     ("zz_quant_rows_dev", c_int, [c_int, c_void_p, c_int, c_int, c_void_p, c_void_p]),
     ("zz_quant_act_dev", c_int, [c_void_p, c_int, c_int, c_void_p, c_void_p, c_void_p, c_void_p]),
     ("zz_matvec_dev", c_int, [ctypes.POINTER(QTensor), c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_void_p]),
+    ("zz_lm_head_dev", c_int, [ctypes.POINTER(QTensor), c_void_p, c_void_p, c_void_p, c_float, c_void_p, c_void_p]),
     ("zz_blocksums_dev", c_int, [ctypes.POINTER(QTensor), c_void_p, c_void_p, c_void_p]),
     ("zz_route_gemma4_dev", c_int, [c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_void_p, c_void_p, c_float,
                                     c_void_p, c_void_p, c_void_p]),

@@ -167,7 +167,7 @@ template <int FMT, int NBL>
 __global__ void __launch_bounds__(gs::THREADS) k_gemv_stream(const uint8_t *__restrict__ codes, const void *__restrict__ scale,
                                                              int O, int I, int R, const int8_t *__restrict__ xq,
                                                              const float *__restrict__ sx, const float *__restrict__ sxtot,
-                                                             float *__restrict__ y) {
+                                                             float *__restrict__ y, float cap) {
     using namespace gs;
     extern __shared__ __align__(128) uint8_t smem[];
     constexpr bool TQ2 = FMT == GPU_FMT_TQ2;
@@ -259,7 +259,10 @@ __global__ void __launch_bounds__(gs::THREADS) k_gemv_stream(const uint8_t *__re
             acc = warp_sum(acc);
             if (lane == 0) {
                 const int o = t * R + r;
-                y[o] = TQ2 ? reinterpret_cast<const float *>(scale)[o] * (acc - tot) : acc;
+                float v = TQ2 ? reinterpret_cast<const float *>(scale)[o] * (acc - tot) : acc;
+                // final-logit softcap of a tied lm_head (gemma4.c:1271-1274)
+                if (cap > 0.f) v = __fmul_rn(tanhf(__fdiv_rn(v, cap)), cap);
+                y[o] = v;
             }
         }
         __syncwarp();
@@ -276,7 +279,7 @@ static int gs_rows(int rowb, int srow) {
 
 // streamed matvec; returns 0 if the shape has no instantiation
 static int launch_gemv_stream(const zz_qtensor *W, const int8_t *xq, const float *sx, const float *sxtot, float *y,
-                              cudaStream_t st) {
+                              cudaStream_t st, float cap = 0.f) {
     const int O = W->O, I = W->I, nb = I / ZZ_BLK, nbp = (nb + 7) & ~7;
     const bool tq2 = W->fmt == GPU_FMT_TQ2;
     const int rowb = tq2 ? I / 4 : W->fmt == GPU_FMT_Q40 ? I / 2 : I, srow = tq2 ? 0 : nbp * 2;
@@ -298,7 +301,7 @@ static int launch_gemv_stream(const zz_qtensor *W, const int8_t *xq, const float
             cudaFuncSetAttribute(k_gemv_stream<F, N>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024); \
             attr = true;                                                                                       \
         }                                                                                                      \
-        k_gemv_stream<F, N><<<grid, gs::THREADS, smem, st>>>(W->codes, W->scale, O, I, R, xq, sx, sxtot, y);    \
+        k_gemv_stream<F, N><<<grid, gs::THREADS, smem, st>>>(W->codes, W->scale, O, I, R, xq, sx, sxtot, y, cap); \
         break;                                                                                                 \
     }
     if (W->fmt == GPU_FMT_Q40) {
@@ -402,3 +405,35 @@ int launch_blocksums(const zz_qtensor *W, const int8_t *xq, int32_t *out, cudaSt
 }
 
 }  // namespace zz
+
+// ---------------------------------------------------------------- lm_head
+__global__ void k_softcap(float *__restrict__ y, long n, float cap) {
+    const long i = (long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n) y[i] = __fmul_rn(tanhf(__fdiv_rn(y[i], cap)), cap);
+}
+
+namespace zz {
+int matvec_impl(const zz_qtensor *W, const int8_t *xq, const float *sx, const float *sxtot, float *y, int S,
+                cudaStream_t st);
+}
+
+extern "C" int zz_lm_head_dev(const zz_qtensor *W, const int8_t *xq, const float *sx, const float *sxtot, float softcap,
+                              float *y, void *stream) {
+    using namespace zz;
+    if (!W || !W->codes || !W->scale || W->O <= 0 || W->I <= 0 || W->fmt == GPU_FMT_Q4A && W->I % 64)
+        return fail("zz_lm_head_dev: invalid tensor");
+    if (!xq || !sx || !y || (W->fmt == GPU_FMT_TQ2 && !sxtot)) return fail("zz_lm_head_dev: null pointer");
+    if (!(softcap >= 0.f)) return fail("zz_lm_head_dev: softcap %g < 0", (double)softcap);
+    cudaStream_t st = (cudaStream_t)stream;
+    // tall tensors take the streamed kernel with the softcap in its epilogue
+    if (W->fmt != GPU_FMT_Q4A && zz_qtensor_bytes(W->fmt, W->O, W->I) >= ((size_t)64 << 20)) {
+        const int r = launch_gemv_stream(W, xq, sx, sxtot, y, st, softcap);
+        if (r) return r > 0;
+    }
+    if (!matvec_impl(W, xq, sx, sxtot, y, 1, st)) return 0;
+    if (softcap > 0.f) {
+        k_softcap<<<(unsigned)((W->O + 255) / 256), 256, 0, st>>>(y, W->O, softcap);
+        return check_cuda(cudaGetLastError(), "softcap launch");
+    }
+    return 1;
+}
