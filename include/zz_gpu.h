@@ -227,6 +227,31 @@ int zz_moe_ffn_noalloc_dev(const zz_expert_bank *bank, const float *X, const int
                            const float *ewt, float *OUT, int S, int K, int act, float clamp,
                            void *stream);
 
+/* ---- the gemma4 container (manifest.txt / dense.bin / experts.bin, written by the
+ * reference's tools/convert_gemma4.py:361-422 and read by gemma4.c:260-403) loaded
+ * straight into HBM planes. The handle is opaque; the loader allocates its own staging
+ * (it is not a hot path). */
+typedef struct zz_container zz_container;
+/* parse dir/manifest.txt (the reference's manifest(), gemma4.c:260-331) */
+int zz_container_open(const char *dir, zz_container **out);
+void zz_container_close(zz_container *c);
+/* a numeric "cfg <key> <value>" entry */
+int zz_container_cfg(const zz_container *c, const char *key, double *val);
+/* a "dense <name> <off> <len> <fmt> <O> <I>" entry (container formats: f32 0, q4_0 1) */
+int zz_container_dense_info(const zz_container *c, const char *name, int *fmt, int *O, int *I,
+                            int64_t *off, int64_t *len);
+/* the experts.bin offset of (layer, expert), -1 if absent */
+int64_t zz_container_expert_offset(const zz_container *c, int layer, int expert);
+/* device bytes of one layer's expert bank (zz_expert_bank_bytes of the container's shape) */
+size_t zz_container_bank_bytes(const zz_container *c);
+/* one layer's experts from experts.bin into an expert bank in dst (256-byte aligned,
+ * zz_container_bank_bytes bytes); replaces the engine's per-slot read + gpu_map
+ * (gemma4.c:480-495, 2052-2055) for a resident layer */
+int zz_container_load_bank_dev(zz_container *c, int layer, void *dst, zz_expert_bank *bank, void *stream);
+/* a q4_0 dense tensor (e.g. "embed_tokens", the tied lm_head) into zz_qtensor planes in
+ * dst (zz_qtensor_bytes bytes, 256-byte aligned) */
+int zz_container_load_dense_dev(zz_container *c, const char *name, void *dst, zz_qtensor *out, void *stream);
+
 /* ---- expert-parallel exchange layout (no reference counterpart: the reference runs
  * one process; these pack and unpack the rows of the NCCL all-to-all that shards the
  * experts over the GPUs of a node).

@@ -110,3 +110,20 @@ void ref_gemma4_route(const float *res, int S, int D, int E, int K, const float 
     for (int s = 0; s < S; s++) route_row(&m, 0, res + (size_t)s * D, idx + (size_t)s * K, wts + (size_t)s * K, &b);
     free(b.xn);
 }
+
+/* the engine's own container parser (manifest(), gemma4.c:260-403) on a directory:
+ * esz / gate_b / down_b and the first n entries of the expert offset table; returns
+ * n_layers * n_experts */
+int ref_gemma4_manifest(const char *dir, long long *esz3, long long *eoff, int n) {
+    static M m;
+    memset(&m, 0, sizeof m);
+    g_use_gpu = 0;
+    manifest(&m, dir);
+    esz3[0] = m.esz; esz3[1] = m.gate_b; esz3[2] = m.down_b;
+    int tot = m.c.n_layers * m.c.n_experts;
+    for (int i = 0; i < n && i < tot; i++) eoff[i] = m.eoff[i];
+    close(m.efd);
+    free(m.eoff);
+    free((void *)m.dense);
+    return tot;
+}

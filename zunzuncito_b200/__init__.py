@@ -62,6 +62,15 @@ _PROTOS = [
                                     c_void_p, c_void_p, c_void_p]),
     ("zz_route_ling_dev", c_int, [c_void_p, c_int, c_int, c_int, c_int, c_int, c_int, c_int, c_float, c_void_p,
                                   c_void_p, c_void_p, c_void_p, c_void_p]),
+    ("zz_container_open", c_int, [ctypes.c_char_p, ctypes.POINTER(c_void_p)]),
+    ("zz_container_close", None, [c_void_p]),
+    ("zz_container_cfg", c_int, [c_void_p, ctypes.c_char_p, ctypes.POINTER(ctypes.c_double)]),
+    ("zz_container_dense_info", c_int, [c_void_p, ctypes.c_char_p, ctypes.POINTER(c_int), ctypes.POINTER(c_int),
+                                        ctypes.POINTER(c_int), ctypes.POINTER(c_int64), ctypes.POINTER(c_int64)]),
+    ("zz_container_expert_offset", c_int64, [c_void_p, c_int, c_int]),
+    ("zz_container_bank_bytes", c_size_t, [c_void_p]),
+    ("zz_container_load_bank_dev", c_int, [c_void_p, c_int, c_void_p, ctypes.POINTER(ExpertBank), c_void_p]),
+    ("zz_container_load_dense_dev", c_int, [c_void_p, ctypes.c_char_p, c_void_p, ctypes.POINTER(QTensor), c_void_p]),
     ("zz_expert_bank_bytes", c_size_t, [c_int, c_int, c_int, c_int]),
     ("zz_expert_bank_pack_dev", c_int, [c_int, c_int, c_int, c_int, c_void_p, c_int64, c_void_p,
                                         ctypes.POINTER(ExpertBank), c_void_p]),
