@@ -43,7 +43,8 @@ def parse():
     ap.add_argument("--layers", type=int, default=LAYERS)
     ap.add_argument("--no-sub", action="store_true", help="skip the sub-benchmarks")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
-    ap.add_argument("--profile-case", choices=["moe", "gemv", "decode"],
+    ap.add_argument("--profile-case", choices=["moe", "gemv", "decode", "prefill", "maple", "lmhead", "route", "f32",
+                                               "ep"],
                     help="run a small case of one kernel family a few times and exit (for ncu)")
     return ap.parse_args()
 
@@ -143,7 +144,7 @@ def gateup_alg_bytes(S, distinct):
 # moe` (the same kernel and shapes, routings zipf_routing(88 + l), l = 0, 1; 4 launches):
 # the full 30-layer stack is too large to capture, so the bench scales this by the
 # algorithmic bytes of its own routing.
-PROFILE_GU_TRAFFIC = 206037888.0 + 2295296.0
+PROFILE_GU_TRAFFIC = 206104960.0 + 5479616.0   # mean read + write of the 4 gate/up launches
 
 
 def timed(torch, fn, steps, warmup, stream):
@@ -161,7 +162,9 @@ def timed(torch, fn, steps, warmup, stream):
 
 
 def profile_case(kind, zz, torch, synth):
-    """small cases sized for an ncu capture (a few GB at most on the device)"""
+    """small cases sized for an ncu capture (a few GB at most on the device); the
+    MoE cases run whichever engine ZZ_MOE_KERNEL selects"""
+    dev = lambda a: torch.from_numpy(np.ascontiguousarray(a)).cuda()  # noqa: E731
     if kind == "gemv":
         G = 64  # 64 distinct 2816 x 2816 q4_0 matrices stacked: 285 MB > L2
         w = torch.randn((G * 2816, 2816), device="cuda") * 0.02
@@ -170,15 +173,66 @@ def profile_case(kind, zz, torch, synth):
         xq, sx, _ = zz.quant_act(torch.randn((1, 2816), device="cuda"))
         for _ in range(3):
             zz.matvec(T, xq, sx)
+    elif kind == "lmhead":
+        # tied lm_head 262144 x 2816 q4_0 (415 MiB) with the softcap
+        V = 262144
+        Wl = torch.empty(V * 1584, dtype=torch.uint8, device="cuda")
+        for c0 in range(0, V, 32768):
+            Wl[c0 * 1584:(c0 + 32768) * 1584] = zz.quant_rows(zz.GPU_FMT_Q40, torch.randn((32768, 2816), device="cuda") * 0.02)
+        T = zz.QTensorDev(zz.GPU_FMT_Q40, Wl, V, 2816)
+        del Wl
+        xq, sx, _ = zz.quant_act(torch.randn((1, 2816), device="cuda"))
+        y = torch.empty(V, device="cuda")
+        for _ in range(3):
+            zz.check(zz.lib.zz_lm_head_dev(ctypes.byref(T.t), ctypes.c_void_p(xq.data_ptr()), ctypes.c_void_p(sx.data_ptr()),
+                                           None, 30.0, ctypes.c_void_p(y.data_ptr()), None), "lm_head")
+    elif kind == "f32":
+        # f32-activation matvecs (the gpu.h numerics): q4_0 4096 x 2816, q4a 151936 x 2048 (Maple lm_head)
+        for fmt, O, I in [(zz.GPU_FMT_Q40, 4096 * 16, 2816), (zz.GPU_FMT_Q4A, 151936, 2048)]:
+            src = dev(synth.q4a_tensor(5, O, I)) if fmt == zz.GPU_FMT_Q4A else \
+                zz.quant_rows(zz.GPU_FMT_Q40, torch.randn((O, I), device="cuda") * 0.02)
+            T = zz.QTensorDev(fmt, src, O, I)
+            x = torch.randn((1, I), device="cuda")
+            y = torch.empty(O, device="cuda")
+            for _ in range(2):
+                zz.check(zz.lib.zz_matvec_f32_dev(ctypes.byref(T.t), ctypes.c_void_p(x.data_ptr()),
+                                                  ctypes.c_void_p(y.data_ptr()), 1, None), "f32")
+            xq, sx, _ = zz.quant_act(x)
+            zz.matvec(T, xq, sx)
+    elif kind == "route":
+        S = 512
+        res = torch.randn((S, D), device="cuda")
+        proj, sc, pes = torch.randn((E, D), device="cuda") * 0.02, torch.randn(D, device="cuda"), torch.rand(E, device="cuda")
+        for _ in range(2):
+            zz.route_gemma4(res, proj, sc, pes, K)
+        xn = torch.randn((S, 1536), device="cuda")
+        rt, bi = torch.randn((256, 1536), device="cuda") * 0.05, torch.randn(256, device="cuda") * 0.01
+        for _ in range(2):
+            zz.route_ling(xn, rt, bi, 8, 8, 4, 1, 2.5)
+    elif kind == "ep":
+        S, W = 512, 8
+        xq = torch.randint(-127, 128, (S, D), dtype=torch.int8, device="cuda")
+        xs = torch.rand((S, D // 32), device="cuda")
+        e, w = synth.zipf_routing(5, S, E, K)[:2]
+        for _ in range(2):
+            rows = zz.ep_pack(xq, xs, dev(e), dev(w), W, E // W)
+            zz.ep_unpack(rows, D, K)
+    elif kind == "maple":
+        gen = torch.Generator(device="cuda").manual_seed(4321)
+        bank = tq2_bank_dev(zz, torch, synth.MAPLE_E, synth.MAPLE_D, synth.MAPLE_MI, gen)
+        for S in (512, 1):
+            r = synth.zipf_routing(31, S, synth.MAPLE_E, synth.MAPLE_K)
+            X = torch.randn((S, synth.MAPLE_D), device="cuda")
+            for _ in range(2):
+                zz.moe_ffn(bank, X, dev(r[0]), dev(r[1]), zz.ZZ_ACT_SWIGLU_CLAMP, synth.MAPLE_CLAMP)
     else:
         banks, _ = make_stack(zz, torch, 2, seed=77)
-        S = 512 if kind == "moe" else 1
+        S = {"moe": 512, "prefill": 4096}.get(kind, 1)
         for l in range(2):
             r = synth.zipf_routing(88 + l, S, E, K)
             X = torch.randn((S, D), device="cuda")
             for _ in range(2):
-                zz.moe_ffn(banks[l], X, torch.from_numpy(r[0]).cuda(), torch.from_numpy(r[1]).cuda(),
-                           zz.ZZ_ACT_GEGLU_TANH)
+                zz.moe_ffn(banks[l], X, dev(r[0]), dev(r[1]), zz.ZZ_ACT_GEGLU_TANH)
     torch.cuda.synchronize()
     print(f"profile case {kind} done")
 

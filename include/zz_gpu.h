@@ -154,7 +154,8 @@ int zz_blocksums_dev(const zz_qtensor *W, const int8_t *xq, int32_t *out, void *
 
 /* replaces gemma4's route_row (gemma4.c:581-613): rmsnorm(res) * router_scale * D^-1/2,
  * f32 logits = router_proj [E][D] . xn, top-K, softmax over the K, times the per-expert
- * scale pes [E]. res [S][D] is the residual row before the pre-FFN norm. */
+ * scale pes [E]. res [S][D] is the residual row before the pre-FFN norm. E <= 256; D % 4 == 0
+ * and 16-byte-aligned router rows (both routers). */
 int zz_route_gemma4_dev(const float *res, int S, int D, int E, int K, const float *proj,
                         const float *scale, const float *pes, float eps, int32_t *idx, float *wts,
                         void *stream);
@@ -162,7 +163,7 @@ int zz_route_gemma4_dev(const float *res, int S, int D, int E, int K, const floa
  * against the normalized rows xn [S][D], biased by bias [E] for selection only; the E
  * experts in n_group contiguous groups ranked by the sum of their two best biased
  * scores, the best topk_group kept; top-K of those; weights the unbiased scores,
- * renormalised when norm_topk_prob, times routed_scale. E <= 1024, n_group <= 32. */
+ * renormalised when norm_topk_prob, times routed_scale. E <= 256, n_group <= 32. */
 int zz_route_ling_dev(const float *xn, int S, int D, int E, int K, int n_group, int topk_group,
                       int norm_topk_prob, float routed_scale, const float *router, const float *bias,
                       int32_t *idx, float *wts, void *stream);
