@@ -304,3 +304,40 @@ def test_lm_head_softcap(orc, O, cap):
     if cap > 0:
         want = np.tanh(want / cap) * cap
     assert rel(y.cpu().numpy(), want) < TOL
+
+
+def _pow2_inputs(fmt, O, S, seed):
+    """one 32-weight block per row with power-of-two scales: q4_0 / q8_0 codes random, every
+    fp16 block scale 2^-4; activations k * 2^-3 with each row's block max |x| = 127 * 2^-3,
+    so q8_0 gives xq = 8 x and sx = 2^-3 exactly. Then y = 2^-7 * (the block's integer sum),
+    exact in fp32 whatever the kernel's arithmetic order."""
+    r = synth.rng(seed)
+    bb = 18 if fmt == zz.GPU_FMT_Q40 else 34
+    W = np.zeros((O, bb), np.uint8)
+    W[:, 0:2] = np.frombuffer(np.float16(2.0 ** -4).tobytes(), np.uint8)
+    W[:, 2:] = r.integers(0, 256, size=(O, bb - 2), dtype=np.uint8)
+    if fmt == zz.GPU_FMT_Q80:
+        W[:, 2:][W[:, 2:] == 128] = 129           # q8_0 codes stay in [-127, 127]
+    xq = r.integers(-127, 128, size=(S, 32)).astype(np.int8)
+    xq[:, 5] = 127
+    x = (xq.astype(np.float32) * np.float32(0.125))
+    if fmt == zz.GPU_FMT_Q40:
+        q = np.concatenate([W[:, 2:] & 15, W[:, 2:] >> 4], axis=1).astype(np.int32) - 8
+    else:
+        q = W[:, 2:].view(np.int8).astype(np.int32)
+    ints = xq.astype(np.int32) @ q.T             # [S, O] block integer sums
+    return W.reshape(-1), x, ints
+
+
+@pytest.mark.parametrize("fmt", [zz.GPU_FMT_Q40, zz.GPU_FMT_Q80])
+@pytest.mark.parametrize("O,S", [(1000, 1), (2200000, 1), (300, 5)])
+def test_block_integers_exact_on_production_kernels(orc, fmt, O, S):
+    """I = 32 with power-of-two scales makes every production matvec output the exact block
+    integer times 2^-7: the register GEMV (S=1, small), the streamed GEMV (S=1, >= 64 MB:
+    4M rows), the int8 mma.sync GEMM (S>1); all must equal the integers bit for bit"""
+    W, x, ints = _pow2_inputs(fmt, O, S, 90 + fmt)
+    xq, sx = orc.quant_act(x)
+    assert np.all(sx == np.float32(0.125)) and np.array_equal(xq.astype(np.float32), x * 8)
+    t = zz.QTensorDev(fmt, dev(W), O, 32)
+    y = zz.matvec(t, dev(xq), dev(sx)).cpu().numpy()
+    assert np.array_equal(y.astype(np.float64) * 128.0, ints.astype(np.float64))
