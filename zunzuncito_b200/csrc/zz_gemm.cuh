@@ -173,7 +173,7 @@ __device__ __forceinline__ uint32_t s8_h2(uint32_t p) { return h2sub((p ^ 0x0080
 // tq2 2-bit codes at bit offset sh -> c
 __device__ __forceinline__ uint32_t c2_h2(uint32_t p, int sh) { return h2sub(((p >> sh) & 0x00030003u) | H1024, H1024); }
 
-template <int FMT, int BN, bool B_HALF>
+template <int FMT, int BN, bool B_HALF, bool S8 = false>
 struct GemmSmem {
     using T = FmtTraits<FMT>;
     static constexpr int B_STRIDE = B_HALF ? (32 * G_BKB * 2 + 16) : (32 * G_BKB + 16);  // bytes per row
@@ -184,7 +184,8 @@ struct GemmSmem {
     static constexpr int STAGE = A_BYTES + AS_BYTES + B_BYTES + BS_BYTES;
     static constexpr int PIPE = STAGE * G_STAGES;
     static constexpr int EPI = G_BM * (BN + 4) * 4;  // fp32 C tile, padded
-    static constexpr int TOTAL = (PIPE > EPI ? PIPE : EPI) + BN * 16;  // + per-column info
+    static constexpr int COL = PIPE > EPI ? PIPE : EPI;  // per-column info
+    static constexpr int TOTAL = COL + BN * 16;
 };
 
 // S8: int8 tensor-core path (m16n8k32.s8, int8 activations in shared memory, int32
@@ -192,7 +193,7 @@ struct GemmSmem {
 template <int FMT, int BN, int EPI, bool B_HALF, bool S8 = false>
 __device__ __forceinline__ void gemm_item(const GemmArgs &a, int item_idx) {
     using T = FmtTraits<FMT>;
-    using L = GemmSmem<FMT, BN, B_HALF>;
+    using L = GemmSmem<FMT, BN, B_HALF, S8>;
     extern __shared__ __align__(128) uint8_t smem[];
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, t = lane & 3;
 
@@ -216,8 +217,8 @@ __device__ __forceinline__ void gemm_item(const GemmArgs &a, int item_idx) {
     const uint8_t *xbase = reinterpret_cast<const uint8_t *>(a.xq);
 
     // per-column info: X row index (after gather) and the tq2 offset total
-    int *col_xrow = reinterpret_cast<int *>(smem + L::TOTAL - BN * 16);
-    float *col_sx = reinterpret_cast<float *>(smem + L::TOTAL - BN * 12);
+    int *col_xrow = reinterpret_cast<int *>(smem + L::COL);
+    float *col_sx = reinterpret_cast<float *>(smem + L::COL + BN * 4);
     for (int n = tid; n < BN; n += G_THREADS) {
         int r = it.row0 + (n < ncols ? n : 0);
         int xr = a.gather ? a.gather[r] / a.gather_div : r;
@@ -277,15 +278,12 @@ __device__ __forceinline__ void gemm_item(const GemmArgs &a, int item_idx) {
             const uint8_t *src = xbase + (size_t)col_xrow[n] * xrow_bytes + (size_t)b0 * (B_HALF ? 64 : 32) + p * 16;
             cp_async16_zfill(sb + n * L::B_STRIDE + p * 16, ok ? (const void *)src : (const void *)xbase, ok);
         }
-        // activation scales per block: fp16 path [block][column] (a column pair is one
-        // 8-byte load); int8 path [block][t][tile][pair], so the 2*NT scales of the column
-        // pairs (8j + 2t, 8j + 2t + 1) one thread uses in a block are 16-byte loads
+        // activation scales per block, [block][column] (a column pair is one 8-byte load)
         for (int i = tid; i < BN * G_BKB; i += G_THREADS) {
             int n = i / G_BKB, k = i % G_BKB;
             bool ok = n < ncols && k < nbk;
             const float *src = a.xs + (size_t)col_xrow[n] * nb + b0 + k;
-            const int pos = S8 ? ((n % 8) / 2) * (2 * (BN / 8)) + (n / 8) * 2 + (n % 2) : n;
-            cp_async4_zfill(sbs + (k * BN + pos) * 4, ok ? (const void *)src : (const void *)a.xs, ok);
+            cp_async4_zfill(sbs + (k * BN + n) * 4, ok ? (const void *)src : (const void *)a.xs, ok);
         }
     };
 
@@ -296,174 +294,235 @@ __device__ __forceinline__ void gemm_item(const GemmArgs &a, int item_idx) {
     for (int j = 0; j < NT; j++) acc[j][0] = acc[j][1] = make_float2(0.f, 0.f);
     const int jv = (ncols + 7) >> 3;  // n8 tiles holding valid columns (warp-uniform)
 
-#pragma unroll
-    for (int s = 0; s < G_STAGES - 1; s++) {
-        if (s < nchunks) load_chunk(s, s);
-        cp_async_commit();
-    }
     const int rA = warp * 16 + g;
-    for (int c = 0; c < nchunks; c++) {
-        cp_async_wait<G_STAGES - 2>();
-        __syncthreads();
-        {
-            int cn = c + G_STAGES - 1;
-            if (cn < nchunks) load_chunk(cn, cn % G_STAGES);
+    if constexpr (S8) {
+        // ---- int8 path (m16n8k32.s8). Each thread's copies are fixed for the item, so a
+        // chunk only moves the sources along K. The activation scales sit in shared memory
+        // as [block][t][tile][pair]: the 2 NT scales of the column pairs (8j + 2t,
+        // 8j + 2t + 1) that one thread uses in a block are 16-byte loads ----
+        constexpr int APR = T::CB * G_BKB / 16;          // 16-byte code pieces per row and chunk
+        constexpr int NA = G_BM * APR / G_THREADS;       // per thread: 2 (q4_0), 4 (q8_0), 1 (tq2)
+        static_assert(NA >= 1 && G_BM * APR % G_THREADS == 0, "code pieces per thread");
+        static_assert(BN * 8 == G_THREADS, "one activation piece per thread");
+        static_assert(BN * G_BKB <= G_THREADS, "one activation scale per thread");
+        // piece k of this thread: row r0 + k * RSTEP, the same 16 bytes of it
+        constexpr int RSTEP = G_THREADS / APR;
+        const int r0 = tid / APR, ap = tid % APR, alim = (ap * 16) / T::CB;
+        const uint8_t *asrc = codes + (size_t)(m0 + r0) * code_row + ap * 16;
+        const uint32_t adst = r0 * T::A_STRIDE + ap * 16;
+        const uint8_t *sc = T::HAS_WSCALE ? reinterpret_cast<const uint8_t *>(a.scale) + (long)it.group * a.scale_gstride
+                                          : nullptr;
+        const int nbp = (nb + 7) & ~7;
+        const bool s_ok = T::HAS_WSCALE && tid < G_BM && m0 + tid < a.O;
+        const uint8_t *ssrc = s_ok ? sc + (size_t)(m0 + tid) * nbp * 2 : sc;
+        const int bn_ = tid >> 3, bp = tid & 7;
+        const bool b_ok = bn_ < ncols;
+        const uint8_t *bsrc = xbase + (size_t)col_xrow[bn_] * xrow_bytes + bp * 16;
+        const int sn = (tid >> 2) % BN, sk = tid & 3;
+        const bool d_thr = tid < BN * G_BKB, d_ok = d_thr && sn < ncols;
+        const float *dsrc = a.xs + (size_t)col_xrow[sn] * nb + sk;
+        const int dpos = (sk * BN + ((sn % 8) / 2) * (2 * NT) + (sn / 8) * 2 + (sn % 2)) * 4;
+
+        auto load8 = [&](int c, int s) {
+            uint8_t *sa = stage_ptr(s);
+            uint8_t *sas = sa + L::A_BYTES;
+            uint8_t *sb = sas + L::AS_BYTES;
+            uint8_t *sbs = sb + L::B_BYTES;
+            const int b0 = c * G_BKB;
+            const int nbk = nb - b0 < G_BKB ? nb - b0 : G_BKB;
+#pragma unroll
+            for (int k = 0; k < NA; k++) {
+                const bool ok = alim < nbk && m0 + r0 + k * RSTEP < a.O;
+                cp_async16_zfill(sa + adst + k * RSTEP * T::A_STRIDE,
+                                 ok ? asrc + (size_t)k * RSTEP * code_row + (size_t)b0 * T::CB : codes, ok);
+            }
+            if (T::HAS_WSCALE && tid < G_BM) cp_async8_zfill(sas + tid * 8, ssrc + b0 * 2, s_ok);
+            {
+                const bool ok = b_ok && (bp >> 1) < nbk;
+                cp_async16_zfill(sb + bn_ * L::B_STRIDE + bp * 16, ok ? bsrc + b0 * 32 : xbase, ok);
+            }
+            if (d_thr) {
+                const bool ok = d_ok && sk < nbk;
+                cp_async4_zfill(sbs + dpos, ok ? dsrc + b0 : a.xs, ok);
+            }
+        };
+
+#pragma unroll
+        for (int s = 0; s < G_STAGES - 1; s++) {
+            if (s < nchunks) load8(s, s);
             cp_async_commit();
         }
-        const uint8_t *sa = stage_ptr(c % G_STAGES);
-        const uint8_t *sas = sa + L::A_BYTES;
-        const uint8_t *sb = sas + L::AS_BYTES;
-        const float *sbs = reinterpret_cast<const float *>(sb + L::B_BYTES);
-        const int nbk = nb - c * G_BKB < G_BKB ? nb - c * G_BKB : G_BKB;
-        // one K block: fragments, MMAs for the valid n8 tiles, block-scale epilogue
-        auto block8 = [&](int kb) {
-            // A fragment of m16n8k32: {row g k 4t.., row g+8 k 4t.., row g k 16+4t.., row g+8 k 16+4t..}
-            uint32_t a0, a1, a2, a3;
-            const uint8_t *r0 = sa + rA * T::A_STRIDE, *r1 = r0 + 8 * T::A_STRIDE;
-            if (FMT == GPU_FMT_Q40) {
-                // the q4_0 byte layout is the fragment split: low nibbles k, high k+16.
-                // Each nibble q goes to the high half of its byte xor 8: the signed byte is
-                // then 16 (q - 8) exactly (one op for a high nibble, two for a low one); the
-                // factor 16 leaves through the weight scale dw / 16 (a power of two, so
-                // every product and rounding below is the same as with q - 8 and dw).
-                uint32_t w0 = *reinterpret_cast<const uint32_t *>(r0 + kb * 16 + 4 * t);
-                uint32_t w1 = *reinterpret_cast<const uint32_t *>(r1 + kb * 16 + 4 * t);
-                a0 = ((w0 << 4) & 0xF0F0F0F0u) ^ 0x80808080u; a2 = (w0 & 0xF0F0F0F0u) ^ 0x80808080u;
-                a1 = ((w1 << 4) & 0xF0F0F0F0u) ^ 0x80808080u; a3 = (w1 & 0xF0F0F0F0u) ^ 0x80808080u;
-            } else if (FMT == GPU_FMT_Q80) {
-                const uint8_t *p0 = r0 + kb * 32 + 4 * t, *p1 = r1 + kb * 32 + 4 * t;
-                a0 = *reinterpret_cast<const uint32_t *>(p0); a2 = *reinterpret_cast<const uint32_t *>(p0 + 16);
-                a1 = *reinterpret_cast<const uint32_t *>(p1); a3 = *reinterpret_cast<const uint32_t *>(p1 + 16);
-            } else {
-                const int sh = (kb & 1) * 4;
-                uint32_t w0 = *reinterpret_cast<const uint32_t *>(r0 + (kb >> 1) * 16 + 4 * t);
-                uint32_t w1 = *reinterpret_cast<const uint32_t *>(r1 + (kb >> 1) * 16 + 4 * t);
-                a0 = (w0 >> sh) & 0x03030303u; a2 = (w0 >> (sh + 2)) & 0x03030303u;
-                a1 = (w1 >> sh) & 0x03030303u; a3 = (w1 >> (sh + 2)) & 0x03030303u;
-            }
-            // per row: dw and -M*dw (exact: dw has 11 significant bits), so that
-            // fma(F, dw, -M*dw) = dw * I rounded once for F = M + I
-            float w0 = 1.f, w1 = 1.f;
-            if (T::HAS_WSCALE) {
-                const __half *hs = reinterpret_cast<const __half *>(sas);
-                w0 = __half2float(hs[rA * G_BKB + kb]);
-                w1 = __half2float(hs[(rA + 8) * G_BKB + kb]);
-                if (FMT == GPU_FMT_Q40) { w0 *= 0.0625f; w1 *= 0.0625f; }  // codes carry 16 (q - 8)
-            }
-            const float2 dw0 = make_float2(w0, w0), dw1 = make_float2(w1, w1);
-            const float2 cm0 = make_float2(-S8_BIAS_F * w0, -S8_BIAS_F * w0), cm1 = make_float2(-S8_BIAS_F * w1, -S8_BIAS_F * w1);
-            // this thread's activation scales of the block: column pairs 8j + 2t (+1)
-            float dxv[2 * NT];
-#pragma unroll
-            for (int q4 = 0; q4 < NT / 2; q4++) {
-                const float4 v = *reinterpret_cast<const float4 *>(sbs + kb * BN + t * 2 * NT + 4 * q4);
-                dxv[4 * q4] = v.x; dxv[4 * q4 + 1] = v.y; dxv[4 * q4 + 2] = v.z; dxv[4 * q4 + 3] = v.w;
-            }
-            auto tile = [&](int j, uint32_t b0, uint32_t b1) {
-                int c[4];
-                mma_s8(c, a0, a1, a2, a3, b0, b1);
-                const float2 dx = make_float2(dxv[2 * j], dxv[2 * j + 1]);
-                const float2 f01 = make_float2(__int_as_float(c[0]), __int_as_float(c[1]));
-                const float2 f23 = make_float2(__int_as_float(c[2]), __int_as_float(c[3]));
-                // dw * I (one rounding), then + dx * (dw * I)
-                acc[j][0] = ffma2(ffma2(f01, dw0, cm0), dx, acc[j][0]);
-                acc[j][1] = ffma2(ffma2(f23, dw1, cm1), dx, acc[j][1]);
-            };
-            // B fragments of two n8 tiles per ldmatrix.x4: matrices (tile jp, k 0-15),
-            // (jp, k 16-31), (jp+1, k 0-15), (jp+1, k 16-31); lane l addresses row l % 8
-            // of matrix l / 8, and receives row g, bytes 4t..4t+3 of each
-#pragma unroll
-            for (int jp = 0; jp < NT; jp += 2) {
-                if (jp < jv) {
-                    uint32_t b0, b1, b2, b3;
-                    const int lrow = (jp + (lane >> 4)) * 8 + (lane & 7);
-                    ldsm_x4(b0, b1, b2, b3, sb + lrow * L::B_STRIDE + kb * 32 + ((lane >> 3) & 1) * 16);
-                    tile(jp, b0, b1);
-                    if (jp + 1 < jv) tile(jp + 1, b2, b3);
-                }
-            }
-        };
-        auto block = [&](int kb) {
-            if constexpr (S8) {
-                block8(kb);
-                return;
-            }
-            // A fragments of the two k16 steps of this block: s0 = k 0..15, s1 = k 16..31
-            uint32_t a0[4], a1[4];  // {row g k 2t.., row g+8 k 2t.., row g k 2t+8.., row g+8 k 2t+8..}
+        for (int c = 0; c < nchunks; c++) {
+            cp_async_wait<G_STAGES - 2>();
+            __syncthreads();
             {
+                int cn = c + G_STAGES - 1;
+                if (cn < nchunks) load8(cn, cn % G_STAGES);
+                cp_async_commit();
+            }
+            const uint8_t *sa = stage_ptr(c % G_STAGES);
+            const uint8_t *sas = sa + L::A_BYTES;
+            const uint8_t *sb = sas + L::AS_BYTES;
+            const float *sbs = reinterpret_cast<const float *>(sb + L::B_BYTES);
+            const int nbk = nb - c * G_BKB < G_BKB ? nb - c * G_BKB : G_BKB;
+            auto blk = [&](int kb) {
+                uint32_t a0, a1, a2, a3;
                 const uint8_t *r0 = sa + rA * T::A_STRIDE, *r1 = r0 + 8 * T::A_STRIDE;
                 if (FMT == GPU_FMT_Q40) {
-                    const int o = kb * 16 + 2 * t;
-                    uint32_t p00 = spread2(*reinterpret_cast<const uint16_t *>(r0 + o));
-                    uint32_t p10 = spread2(*reinterpret_cast<const uint16_t *>(r1 + o));
-                    uint32_t p01 = spread2(*reinterpret_cast<const uint16_t *>(r0 + o + 8));
-                    uint32_t p11 = spread2(*reinterpret_cast<const uint16_t *>(r1 + o + 8));
-                    a0[0] = q4lo_h2(p00); a0[1] = q4lo_h2(p10); a0[2] = q4lo_h2(p01); a0[3] = q4lo_h2(p11);
-                    a1[0] = q4hi_h2(p00); a1[1] = q4hi_h2(p10); a1[2] = q4hi_h2(p01); a1[3] = q4hi_h2(p11);
+                    // low nibbles are k = j, high k = j + 16: the fragment split. Nibble q
+                    // to the high half of its byte xor 8 gives the signed byte 16 (q - 8)
+                    uint32_t w0 = *reinterpret_cast<const uint32_t *>(r0 + kb * 16 + 4 * t);
+                    uint32_t w1 = *reinterpret_cast<const uint32_t *>(r1 + kb * 16 + 4 * t);
+                    a0 = ((w0 << 4) & 0xF0F0F0F0u) ^ 0x80808080u; a2 = (w0 & 0xF0F0F0F0u) ^ 0x80808080u;
+                    a1 = ((w1 << 4) & 0xF0F0F0F0u) ^ 0x80808080u; a3 = (w1 & 0xF0F0F0F0u) ^ 0x80808080u;
                 } else if (FMT == GPU_FMT_Q80) {
-                    const int o = kb * 32 + 2 * t;
-                    a0[0] = s8_h2(spread2(*reinterpret_cast<const uint16_t *>(r0 + o)));
-                    a0[1] = s8_h2(spread2(*reinterpret_cast<const uint16_t *>(r1 + o)));
-                    a0[2] = s8_h2(spread2(*reinterpret_cast<const uint16_t *>(r0 + o + 8)));
-                    a0[3] = s8_h2(spread2(*reinterpret_cast<const uint16_t *>(r1 + o + 8)));
-                    a1[0] = s8_h2(spread2(*reinterpret_cast<const uint16_t *>(r0 + o + 16)));
-                    a1[1] = s8_h2(spread2(*reinterpret_cast<const uint16_t *>(r1 + o + 16)));
-                    a1[2] = s8_h2(spread2(*reinterpret_cast<const uint16_t *>(r0 + o + 24)));
-                    a1[3] = s8_h2(spread2(*reinterpret_cast<const uint16_t *>(r1 + o + 24)));
+                    const uint8_t *p0 = r0 + kb * 32 + 4 * t, *p1 = r1 + kb * 32 + 4 * t;
+                    a0 = *reinterpret_cast<const uint32_t *>(p0); a2 = *reinterpret_cast<const uint32_t *>(p0 + 16);
+                    a1 = *reinterpret_cast<const uint32_t *>(p1); a3 = *reinterpret_cast<const uint32_t *>(p1 + 16);
                 } else {
-                    const int o = (kb >> 1) * 16 + 2 * t, sh = (kb & 1) * 4;
-                    uint32_t p00 = spread2(*reinterpret_cast<const uint16_t *>(r0 + o));
-                    uint32_t p10 = spread2(*reinterpret_cast<const uint16_t *>(r1 + o));
-                    uint32_t p01 = spread2(*reinterpret_cast<const uint16_t *>(r0 + o + 8));
-                    uint32_t p11 = spread2(*reinterpret_cast<const uint16_t *>(r1 + o + 8));
-                    a0[0] = c2_h2(p00, sh); a0[1] = c2_h2(p10, sh); a0[2] = c2_h2(p01, sh); a0[3] = c2_h2(p11, sh);
-                    a1[0] = c2_h2(p00, sh + 2); a1[1] = c2_h2(p10, sh + 2);
-                    a1[2] = c2_h2(p01, sh + 2); a1[3] = c2_h2(p11, sh + 2);
+                    const int sh = (kb & 1) * 4;
+                    uint32_t w0 = *reinterpret_cast<const uint32_t *>(r0 + (kb >> 1) * 16 + 4 * t);
+                    uint32_t w1 = *reinterpret_cast<const uint32_t *>(r1 + (kb >> 1) * 16 + 4 * t);
+                    a0 = (w0 >> sh) & 0x03030303u; a2 = (w0 >> (sh + 2)) & 0x03030303u;
+                    a1 = (w1 >> sh) & 0x03030303u; a3 = (w1 >> (sh + 2)) & 0x03030303u;
                 }
-            }
-            float2 dw0 = make_float2(1.f, 1.f), dw1 = make_float2(1.f, 1.f);
-            if (T::HAS_WSCALE) {
-                const __half *hs = reinterpret_cast<const __half *>(sas);
-                float w0 = __half2float(hs[rA * G_BKB + kb]), w1 = __half2float(hs[(rA + 8) * G_BKB + kb]);
-                dw0 = make_float2(w0, w0);
-                dw1 = make_float2(w1, w1);
-            }
+                float2 dw0 = make_float2(1.f, 1.f), dw1 = dw0;
+                float2 cm0 = make_float2(-S8_BIAS_F, -S8_BIAS_F), cm1 = cm0;
+                if (T::HAS_WSCALE) {
+                    const __half *hs = reinterpret_cast<const __half *>(sas);
+                    float w0 = __half2float(hs[rA * G_BKB + kb]), w1 = __half2float(hs[(rA + 8) * G_BKB + kb]);
+                    if (FMT == GPU_FMT_Q40) { w0 *= 0.0625f; w1 *= 0.0625f; }
+                    dw0 = make_float2(w0, w0); dw1 = make_float2(w1, w1);
+                    cm0 = make_float2(-S8_BIAS_F * w0, -S8_BIAS_F * w0); cm1 = make_float2(-S8_BIAS_F * w1, -S8_BIAS_F * w1);
+                }
+                auto tile = [&](int j, uint32_t b0, uint32_t b1, float2 dx) {
+                    int cc[4];
+                    mma_s8(cc, a0, a1, a2, a3, b0, b1);
+                    const float2 f01 = make_float2(__int_as_float(cc[0]), __int_as_float(cc[1]));
+                    const float2 f23 = make_float2(__int_as_float(cc[2]), __int_as_float(cc[3]));
+                    // dw * I rounded once, then + dx * (dw * I)
+                    acc[j][0] = ffma2(ffma2(f01, dw0, cm0), dx, acc[j][0]);
+                    acc[j][1] = ffma2(ffma2(f23, dw1, cm1), dx, acc[j][1]);
+                };
+                // B fragments of n8 tiles jp, jp + 1 per ldmatrix.x4 and their 4 activation
+                // scales per 16-byte load (columns 8j + 2t, 8j + 2t + 1)
 #pragma unroll
-            for (int j = 0; j < NT; j++) {
-                if (j < jv) {
-                    uint32_t b00, b01, b10, b11;  // step 0: k 2t.., k 2t+8..; step 1: +16
-                    if (B_HALF) {
-                        // lanes 0-7 address k 0-7 of rows n, 8-15 k 8-15, 16-23 k 16-23, 24-31 k 24-31
-                        const uint8_t *pb = sb + (j * 8 + (lane & 7)) * L::B_STRIDE + kb * 64 + (lane >> 3) * 16;
-                        ldsm_x4(b00, b01, b10, b11, pb);
-                    } else {
-                        const uint8_t *pb = sb + (j * 8 + g) * L::B_STRIDE + kb * 32 + 2 * t;
-                        b00 = s8_h2(spread2(*reinterpret_cast<const uint16_t *>(pb)));
-                        b01 = s8_h2(spread2(*reinterpret_cast<const uint16_t *>(pb + 8)));
-                        b10 = s8_h2(spread2(*reinterpret_cast<const uint16_t *>(pb + 16)));
-                        b11 = s8_h2(spread2(*reinterpret_cast<const uint16_t *>(pb + 24)));
-                    }
-                    float d[4];
-                    mma_f16(d, a0[0], a0[1], a0[2], a0[3], b00, b01, 0.f, 0.f, 0.f, 0.f);
-                    mma_f16(d, a1[0], a1[1], a1[2], a1[3], b10, b11, d[0], d[1], d[2], d[3]);
-                    // d = this block's exact integer sums; scale by dw*dx and accumulate
-                    const float2 dx = *reinterpret_cast<const float2 *>(sbs + kb * BN + j * 8 + 2 * t);
-                    if (T::HAS_WSCALE) {
-                        acc[j][0] = ffma2(fmul2(dw0, dx), make_float2(d[0], d[1]), acc[j][0]);
-                        acc[j][1] = ffma2(fmul2(dw1, dx), make_float2(d[2], d[3]), acc[j][1]);
-                    } else {
-                        acc[j][0] = ffma2(dx, make_float2(d[0], d[1]), acc[j][0]);
-                        acc[j][1] = ffma2(dx, make_float2(d[2], d[3]), acc[j][1]);
+                for (int jp = 0; jp < NT; jp += 2) {
+                    if (jp < jv) {
+                        uint32_t b0, b1, b2, b3;
+                        const int lrow = (jp + (lane >> 4)) * 8 + (lane & 7);
+                        ldsm_x4(b0, b1, b2, b3, sb + lrow * L::B_STRIDE + kb * 32 + ((lane >> 3) & 1) * 16);
+                        const float4 dx = *reinterpret_cast<const float4 *>(sbs + kb * BN + t * 2 * NT + 2 * jp);
+                        tile(jp, b0, b1, make_float2(dx.x, dx.y));
+                        if (jp + 1 < jv) tile(jp + 1, b2, b3, make_float2(dx.z, dx.w));
                     }
                 }
-            }
-        };
-        if (nbk == G_BKB) {
-            // full chunk: unrolled so the 4 blocks' MMA -> FMA chains interleave
+            };
+            if (nbk == G_BKB) {
 #pragma unroll
-            for (int kb = 0; kb < G_BKB; kb++) block(kb);
-        } else {
-            for (int kb = 0; kb < nbk; kb++) block(kb);
+                for (int kb = 0; kb < G_BKB; kb++) blk(kb);
+            } else {
+                for (int kb = 0; kb < nbk; kb++) blk(kb);
+            }
+        }
+    } else {
+    #pragma unroll
+        for (int s = 0; s < G_STAGES - 1; s++) {
+            if (s < nchunks) load_chunk(s, s);
+            cp_async_commit();
+        }
+        for (int c = 0; c < nchunks; c++) {
+            cp_async_wait<G_STAGES - 2>();
+            __syncthreads();
+            {
+                int cn = c + G_STAGES - 1;
+                if (cn < nchunks) load_chunk(cn, cn % G_STAGES);
+                cp_async_commit();
+            }
+            const uint8_t *sa = stage_ptr(c % G_STAGES);
+            const uint8_t *sas = sa + L::A_BYTES;
+            const uint8_t *sb = sas + L::AS_BYTES;
+            const float *sbs = reinterpret_cast<const float *>(sb + L::B_BYTES);
+            const int nbk = nb - c * G_BKB < G_BKB ? nb - c * G_BKB : G_BKB;
+            // one K block: fragments, MMAs for the valid n8 tiles, block-scale epilogue
+            auto block = [&](int kb) {
+                // A fragments of the two k16 steps of this block: s0 = k 0..15, s1 = k 16..31
+                uint32_t a0[4], a1[4];  // {row g k 2t.., row g+8 k 2t.., row g k 2t+8.., row g+8 k 2t+8..}
+                {
+                    const uint8_t *r0 = sa + rA * T::A_STRIDE, *r1 = r0 + 8 * T::A_STRIDE;
+                    if (FMT == GPU_FMT_Q40) {
+                        const int o = kb * 16 + 2 * t;
+                        uint32_t p00 = spread2(*reinterpret_cast<const uint16_t *>(r0 + o));
+                        uint32_t p10 = spread2(*reinterpret_cast<const uint16_t *>(r1 + o));
+                        uint32_t p01 = spread2(*reinterpret_cast<const uint16_t *>(r0 + o + 8));
+                        uint32_t p11 = spread2(*reinterpret_cast<const uint16_t *>(r1 + o + 8));
+                        a0[0] = q4lo_h2(p00); a0[1] = q4lo_h2(p10); a0[2] = q4lo_h2(p01); a0[3] = q4lo_h2(p11);
+                        a1[0] = q4hi_h2(p00); a1[1] = q4hi_h2(p10); a1[2] = q4hi_h2(p01); a1[3] = q4hi_h2(p11);
+                    } else if (FMT == GPU_FMT_Q80) {
+                        const int o = kb * 32 + 2 * t;
+                        a0[0] = s8_h2(spread2(*reinterpret_cast<const uint16_t *>(r0 + o)));
+                        a0[1] = s8_h2(spread2(*reinterpret_cast<const uint16_t *>(r1 + o)));
+                        a0[2] = s8_h2(spread2(*reinterpret_cast<const uint16_t *>(r0 + o + 8)));
+                        a0[3] = s8_h2(spread2(*reinterpret_cast<const uint16_t *>(r1 + o + 8)));
+                        a1[0] = s8_h2(spread2(*reinterpret_cast<const uint16_t *>(r0 + o + 16)));
+                        a1[1] = s8_h2(spread2(*reinterpret_cast<const uint16_t *>(r1 + o + 16)));
+                        a1[2] = s8_h2(spread2(*reinterpret_cast<const uint16_t *>(r0 + o + 24)));
+                        a1[3] = s8_h2(spread2(*reinterpret_cast<const uint16_t *>(r1 + o + 24)));
+                    } else {
+                        const int o = (kb >> 1) * 16 + 2 * t, sh = (kb & 1) * 4;
+                        uint32_t p00 = spread2(*reinterpret_cast<const uint16_t *>(r0 + o));
+                        uint32_t p10 = spread2(*reinterpret_cast<const uint16_t *>(r1 + o));
+                        uint32_t p01 = spread2(*reinterpret_cast<const uint16_t *>(r0 + o + 8));
+                        uint32_t p11 = spread2(*reinterpret_cast<const uint16_t *>(r1 + o + 8));
+                        a0[0] = c2_h2(p00, sh); a0[1] = c2_h2(p10, sh); a0[2] = c2_h2(p01, sh); a0[3] = c2_h2(p11, sh);
+                        a1[0] = c2_h2(p00, sh + 2); a1[1] = c2_h2(p10, sh + 2);
+                        a1[2] = c2_h2(p01, sh + 2); a1[3] = c2_h2(p11, sh + 2);
+                    }
+                }
+                float2 dw0 = make_float2(1.f, 1.f), dw1 = make_float2(1.f, 1.f);
+                if (T::HAS_WSCALE) {
+                    const __half *hs = reinterpret_cast<const __half *>(sas);
+                    float w0 = __half2float(hs[rA * G_BKB + kb]), w1 = __half2float(hs[(rA + 8) * G_BKB + kb]);
+                    dw0 = make_float2(w0, w0);
+                    dw1 = make_float2(w1, w1);
+                }
+    #pragma unroll
+                for (int j = 0; j < NT; j++) {
+                    if (j < jv) {
+                        uint32_t b00, b01, b10, b11;  // step 0: k 2t.., k 2t+8..; step 1: +16
+                        if (B_HALF) {
+                            // lanes 0-7 address k 0-7 of rows n, 8-15 k 8-15, 16-23 k 16-23, 24-31 k 24-31
+                            const uint8_t *pb = sb + (j * 8 + (lane & 7)) * L::B_STRIDE + kb * 64 + (lane >> 3) * 16;
+                            ldsm_x4(b00, b01, b10, b11, pb);
+                        } else {
+                            const uint8_t *pb = sb + (j * 8 + g) * L::B_STRIDE + kb * 32 + 2 * t;
+                            b00 = s8_h2(spread2(*reinterpret_cast<const uint16_t *>(pb)));
+                            b01 = s8_h2(spread2(*reinterpret_cast<const uint16_t *>(pb + 8)));
+                            b10 = s8_h2(spread2(*reinterpret_cast<const uint16_t *>(pb + 16)));
+                            b11 = s8_h2(spread2(*reinterpret_cast<const uint16_t *>(pb + 24)));
+                        }
+                        float d[4];
+                        mma_f16(d, a0[0], a0[1], a0[2], a0[3], b00, b01, 0.f, 0.f, 0.f, 0.f);
+                        mma_f16(d, a1[0], a1[1], a1[2], a1[3], b10, b11, d[0], d[1], d[2], d[3]);
+                        // d = this block's exact integer sums; scale by dw*dx and accumulate
+                        const float2 dx = *reinterpret_cast<const float2 *>(sbs + kb * BN + j * 8 + 2 * t);
+                        if (T::HAS_WSCALE) {
+                            acc[j][0] = ffma2(fmul2(dw0, dx), make_float2(d[0], d[1]), acc[j][0]);
+                            acc[j][1] = ffma2(fmul2(dw1, dx), make_float2(d[2], d[3]), acc[j][1]);
+                        } else {
+                            acc[j][0] = ffma2(dx, make_float2(d[0], d[1]), acc[j][0]);
+                            acc[j][1] = ffma2(dx, make_float2(d[2], d[3]), acc[j][1]);
+                        }
+                    }
+                }
+            };
+            if (nbk == G_BKB) {
+                // full chunk: unrolled so the 4 blocks' MMA -> FMA chains interleave
+    #pragma unroll
+                for (int kb = 0; kb < G_BKB; kb++) block(kb);
+            } else {
+                for (int kb = 0; kb < nbk; kb++) block(kb);
+            }
         }
     }
     cp_async_wait<0>();
@@ -556,7 +615,8 @@ __device__ __forceinline__ void gemm_item(const GemmArgs &a, int item_idx) {
 // grid capped below the worst-case item count then launches no CTA that finds no item;
 // the loop costs a few registers, so exact grids use the plain form).
 template <int FMT, int BN, int EPI, bool B_HALF, bool S8 = false, bool STRIDE = false>
-__global__ void __launch_bounds__(G_THREADS) k_gemm(GemmArgs a) {
+// (4 CTAs per SM: the int8 path fits 64 registers and its 33 KB of shared memory)
+__global__ void __launch_bounds__(G_THREADS, 4) k_gemm(GemmArgs a) {
     const int n = a.n_items ? *a.n_items : (int)gridDim.y;
     if constexpr (!STRIDE) {
         if ((int)blockIdx.y < n) gemm_item<FMT, BN, EPI, B_HALF, S8>(a, blockIdx.y);

@@ -71,7 +71,7 @@ static inline size_t a256(size_t n) { return (n + 255) & ~(size_t)255; }
 
 template <int FMT, int BN, int EPI, bool BH, bool S8, bool STRIDE>
 static int launch_gemm_k(const GemmArgs &a, dim3 grid, cudaStream_t st) {
-    constexpr int smem = GemmSmem<FMT, BN, BH>::TOTAL;
+    constexpr int smem = GemmSmem<FMT, BN, BH, S8>::TOTAL;
     static bool attr_set = false;  // per process; the library drives one device
     if (!attr_set) {
         if (!check_cuda(cudaFuncSetAttribute(k_gemm<FMT, BN, EPI, BH, S8, STRIDE>,
