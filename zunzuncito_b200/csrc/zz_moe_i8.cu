@@ -139,7 +139,7 @@ __host__ __device__ constexpr uint32_t idesc_i8(int M, int N) {
     return (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
 }
 #ifndef ZZ_I8_PRESET
-#define ZZ_I8_PRESET 1
+#define ZZ_I8_PRESET 0
 #endif
 __device__ __forceinline__ void mma_i8_acc(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc) {
 #if ZZ_I8_PRESET

@@ -94,9 +94,12 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, volati
         if (blockIdx.x == 0 && (threadIdx.x & 31) == 0) atomicAdd(&g_tc_prof[64 + code], 1ull);
 #endif
         for (int i = 0; i < 16; i++) {
-            __nanosleep(ns);
+#ifndef ZZ_TC_MAXSLEEP
+#define ZZ_TC_MAXSLEEP 256
+#endif
+            if (ZZ_TC_MAXSLEEP) __nanosleep(ns);
             if (mbar_try(bar, parity)) return true;
-            ns = ns < 256 ? 2 * ns : 256;
+            ns = ns < ZZ_TC_MAXSLEEP ? 2 * ns : ZZ_TC_MAXSLEEP;
         }
         if (*abort) return false;
         if (global_ns() - w0 > WAIT_LIMIT_NS) break;
