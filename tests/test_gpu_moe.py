@@ -122,11 +122,12 @@ def check_pairs(orc, kind, blobs, X, eidx, ewt, out_gpu, bank, pairs=None):
     return flipped_tok
 
 
-@pytest.fixture(params=["auto", "i8", "mma8"])
+@pytest.fixture(params=["auto", "i8", "mma8", "mma8w"])
 def engine(request, monkeypatch):
     """every expert engine: auto (the decode GEMV kernels for calls of <= 64 pairs, else the
-    int8 tcgen05 engine), and the int8 tcgen05 / int8 mma.sync engines forced for every
-    call size (ZZ_MOE_KERNEL)"""
+    int8 mma.sync GEMM with 32- or 64-row items by the rows per expert), and the int8
+    tcgen05 engine and the narrow / wide mma.sync items forced for every call size
+    (ZZ_MOE_KERNEL)"""
     monkeypatch.setenv("ZZ_MOE_KERNEL", request.param)
     return request.param
 
@@ -175,6 +176,25 @@ def test_moe_declines():
         zz.moe_ffn(bank, X, bad, w, zz.ZZ_ACT_GEGLU_TANH, validate=True)
     with pytest.raises(zz.ZZError):
         zz.moe_ffn(bank, X, bad, w, 7)
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_moe_two_devices_one_thread(orc):
+    # the library's per-device state (side stream, fork/join events): one host thread runs
+    # the layer on device 0, then device 1, then device 0 again, with the same result
+    E, D, MI, K, S = 8, 256, 128, 4, 80
+    blobs = make_blobs(orc, 0, 1300, E, D, MI)
+    X = synth.gaussian(1310, (S, D))
+    eidx, ewt, _ = synth.zipf_routing(1320, S, E, K)
+    outs = []
+    for d in (0, 1, 0):
+        with torch.cuda.device(d):
+            t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(f"cuda:{d}")
+            bank = zz.ExpertBankDev(zz.GPU_FMT_Q40, t(blobs), D, MI)
+            outs.append(zz.moe_ffn(bank, t(X), t(eidx), t(ewt), zz.ZZ_ACT_GEGLU_TANH).cpu().numpy())
+    scale = np.max(np.abs(outs[0]))
+    for o in outs[1:]:
+        assert np.max(np.abs(o - outs[0])) <= 1e-6 * scale
 
 
 def _gemma_blobs(seed, E=synth.GEMMA_E):

@@ -303,7 +303,8 @@ __device__ __forceinline__ void gemm_item(const GemmArgs &a, int item_idx) {
         constexpr int APR = T::CB * G_BKB / 16;          // 16-byte code pieces per row and chunk
         constexpr int NA = G_BM * APR / G_THREADS;       // per thread: 2 (q4_0), 4 (q8_0), 1 (tq2)
         static_assert(NA >= 1 && G_BM * APR % G_THREADS == 0, "code pieces per thread");
-        static_assert(BN * 8 == G_THREADS, "one activation piece per thread");
+        static_assert(BN * 8 % G_THREADS == 0, "whole activation pieces per thread");
+        constexpr int NBP = BN * 8 / G_THREADS, BSTEP = G_THREADS / 8;  // pieces per thread, row step
         static_assert(BN * G_BKB <= G_THREADS, "one activation scale per thread");
         // piece k of this thread: row r0 + k * RSTEP, the same 16 bytes of it
         constexpr int RSTEP = G_THREADS / APR;
@@ -315,9 +316,10 @@ __device__ __forceinline__ void gemm_item(const GemmArgs &a, int item_idx) {
         const int nbp = (nb + 7) & ~7;
         const bool s_ok = T::HAS_WSCALE && tid < G_BM && m0 + tid < a.O;
         const uint8_t *ssrc = s_ok ? sc + (size_t)(m0 + tid) * nbp * 2 : sc;
-        const int bn_ = tid >> 3, bp = tid & 7;
-        const bool b_ok = bn_ < ncols;
-        const uint8_t *bsrc = xbase + (size_t)col_xrow[bn_] * xrow_bytes + bp * 16;
+        const int bn_ = tid >> 3, bp = tid & 7;  // piece k: row bn_ + k BSTEP, bytes 16 bp of the chunk
+        const uint8_t *bsrc[NBP];
+#pragma unroll
+        for (int k = 0; k < NBP; k++) bsrc[k] = xbase + (size_t)col_xrow[bn_ + k * BSTEP] * xrow_bytes + bp * 16;
         const int sn = (tid >> 2) % BN, sk = tid & 3;
         const bool d_thr = tid < BN * G_BKB, d_ok = d_thr && sn < ncols;
         const float *dsrc = a.xs + (size_t)col_xrow[sn] * nb + sk;
@@ -337,9 +339,10 @@ __device__ __forceinline__ void gemm_item(const GemmArgs &a, int item_idx) {
                                  ok ? asrc + (size_t)k * RSTEP * code_row + (size_t)b0 * T::CB : codes, ok);
             }
             if (T::HAS_WSCALE && tid < G_BM) cp_async8_zfill(sas + tid * 8, ssrc + b0 * 2, s_ok);
-            {
-                const bool ok = b_ok && (bp >> 1) < nbk;
-                cp_async16_zfill(sb + bn_ * L::B_STRIDE + bp * 16, ok ? bsrc + b0 * 32 : xbase, ok);
+#pragma unroll
+            for (int k = 0; k < NBP; k++) {
+                const bool ok = bn_ + k * BSTEP < ncols && (bp >> 1) < nbk;
+                cp_async16_zfill(sb + (bn_ + k * BSTEP) * L::B_STRIDE + bp * 16, ok ? bsrc[k] + b0 * 32 : xbase, ok);
             }
             if (d_thr) {
                 const bool ok = d_ok && sk < nbk;
@@ -615,8 +618,11 @@ __device__ __forceinline__ void gemm_item(const GemmArgs &a, int item_idx) {
 // grid capped below the worst-case item count then launches no CTA that finds no item;
 // the loop costs a few registers, so exact grids use the plain form).
 template <int FMT, int BN, int EPI, bool B_HALF, bool S8 = false, bool STRIDE = false>
-// (4 CTAs per SM: the int8 path fits 64 registers and its 33 KB of shared memory)
-__global__ void __launch_bounds__(G_THREADS, 4) k_gemm(GemmArgs a) {
+// (4 CTAs per SM at BN <= 32: the int8 path fits 64 registers and 33 KB of shared memory)
+#ifndef ZZ_WIDE_MINB
+#define ZZ_WIDE_MINB 3
+#endif
+__global__ void __launch_bounds__(G_THREADS, BN <= 32 ? 4 : ZZ_WIDE_MINB) k_gemm(GemmArgs a) {
     const int n = a.n_items ? *a.n_items : (int)gridDim.y;
     if constexpr (!STRIDE) {
         if ((int)blockIdx.y < n) gemm_item<FMT, BN, EPI, B_HALF, S8>(a, blockIdx.y);

@@ -42,27 +42,27 @@ bool moe_i8_supported(int fmt, int D, int MI);
 int launch_moe_dec(int fmt, const GemmArgs &gu, const GemmArgs &dn, int P, float *hbuf, cudaStream_t st);
 
 // Expert engine. Default ("auto"): the small-batch GEMV kernels (zz_moe_dec.cu) when
-// S*K <= DEC_MAX_PAIRS, else the int8 mma.sync GEMM (k_gemm<..., S8>), the fastest
-// measured. ZZ_MOE_KERNEL=i8 selects the int8 tcgen05 engine (zz_moe_i8.cu) where the
-// layer's shape allows it, =mma8 the mma.sync GEMM for every call size. All are exact
-// per block.
-enum { ENG_DEC = 0, ENG_MMA8 = 3, ENG_I8 = 5 };
-constexpr int DEC_MAX_PAIRS = 64;
+// S*K <= DEC_MAX_PAIRS; else the int8 mma.sync GEMM (k_gemm<..., S8>), the fastest
+// measured, with work items of up to 32 routed rows, or of up to 64 rows when the experts
+// average at least WIDE_PAIRS_PER_EXPERT rows (prefill: the weight fragments then serve
+// twice the columns; at S=512 top-8 the narrow items are faster). ZZ_MOE_KERNEL=i8
+// selects the int8 tcgen05 engine (zz_moe_i8.cu) where the layer's shape allows it;
+// =mma8 / =mma8w force the narrow / wide mma.sync items. All are exact per block.
+enum { ENG_DEC = 0, ENG_MMA8 = 3, ENG_I8 = 5, ENG_MMA8W = 6 };
+constexpr int DEC_MAX_PAIRS = 64, WIDE_PAIRS_PER_EXPERT = 128;
 static int moe_engine(int P, const zz_expert_bank *b) {
     const char *e = getenv("ZZ_MOE_KERNEL");
     const bool i8_ok = moe_i8_supported(b->fmt, b->hidden, b->inter);
     if (e && !strcmp(e, "mma8")) return ENG_MMA8;
+    if (e && !strcmp(e, "mma8w")) return ENG_MMA8W;
     if (e && !strcmp(e, "i8")) return i8_ok ? ENG_I8 : ENG_MMA8;
     // the decode kernels take calls of up to DEC_MAX_PAIRS pairs
     if (P <= DEC_MAX_PAIRS) return ENG_DEC;
-    return ENG_MMA8;
+    return (long)P >= (long)WIDE_PAIRS_PER_EXPERT * b->n_experts ? ENG_MMA8W : ENG_MMA8;
 }
 constexpr int I8_BN = 128;
 
-#ifndef ZZ_MOE_BN
-#define ZZ_MOE_BN 32
-#endif
-constexpr int MOE_BN = ZZ_MOE_BN;
+constexpr int MOE_BN = 32, MOE_BN_WIDE = 64;
 constexpr int ROW_ALIGN = 4;
 constexpr int DEC_BN = 2;      // rows per work item of the small-batch kernels (DEC_C)
 constexpr int DENSE_BN = 64;
@@ -439,7 +439,6 @@ static int moe_impl(const zz_expert_bank *b, const float *X, const int8_t *xq_in
     MoeWs w = moe_layout(b, S, K, (uint8_t *)workspace);
     cudaStream_t st = (cudaStream_t)stream;
     const int fmt = b->fmt, D = b->hidden, MI = b->inter, E = b->n_experts, P = S * K;
-    const int maxit = P / MOE_BN + E + 1;
 
     if (validate) {
         int bad = 0;
@@ -452,7 +451,9 @@ static int moe_impl(const zz_expert_bank *b, const float *X, const int8_t *xq_in
     }
     prof_mark(st);
     const int eng = moe_engine(P, b);
-    const bool i8 = eng == ENG_I8;
+    const bool i8 = eng == ENG_I8, wide = eng == ENG_MMA8W;
+    const int bn = i8 ? I8_BN : eng == ENG_DEC ? DEC_BN : wide ? MOE_BN_WIDE : MOE_BN;
+    const int maxit = P / bn + E + 1;
     const int8_t *xq = xq_in;
     const float *xs = xs_in;
     // routing (eidx/ewt only) on the side stream, overlapping the quantization
@@ -461,7 +462,7 @@ static int moe_impl(const zz_expert_bank *b, const float *X, const int8_t *xq_in
     if (!check_cuda(cudaEventRecord(side->fork, st), "fork") ||
         !check_cuda(cudaStreamWaitEvent(side->s, side->fork, 0), "fork wait"))
         return 0;
-    k_route<<<1, 1024, 4 * E * sizeof(int), side->s>>>(eidx, ewt, P, E, i8 ? I8_BN : eng == ENG_DEC ? DEC_BN : MOE_BN,
+    k_route<<<1, 1024, 4 * E * sizeof(int), side->s>>>(eidx, ewt, P, E, bn,
                                                       (int)w.cap, w.pair_src, w.pair_w, w.items, w.n_items, w.tcerr,
                                                       i8 ? 1 : 0);
     if (!check_cuda(cudaGetLastError(), "route launch")) return 0;
@@ -516,7 +517,8 @@ static int moe_impl(const zz_expert_bank *b, const float *X, const int8_t *xq_in
     prof_mark(st);
     if (i8) {
         if (!launch_moe_i8(fmt, EPI_GATEUP, g, E, w.tcerr, st)) return 0;
-    } else if (!launch_gemm<EPI_GATEUP, MOE_BN, false, true>(fmt, g, dim3((2 * MI) / G_BM, maxit), st)) {
+    } else if (!(wide ? launch_gemm<EPI_GATEUP, MOE_BN_WIDE, false, true>(fmt, g, dim3((2 * MI) / G_BM, maxit), st)
+                      : launch_gemm<EPI_GATEUP, MOE_BN, false, true>(fmt, g, dim3((2 * MI) / G_BM, maxit), st))) {
         return 0;
     }
     prof_mark(st);
@@ -531,7 +533,8 @@ static int moe_impl(const zz_expert_bank *b, const float *X, const int8_t *xq_in
     d.out = OUT; d.pair_w = w.pair_w; d.pair_src = w.pair_src; d.K = K;
     d.xg8 = w.hq; d.xsT = w.hsT; d.ldT = (int)w.ldT; d.rows_cap = (int)w.cap;
     int ok = i8 ? launch_moe_i8(fmt, EPI_DOWN, d, E, w.tcerr, st)
-                : launch_gemm<EPI_DOWN, MOE_BN, false, true>(fmt, d, dim3((D + G_BM - 1) / G_BM, maxit), st);
+           : wide ? launch_gemm<EPI_DOWN, MOE_BN_WIDE, false, true>(fmt, d, dim3((D + G_BM - 1) / G_BM, maxit), st)
+                  : launch_gemm<EPI_DOWN, MOE_BN, false, true>(fmt, d, dim3((D + G_BM - 1) / G_BM, maxit), st);
     prof_mark(st);
     return ok;
 }
