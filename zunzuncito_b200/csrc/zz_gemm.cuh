@@ -618,11 +618,10 @@ __device__ __forceinline__ void gemm_item(const GemmArgs &a, int item_idx) {
 // grid capped below the worst-case item count then launches no CTA that finds no item;
 // the loop costs a few registers, so exact grids use the plain form).
 template <int FMT, int BN, int EPI, bool B_HALF, bool S8 = false, bool STRIDE = false>
-// (4 CTAs per SM at BN <= 32: the int8 path fits 64 registers and 33 KB of shared memory)
-#ifndef ZZ_WIDE_MINB
-#define ZZ_WIDE_MINB 3
-#endif
-__global__ void __launch_bounds__(G_THREADS, BN <= 32 ? 4 : ZZ_WIDE_MINB) k_gemm(GemmArgs a) {
+// CTAs per SM the register budget targets (measured best): 3 for the 32-row gate/up GEMM
+// (78 registers, no spills), 4 for the 32-row down GEMM (64), 3 for 64-row items and the
+// dense matmul
+__global__ void __launch_bounds__(G_THREADS, BN <= 32 ? (EPI == EPI_GATEUP ? 3 : 4) : 3) k_gemm(GemmArgs a) {
     const int n = a.n_items ? *a.n_items : (int)gridDim.y;
     if constexpr (!STRIDE) {
         if ((int)blockIdx.y < n) gemm_item<FMT, BN, EPI, B_HALF, S8>(a, blockIdx.y);
