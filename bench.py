@@ -253,14 +253,15 @@ def graph_timed(torch, fn, steps, warmup):
 
 
 # ----------------------------------------------------------------------------- CPU
-def cpu_baseline_moe(host_blobs, S, seed):
+def cpu_baseline_moe(host_blobs, S, seed, spare=0):
     """The reference's own gemma4.c expert_apply over the batch union (oracle/_ref),
-    all host threads, one layer of the same workload."""
+    all host threads but `spare` (left to the other ranks' processes, which poll while
+    rank 0 samples), one layer of the same workload."""
     import oracle
     from zunzuncito_b200 import synth
     if oracle.reference_available():
         lib, kind = oracle.Reference(), "reference"
-        lib.set_threads(os.cpu_count())
+        lib.set_threads(max(1, os.cpu_count() - spare))
         cores = lib.max_threads()
     else:
         lib, kind, cores = oracle.Oracle(), "port", 1
@@ -334,8 +335,14 @@ def main():
         return
     import torch
     if world > 1:
+        import zunzuncito_b200 as zz
         from zunzuncito_b200 import ep
-        ep.bench_main(a, rank, world, ClockSampler)
+        cpu_fn = None
+        if not a.no_cpu:
+            # the same CPU sample as the one-GPU line: layer 0 of the 128-expert stack
+            cpu_fn = lambda: cpu_baseline_moe(make_stack(zz, torch, 1, seed=1234, keep_host_layer0=True)[1],
+                                               a.tokens, seed=11, spare=world)
+        ep.bench_main(a, rank, world, ClockSampler, cpu_baseline_fn=cpu_fn)
         return
     import zunzuncito_b200 as zz
     from zunzuncito_b200 import synth

@@ -51,7 +51,7 @@ def _exchange_torch(xq, xs, eidx, ewt, world, per, group):
             recv[:, D + 4 * nb + 4 * K:].contiguous().view(torch.float32))
 
 
-def ep_moe_layer(xq, xs, eidx, ewt, n_experts, local_ffn, group=None):
+def ep_moe_layer(xq, xs, eidx, ewt, n_experts, local_ffn, group=None, events=None):
     """One expert-parallel MoE layer on this rank's tokens.
 
     xq [S, D] int8, xs [S, D/32] f32: this rank's quantized tokens; eidx [S, K] int32
@@ -62,7 +62,10 @@ def ep_moe_layer(xq, xs, eidx, ewt, n_experts, local_ffn, group=None):
     Static exchange: token s bound for rank d always travels in slot (d, s), with the
     routing entries that are not d's experts set to -1, so both all-to-alls use equal
     splits and nothing waits on the host (no size exchange, graph-capturable). A slot
-    whose token routes nothing to d carries only -1 ids and comes back as zeros."""
+    whose token routes nothing to d carries only -1 ids and comes back as zeros.
+
+    events (GPU ranks, optional): a list that receives four CUDA events recorded around
+    the dispatch and the combine collectives, for timing the exchange."""
     world = dist.get_world_size(group)
     dev = xq.device
     S, D = xq.shape
@@ -75,7 +78,13 @@ def ep_moe_layer(xq, xs, eidx, ewt, n_experts, local_ffn, group=None):
         import zunzuncito_b200 as zz
         payload = zz.ep_pack(xq, xs.contiguous(), eidx.to(torch.int32).contiguous(), ewt.contiguous(), world, per)
         recv = torch.empty_like(payload)
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)] if events is not None else None
+        if ev:
+            ev[0].record()
         dist.all_to_all_single(recv.view(world, -1), payload.view(world, -1), group=group)
+        if ev:
+            ev[1].record()
+            events.extend(ev)
         r_xq, r_xs, r_e, r_w = zz.ep_unpack(recv, D, K)
     else:
         r_xq, r_xs, r_e, r_w = _exchange_torch(xq, xs, eidx, ewt, world, per, group)
@@ -84,7 +93,11 @@ def ep_moe_layer(xq, xs, eidx, ewt, n_experts, local_ffn, group=None):
     # reduce-scatter of the slot-major partial rows (summed inside the collective)
     if dev.type == "cuda":
         out = torch.empty((S, D), dtype=part.dtype, device=dev)
+        if events is not None:
+            events[-2].record()
         dist.reduce_scatter_tensor(out, part, group=group)
+        if events is not None:
+            events[-1].record()
         return out
     back = torch.empty_like(part)
     dist.all_to_all_single(back.view(world, -1), part.view(world, -1), group=group)
@@ -92,7 +105,7 @@ def ep_moe_layer(xq, xs, eidx, ewt, n_experts, local_ffn, group=None):
 
 
 # ----------------------------------------------------------------------------- bench
-def bench_main(a, rank, world, clock_sampler=None):
+def bench_main(a, rank, world, clock_sampler=None, cpu_baseline_fn=None):
     """bench.py under torchrun: weak scaling, each rank S tokens and E/G experts per
     layer of the 30-layer Gemma-4 stack; time = max over ranks of the device time."""
     import json
@@ -158,6 +171,24 @@ def bench_main(a, rank, world, clock_sampler=None):
     dist.all_reduce(ms, op=dist.ReduceOp.MAX)
     dist.barrier()
     ms = float(ms.item())
+    # the exchange alone: one more step with events around each layer's two collectives,
+    # the per-layer time as the max over ranks; bytes that cross NVLink per rank and layer:
+    # the dispatch rows bound for the other ranks and the reduce-scatter's (world-1)/world
+    # share of the slot-major f32 partial rows
+    evs = []
+    for l in range(L):
+        xq, xs, _ = zz.quant_act(X)
+        ffn = lambda q, s, e, w, b=banks[l]: zz.moe_ffn_q8(b, q, s, e, w, zz.ZZ_ACT_GEGLU_TANH)
+        ep_moe_layer(xq, xs, eidx[l], ewt[l], E, ffn, events=evs)
+    torch.cuda.synchronize()
+    xms = sum(evs[i].elapsed_time(evs[i + 1]) + evs[i + 2].elapsed_time(evs[i + 3]) for i in range(0, len(evs), 4))
+    xms = torch.tensor([xms / L], device="cuda")
+    dist.all_reduce(xms, op=dist.ReduceOp.MAX)
+    xms = float(xms.item())
+    row_bytes = zz.lib.zz_ep_row_bytes(D, K)
+    xbytes = (world - 1) * S * row_bytes + (world - 1) * S * D * 4
+    cpu = cpu_baseline_fn() if (rank == 0 and cpu_baseline_fn is not None) else None
+    dist.barrier()
     # e2e: the same layers through the public API with this rank's tokens and routing
     # copied in from pinned host memory and each layer's output copied back
     Xh = torch.from_numpy(synth.gaussian(7 + rank, (S, D))).pin_memory()
@@ -229,6 +260,13 @@ def bench_main(a, rank, world, clock_sampler=None):
                 "e2e": {"value": S * world * L / (ems / 1e3), "unit": "token-layers/s",
                         "h2d_bytes_per_step": world * L * (S * D * 4 + S * K * 8),
                         "d2h_bytes_per_step": world * L * S * D * 4},
-                "gpu_launches": a.steps * L * 6}  # quant, pack, unpack, route, gate/up, down
+                "gpu_launches": a.steps * L * 6,  # quant, pack, unpack, route, gate/up, down
+                "roofline": {"kernel": "NCCL all-to-all dispatch + reduce-scatter combine, per layer",
+                             "bound": "nvlink", "achieved": xbytes / (xms / 1e3) / 1e9, "peak": 770.0,
+                             "unit": "GB/s", "frac": xbytes / (xms / 1e3) / 1e9 / 770.0,
+                             "peak_source": "measured NVLink peer copy per direction on this pool (profiling recipe)",
+                             "traffic": None, "bytes_per_layer_per_rank": xbytes,
+                             "exchange_ms_per_layer": xms, "layer_ms": ms / L},
+                "cpu_baseline": cpu}
         print(json.dumps(line), flush=True)
     dist.destroy_process_group()
