@@ -474,7 +474,7 @@ static int moe_impl(const zz_expert_bank *b, const float *X, const int8_t *xq_in
         xs = w.xs;
     } else {
         if (!check_cuda(cudaMemsetAsync(OUT, 0, (size_t)S * D * 4, st), "memset OUT")) return 0;
-        if (fmt == GPU_FMT_TQ2) k_rows_sx<<<(S + 127) / 128, 128, 0, st>>>(xq, xs, S, D, w.xsx);
+        if (fmt == GPU_FMT_TQ2) k_rows_sx<<<(S + 7) / 8, 256, 0, st>>>(xq, xs, S, D, w.xsx);
     }
     if (!check_cuda(cudaStreamWaitEvent(st, side->join, 0), "join wait")) return 0;
     if (i8) {

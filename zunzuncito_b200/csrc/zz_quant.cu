@@ -94,25 +94,37 @@ __global__ void __launch_bounds__(128) k_quant_act_blk(const float *__restrict__
     }
 }
 
-// tq2 offset total of quantized rows: Sx = (float) sum_b (double)sx[b] * sum_j xq,
-// summed serially in block order (tq2.h:103-107); one thread per row
+// tq2 offset total of quantized rows: Sx = (float) sum_b (double)sx[b] * sum_j xq, summed
+// serially in block order (tq2.h:103-107). One warp per row: lane l forms the integer sums
+// of blocks l, l+32, ...; lane 0 then adds the double products in block order.
 __global__ void k_rows_sx(const int8_t *__restrict__ xq, const float *__restrict__ xs, int S, int I,
                           float *__restrict__ xsx) {
-    int r = blockIdx.x * blockDim.x + threadIdx.x;
+    const int r = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5), lane = threadIdx.x & 31;
     if (r >= S) return;
     const int nb = I / 32;
     double tot = 0;
-    for (int b = 0; b < nb; b++) {
-        const char4 *q = reinterpret_cast<const char4 *>(xq + (size_t)r * I + (size_t)b * 32);
+    for (int b0 = 0; b0 < nb; b0 += 32) {
+        const int b = b0 + lane;
         int s = 0;
+        double prod = 0;
+        if (b < nb) {
+            const uint4 *q = reinterpret_cast<const uint4 *>(xq + (size_t)r * I + (size_t)b * 32);
 #pragma unroll
-        for (int i = 0; i < 8; i++) {
-            char4 c = q[i];
-            s += c.x + c.y + c.z + c.w;
+            for (int h = 0; h < 2; h++) {
+                const uint4 v = q[h];
+                const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+                for (int k = 0; k < 4; k++) s = __dp4a((int)w[k], 0x01010101, s);
+            }
+            prod = (double)xs[(size_t)r * nb + b] * (double)s;
         }
-        tot += (double)xs[(size_t)r * nb + b] * (double)s;
+        const int n = nb - b0 < 32 ? nb - b0 : 32;
+        for (int k = 0; k < n; k++) {
+            const double p = __shfl_sync(0xffffffffu, prod, k);
+            tot += p;
+        }
     }
-    xsx[r] = (float)tot;
+    if (lane == 0) xsx[r] = (float)tot;
 }
 
 // ---------------------------------------------------------------- weight quantizers
@@ -344,7 +356,7 @@ int launch_quant_act(const float *x, int S, int I, int8_t *xq, float *sx, float 
     }
     if (!check_cuda(cudaGetLastError(), "quant_act launch")) return 0;
     if (sxtot) {
-        k_rows_sx<<<(S + 127) / 128, 128, 0, st>>>(xq, sx, S, I, sxtot);
+        k_rows_sx<<<(S + 7) / 8, 256, 0, st>>>(xq, sx, S, I, sxtot);
         if (!check_cuda(cudaGetLastError(), "rows_sx launch")) return 0;
     }
     return 1;
