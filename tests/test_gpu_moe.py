@@ -9,6 +9,7 @@ Parity is checked stage by stage, as the survey of the path defines it:
 At the full Gemma-4 layer shape the same checks run on a sample of pairs, plus the
 size-independent properties (linearity in the router weights, token permutation)."""
 import ctypes
+import os
 
 import numpy as np
 import pytest
@@ -22,6 +23,16 @@ pytestmark = pytest.mark.gpu
 KINDS = {0: (zz.GPU_FMT_Q40, zz.ZZ_ACT_GEGLU_TANH), 1: (zz.GPU_FMT_Q40, zz.ZZ_ACT_SWIGLU),
          2: (zz.GPU_FMT_Q80, zz.ZZ_ACT_SWIGLU), 3: (zz.GPU_FMT_TQ2, zz.ZZ_ACT_SWIGLU_CLAMP)}
 CLAMP = 7.0
+
+
+def hs_rtol():
+    """relative tolerance of the requantized hidden scales (amax / 127 of h). The int8
+    engines carry each 32-block sum exactly, so h differs from the oracle's only by fp32
+    summation order (1e-5). The folded-scale fp16 engine (h3) also has the tensor core's
+    truncating f32 adds inside each chunk of 16 K steps (measured up to 8e-6 at the
+    Gemma-4 shape), so its scales are held to 2e-5; the layer output stays within the
+    1e-4 of the spec either way."""
+    return 2e-5 if os.environ.get("ZZ_MOE_KERNEL") == "h3" else 1e-5
 
 
 @pytest.fixture(scope="module", autouse=True)
@@ -105,7 +116,7 @@ def check_pairs(orc, kind, blobs, X, eidx, ewt, out_gpu, bank, pairs=None):
             n_flip += int(np.count_nonzero(diff))
             flipped_tok.add(s)
         # scales: amax/127 of h; h itself carries fp32 accumulation-order noise
-        assert np.allclose(hs[r], es[0], rtol=1e-5, atol=0), r
+        assert np.allclose(hs[r], es[0], rtol=hs_rtol(), atol=0), r
     total = len(rows) * MI
     assert n_flip <= max(3, total // 500), (n_flip, total)
     if pairs is None:
@@ -122,7 +133,7 @@ def check_pairs(orc, kind, blobs, X, eidx, ewt, out_gpu, bank, pairs=None):
     return flipped_tok
 
 
-@pytest.fixture(params=["auto", "i8", "mma8", "mma8w"])
+@pytest.fixture(params=["auto", "i8", "mma8", "mma8w", "h3"])
 def engine(request, monkeypatch):
     """every expert engine: auto (the decode GEMV kernels for calls of <= 64 pairs, else the
     int8 mma.sync GEMM with 32- or 64-row items by the rows per expert), and the int8
@@ -239,7 +250,8 @@ def _full_check(orc, kind, blobs_np, bank, X, eidx, ewt, out, max_flip_frac=0.00
     assert np.max(np.abs(diff)) <= 1
     flips = int(np.count_nonzero(diff))
     assert flips <= max(3, max_flip_frac * diff.size), (flips, diff.size)
-    assert np.allclose(hs_g, hs_r, rtol=1e-5, atol=0)
+    print(f"hs max rel dev {float(np.max(np.abs(hs_g / hs_r - 1))):.2e}, mean {float(np.mean(hs_g / hs_r - 1)):.2e}")
+    assert np.allclose(hs_g, hs_r, rtol=hs_rtol(), atol=0)
     want2 = orc.moe_pairs_combine(kind, blobs_np, hq_g, hs_g, eidx, ewt, D, MI)
     assert np.max(np.abs(out - want2)) <= 1e-5 * np.max(np.abs(want2))
     want = orc.moe_pairs_combine(kind, blobs_np, hq_r, hs_r, eidx, ewt, D, MI)

@@ -9,7 +9,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(HERE)
 CSRC = os.path.join(HERE, "csrc")
 LIB = os.path.join(HERE, "libzz_cuda.so")
-SOURCES = ["zz_capi.cu", "zz_quant.cu", "zz_gemv.cu", "zz_moe.cu", "zz_moe_i8.cu", "zz_moe_dec.cu", "zz_ep.cu", "zz_f32act.cu", "zz_route.cu", "zz_loader.cu"]
+SOURCES = ["zz_capi.cu", "zz_quant.cu", "zz_gemv.cu", "zz_moe.cu", "zz_moe_i8.cu", "zz_moe_h3.cu", "zz_moe_dec.cu", "zz_ep.cu", "zz_f32act.cu", "zz_route.cu", "zz_loader.cu"]
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a", "-O3", "-lineinfo", "-std=c++17",
          "-Xcompiler", "-fPIC,-O3", "-Xptxas", "-v" if os.environ.get("ZZ_PTXAS_V") else "-O3",

@@ -92,6 +92,10 @@ struct GemmArgs {
     const float *xsT;        // [I/32][ldT]
     int ldT, rows_cap;
     float *hsT;              // gate/up: transposed hidden scales [O/64][ldT]
+    // folded-scale fp16 engine: B operand planes of the pair rows, hi at xhs and lo at
+    // xhs + rows_cap * I; gate/up also writes the down GEMM's planes to hhs likewise
+    const __half *xhs;
+    __half *hhs;
 };
 
 

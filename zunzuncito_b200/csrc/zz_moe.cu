@@ -39,6 +39,10 @@ __global__ void k_rows_sx(const int8_t *__restrict__ xq, const float *__restrict
                           float *__restrict__ xsx);
 int launch_moe_i8(int fmt, int epi, const GemmArgs &a, int n_groups, int *err, cudaStream_t st);
 bool moe_i8_supported(int fmt, int D, int MI);
+int launch_moe_h3(int epi, const GemmArgs &a, int *err, cudaStream_t st);
+int launch_split_rows(const int *pair_src, int K, const int8_t *xq, const float *xs, int D, int cap, __half *xhs,
+                      int *err, cudaStream_t st);
+bool moe_h3_supported(int fmt, int D, int MI);
 int launch_moe_dec(int fmt, const GemmArgs &gu, const GemmArgs &dn, int P, float *hbuf, cudaStream_t st);
 
 // Expert engine. Default ("auto"): the small-batch GEMV kernels (zz_moe_dec.cu) when
@@ -47,8 +51,10 @@ int launch_moe_dec(int fmt, const GemmArgs &gu, const GemmArgs &dn, int P, float
 // average at least WIDE_PAIRS_PER_EXPERT rows (prefill: the weight fragments then serve
 // twice the columns; at S=512 top-8 the narrow items are faster). ZZ_MOE_KERNEL=i8
 // selects the int8 tcgen05 engine (zz_moe_i8.cu) where the layer's shape allows it;
-// =mma8 / =mma8w force the narrow / wide mma.sync items. All are exact per block.
-enum { ENG_DEC = 0, ENG_MMA8 = 3, ENG_I8 = 5, ENG_MMA8W = 6 };
+// =mma8 / =mma8w force the narrow / wide mma.sync items; =h3 the folded-scale fp16
+// tcgen05 engine (zz_moe_h3.cu, q4_0 banks). The int8 engines are exact per block; h3
+// carries every product to a relative 2^-21.
+enum { ENG_DEC = 0, ENG_MMA8 = 3, ENG_I8 = 5, ENG_MMA8W = 6, ENG_H3 = 7 };
 constexpr int DEC_MAX_PAIRS = 64, WIDE_PAIRS_PER_EXPERT = 128;
 static int moe_engine(int P, const zz_expert_bank *b) {
     const char *e = getenv("ZZ_MOE_KERNEL");
@@ -56,6 +62,7 @@ static int moe_engine(int P, const zz_expert_bank *b) {
     if (e && !strcmp(e, "mma8")) return ENG_MMA8;
     if (e && !strcmp(e, "mma8w")) return ENG_MMA8W;
     if (e && !strcmp(e, "i8")) return i8_ok ? ENG_I8 : ENG_MMA8;
+    if (e && !strcmp(e, "h3")) return moe_h3_supported(b->fmt, b->hidden, b->inter) ? ENG_H3 : ENG_MMA8;
     // the decode kernels take calls of up to DEC_MAX_PAIRS pairs
     if (P <= DEC_MAX_PAIRS) return ENG_DEC;
     return (long)P >= (long)WIDE_PAIRS_PER_EXPERT * b->n_experts ? ENG_MMA8W : ENG_MMA8;
@@ -250,6 +257,7 @@ struct MoeWs {
     int8_t *xg8; float *xsT, *hsT; size_t cap, ldT;
     WorkItem *items; int *n_items;
     int8_t *hq; float *hs; int *hblk; float *hf;
+    __half *xhs, *hhs;  // h3 engine: fp16 (hi, lo) operand planes of the pair rows
     int *bad;
     int *tcerr;
     size_t total;
@@ -259,7 +267,9 @@ struct MoeWs {
 // plus each expert's padding to ROW_ALIGN rows; per pair row: the gathered int8
 // activation row (D), its block scales transposed (D/32 f32), the requantized hidden
 // row (MI int8 + MI/32 f32 scales, also transposed, + MI/32 int block sums for tq2).
-// The decode engine's f32 hidden rows exist only for calls it takes (S*K <= 64 pairs).
+// The decode engine's f32 hidden rows exist only for calls it takes (S*K <= 64 pairs);
+// the h3 engine's fp16 operand planes (hi and lo of every gathered activation row and
+// requantized hidden row, 4 bytes per element) only for calls it takes.
 static MoeWs moe_layout(const zz_expert_bank *b, int S, int K, uint8_t *base) {
     MoeWs w{};
     const int D = b->hidden, MI = b->inter, E = b->n_experts;
@@ -284,6 +294,9 @@ static MoeWs moe_layout(const zz_expert_bank *b, int S, int K, uint8_t *base) {
     w.hs = (float *)take(cap * (MI / 32) * 4);
     w.hblk = (int *)take(cap * (MI / 32) * 4);
     w.hf = (float *)take(P <= (size_t)DEC_MAX_PAIRS ? cap * MI * 4 : 0);
+    const bool h3 = moe_engine((int)P, b) == ENG_H3;
+    w.xhs = (__half *)take(h3 ? cap * D * 4 : 0);
+    w.hhs = (__half *)take(h3 ? cap * MI * 4 : 0);
     w.bad = (int *)take(4);
     w.tcerr = (int *)take(4);
     w.total = o;
@@ -451,7 +464,7 @@ static int moe_impl(const zz_expert_bank *b, const float *X, const int8_t *xq_in
     }
     prof_mark(st);
     const int eng = moe_engine(P, b);
-    const bool i8 = eng == ENG_I8, wide = eng == ENG_MMA8W;
+    const bool h3 = eng == ENG_H3, i8 = eng == ENG_I8 || h3, wide = eng == ENG_MMA8W;
     const int bn = i8 ? I8_BN : eng == ENG_DEC ? DEC_BN : wide ? MOE_BN_WIDE : MOE_BN;
     const int maxit = P / bn + E + 1;
     const int8_t *xq = xq_in;
@@ -477,7 +490,9 @@ static int moe_impl(const zz_expert_bank *b, const float *X, const int8_t *xq_in
         if (fmt == GPU_FMT_TQ2) k_rows_sx<<<(S + 7) / 8, 256, 0, st>>>(xq, xs, S, D, w.xsx);
     }
     if (!check_cuda(cudaStreamWaitEvent(st, side->join, 0), "join wait")) return 0;
-    if (i8) {
+    if (h3) {
+        if (!launch_split_rows(w.pair_src, K, xq, xs, D, (int)w.cap, w.xhs, w.tcerr, st)) return 0;
+    } else if (i8) {
         k_gather_rows8<<<(unsigned)w.cap, 128, 0, st>>>(w.pair_src, K, xq, xs, D, w.xg8, w.xsT, (int)w.ldT);
         if (!check_cuda(cudaGetLastError(), "gather launch")) return 0;
     }
@@ -515,7 +530,11 @@ static int moe_impl(const zz_expert_bank *b, const float *X, const int8_t *xq_in
     g.pair_src = w.pair_src; g.K = K;
     g.xg8 = w.xg8; g.xsT = w.xsT; g.ldT = (int)w.ldT; g.hsT = w.hsT; g.rows_cap = (int)w.cap;
     prof_mark(st);
-    if (i8) {
+    if (h3) {
+        g.hsT = nullptr;  // the down GEMM reads the fp16 planes instead
+        g.xhs = w.xhs; g.hhs = w.hhs;
+        if (!launch_moe_h3(EPI_GATEUP, g, w.tcerr, st)) return 0;
+    } else if (i8) {
         if (!launch_moe_i8(fmt, EPI_GATEUP, g, E, w.tcerr, st)) return 0;
     } else if (!(wide ? launch_gemm<EPI_GATEUP, MOE_BN_WIDE, false, true>(fmt, g, dim3((2 * MI) / G_BM, maxit), st)
                       : launch_gemm<EPI_GATEUP, MOE_BN, false, true>(fmt, g, dim3((2 * MI) / G_BM, maxit), st))) {
@@ -532,7 +551,9 @@ static int moe_impl(const zz_expert_bank *b, const float *X, const int8_t *xq_in
     d.items = w.items; d.n_items = w.n_items;
     d.out = OUT; d.pair_w = w.pair_w; d.pair_src = w.pair_src; d.K = K;
     d.xg8 = w.hq; d.xsT = w.hsT; d.ldT = (int)w.ldT; d.rows_cap = (int)w.cap;
-    int ok = i8 ? launch_moe_i8(fmt, EPI_DOWN, d, E, w.tcerr, st)
+    d.xhs = w.hhs;
+    int ok = h3 ? launch_moe_h3(EPI_DOWN, d, w.tcerr, st)
+           : i8 ? launch_moe_i8(fmt, EPI_DOWN, d, E, w.tcerr, st)
            : wide ? launch_gemm<EPI_DOWN, MOE_BN_WIDE, false, true>(fmt, d, dim3((D + G_BM - 1) / G_BM, maxit), st)
                   : launch_gemm<EPI_DOWN, MOE_BN, false, true>(fmt, d, dim3((D + G_BM - 1) / G_BM, maxit), st);
     prof_mark(st);

@@ -78,7 +78,7 @@ constexpr int OFF_DX = OFF_RING + RING;
 constexpr int OFF_W = OFF_DX + ND * DX_STAGE;
 constexpr int OFF_CT = OFF_W + NW * W_SLOT;
 constexpr int OFF_BAR = OFF_CT + CT_BYTES;
-constexpr int NBAR = 2 * RC_MAX + 2 * NS + 2 * RB + 2 * ND + 2 * NW + 2 * NGRP;
+constexpr int NBAR = 2 * RC_MAX + 2 * NS + 2 * RB + 2 * ND + 2 * NW + 2 * NGRP + 1;
 constexpr int SMEM = OFF_BAR + NBAR * 8 + 16 + 1024;  // + slack to align the base to 1 KB
 static_assert(SMEM <= 232448, "shared memory");
 constexpr uint32_t BIAS = 0x4B400000u;   // fp32 12582912.0
@@ -122,18 +122,6 @@ __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16
 }
 __device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
-// K-major operand in 128-byte-swizzled atoms (8 rows x 128 bytes, 1024 bytes apart):
-// the layout a SWIZZLE_128B TMA box of 128-byte rows writes. A K = 32 slice at byte
-// offset 32j inside the atom is addressed by advancing the start address.
-__device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t addr) {
-    uint64_t d = 0;
-    d |= (uint64_t)((addr >> 4) & 0x3FFFu);
-    d |= (uint64_t)1 << 16;                 // leading offset: unused for swizzled K-major
-    d |= (uint64_t)(1024 >> 4) << 32;       // 8-row groups 1024 bytes apart
-    d |= (uint64_t)1 << 46;                 // descriptor version for sm_100
-    d |= (uint64_t)2 << 61;                 // layout type: 128-byte swizzle
-    return d;
-}
 // instruction descriptor, kind::i8: s8 A and B (K-major), s32 accumulator, M x N
 __host__ __device__ constexpr uint32_t idesc_i8(int M, int N) {
     return (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
@@ -180,7 +168,7 @@ __device__ __forceinline__ void widen_tq2(uint4 w, int odd, uint4 &lo, uint4 &hi
 // shared state of the CTA's roles
 struct I8Ctx {
     uint8_t *smem;
-    uint64_t *cfull, *cempty, *sfull, *sempty, *bfull, *bempty, *dfull, *dempty, *wfull, *wempty, *tfull, *tempty;
+    uint64_t *cfull, *cempty, *sfull, *sempty, *bfull, *bempty, *dfull, *dempty, *wfull, *wempty, *tfull, *tempty, *drain;
     volatile int *abort_flag;
     uint32_t tbase;
     int nb, nss, MT, T;
@@ -477,7 +465,7 @@ __global__ void __launch_bounds__(i8k::NTHREADS, 1)
     c.bfull = c.sempty + NS; c.bempty = c.bfull + RB;
     c.dfull = c.bempty + RB; c.dempty = c.dfull + ND;
     c.wfull = c.dempty + ND; c.wempty = c.wfull + NW;
-    c.tfull = c.wempty + NW; c.tempty = c.tfull + NGRP;
+    c.tfull = c.wempty + NW; c.tempty = c.tfull + NGRP; c.drain = c.tempty + NGRP;
     uint32_t *tmem_base_smem = reinterpret_cast<uint32_t *>(smem + OFF_BAR + NBAR * 8);
     c.abort_flag = reinterpret_cast<volatile int *>(smem + OFF_BAR + NBAR * 8 + 4);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -497,6 +485,7 @@ __global__ void __launch_bounds__(i8k::NTHREADS, 1)
         for (int i = 0; i < ND; i++) { tc::mbar_init(&c.dfull[i], 1); tc::mbar_init(&c.dempty[i], 8); }
         for (int i = 0; i < NW; i++) { tc::mbar_init(&c.wfull[i], 1); tc::mbar_init(&c.wempty[i], 8); }
         for (int i = 0; i < NGRP; i++) { tc::mbar_init(&c.tfull[i], 1); tc::mbar_init(&c.tempty[i], 8); }
+        tc::mbar_init(c.drain, 1);
         *c.abort_flag = 0;
         tc::mbar_init_fence();
     }
@@ -529,6 +518,12 @@ __global__ void __launch_bounds__(i8k::NTHREADS, 1)
                 tile(t, it, m0);
                 const int y = it.group * a.O + m0;
                 for (int ss = 0; ss < c.nss; ss++, g++) {
+                    // both slots are free before either copy is issued, so an abort leaves
+                    // copies in flight only for stages below g
+                    if (HAS_DW) {
+                        const uint32_t wu = g / NW;
+                        if (wu && !tc::mbar_wait(&c.wempty[g % NW], (wu - 1) & 1, c.abort_flag, err, 16)) { ok = false; break; }
+                    }
                     if (DIRECT) {
                         const int st = g % NS;
                         const uint32_t u = g / NS;
@@ -546,19 +541,17 @@ __global__ void __launch_bounds__(i8k::NTHREADS, 1)
                     }
                     if (HAS_DW) {
                         const int ws = g % NW;
-                        const uint32_t wu = g / NW;
-                        if (wu && !tc::mbar_wait(&c.wempty[ws], (wu - 1) & 1, c.abort_flag, err, 16)) { ok = false; break; }
                         tc::mbar_arrive_tx(&c.wfull[ws], W_SLOT);
                         tc::tma_load_3d(smem + OFF_W + ws * W_SLOT, &scale_map, ss * KB, m0, it.group, &c.wfull[ws]);
                     }
                 }
             }
             // wait for the last copies to land before the CTA may exit
-            if (g) {
-                if (DIRECT) tc::mbar_wait(&c.sfull[(g - 1) % NS], ((g - 1) / NS) & 1, c.abort_flag, err, 2);
-                else tc::mbar_wait(&c.cfull[(g - 1) % RC], ((g - 1) / RC) & 1, c.abort_flag, err, 2);
-                if (HAS_DW) tc::mbar_wait(&c.wfull[(g - 1) % NW], ((g - 1) / NW) & 1, c.abort_flag, err, 17);
-            }
+            // (bounded by time only: after an abort the copies still land in this CTA's memory)
+            // (each slot's latest use)
+            for (uint32_t k = g > (uint32_t)NS ? g - NS : 0; DIRECT && k < g; k++) tc::mbar_drain(&c.sfull[k % NS], (k / NS) & 1);
+            for (uint32_t k = g > (uint32_t)RC ? g - RC : 0; !DIRECT && k < g; k++) tc::mbar_drain(&c.cfull[k % RC], (k / RC) & 1);
+            for (uint32_t k = g > (uint32_t)NW ? g - NW : 0; HAS_DW && k < g; k++) tc::mbar_drain(&c.wfull[k % NW], (k / NW) & 1);
         }
     } else if (warp == 13) {
         if (lane == 0) {
@@ -575,6 +568,7 @@ __global__ void __launch_bounds__(i8k::NTHREADS, 1)
                     const int nbl = min(KB, c.nb - ss * KB);
                     const int nbox = (nbl + 3) / 4;
                     if (g >= RB && !tc::mbar_wait(&c.bempty[bs], ((g / RB) - 1) & 1, c.abort_flag, err, 3)) { ok = false; break; }
+                    if (g >= ND && !tc::mbar_wait(&c.dempty[ds], ((g / ND) - 1) & 1, c.abort_flag, err, 11)) { ok = false; break; }
                     tc::mbar_arrive_tx(&c.bfull[bs], box * nbox);
                     uint8_t *dst = smem + OFF_B + bs * B_STAGE;
                     for (int bx = 0; bx < nbox; bx++) {
@@ -587,17 +581,14 @@ __global__ void __launch_bounds__(i8k::NTHREADS, 1)
                             default: tc::tma_load_2d(dst + bx * box, &bmaps.m[3], x, it.row0, &c.bfull[bs]); break;
                         }
                     }
-                    if (g >= ND && !tc::mbar_wait(&c.dempty[ds], ((g / ND) - 1) & 1, c.abort_flag, err, 11)) { ok = false; break; }
                     tc::mbar_arrive_tx(&c.dfull[ds], (uint32_t)(nbl * np2 * 4));
                     for (int jj = 0; jj < nbl; jj++)
                         tc::bulk_load(smem + OFF_DX + ds * DX_STAGE + jj * BN * 4,
                                       a.xsT + (size_t)(ss * KB + jj) * a.ldT + it.row0, (uint32_t)(np2 * 4), &c.dfull[ds]);
                 }
             }
-            if (g) {
-                tc::mbar_wait(&c.bfull[(g - 1) % RB], ((g - 1) / RB) & 1, c.abort_flag, err, 12);
-                tc::mbar_wait(&c.dfull[(g - 1) % ND], ((g - 1) / ND) & 1, c.abort_flag, err, 13);
-            }
+            for (uint32_t k = g > (uint32_t)RB ? g - RB : 0; k < g; k++) tc::mbar_drain(&c.bfull[k % RB], (k / RB) & 1);
+            for (uint32_t k = g > (uint32_t)ND ? g - ND : 0; k < g; k++) tc::mbar_drain(&c.dfull[k % ND], (k / ND) & 1);
         }
     } else if (warp == 14) {
         // ---------------- MMA issue ----------------
@@ -626,8 +617,8 @@ __global__ void __launch_bounds__(i8k::NTHREADS, 1)
                             break;
                         }
                         tc::tc_fence_after();
-                        const uint64_t ad = smem_desc_sw128(sa + (jb >> 2) * A_ATOM + (jb & 3) * 32);
-                        const uint64_t bd = smem_desc_sw128(sb + (jb >> 2) * box + (jb & 3) * 32);
+                        const uint64_t ad = tc::smem_desc_sw128(sa + (jb >> 2) * A_ATOM + (jb & 3) * 32);
+                        const uint64_t bd = tc::smem_desc_sw128(sb + (jb >> 2) * box + (jb & 3) * 32);
                         mma_i8_acc(c.tbase + (uint32_t)(p * BN + sub * cw), ad, bd, idesc);
                         if (sub == G - 1 || jb == nbl - 1) {
                             tc::mma_commit(&c.tfull[p]);
@@ -639,7 +630,9 @@ __global__ void __launch_bounds__(i8k::NTHREADS, 1)
                     tc::mma_commit(&c.bempty[bs]);  // B stage likewise
                 }
             }
-            if (gg) tc::mbar_wait(&c.tfull[(gg - 1) % NGRP], ((gg - 1) / NGRP) & 1, c.abort_flag, err, 7);
+            // every MMA issued has completed before TMEM may be freed
+            tc::mma_commit(&c.drain[0]);
+            tc::mbar_drain(&c.drain[0], 0);
         }
     }
     } else if (warp >= 8) {

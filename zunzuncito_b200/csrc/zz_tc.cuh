@@ -109,6 +109,44 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, volati
     return false;
 }
 
+// bounded wait without back-off, for the roles on a pipeline's critical path (the MMA
+// issuer, copy issuers, operand producers): the phase change is seen within one try
+// instead of after a sleep. The clock and the abort flag are read every 256 tries.
+__device__ __forceinline__ bool mbar_wait_spin(uint64_t *bar, uint32_t parity, volatile int *abort, int *err,
+                                               int code) {
+#ifdef ZZ_TC_PROF
+    const long long t0 = clock64();
+    struct Acc {
+        long long t0;
+        int code;
+        __device__ ~Acc() {
+            if (blockIdx.x == 0 && (threadIdx.x & 31) == 0)
+                atomicAdd(&g_tc_prof[code], (unsigned long long)(clock64() - t0));
+        }
+    } acc_{t0, code};
+#endif
+    if (mbar_try(bar, parity)) return true;
+    const unsigned long long w0 = global_ns();
+    for (;;) {
+        for (int i = 0; i < 256; i++)
+            if (mbar_try(bar, parity)) return true;
+        if (*abort) return false;
+        if (global_ns() - w0 > WAIT_LIMIT_NS) break;
+    }
+    *abort = 1;
+    atomicCAS(err, 0, code);
+    return false;
+}
+
+// wait, bounded by time only (not by the abort flag), for copies or MMAs this thread has
+// issued: a CTA must not exit, nor free TMEM, while they may still write its memory
+__device__ __forceinline__ bool mbar_drain(uint64_t *bar, uint32_t parity) {
+    const unsigned long long w0 = global_ns();
+    while (!mbar_try(bar, parity))
+        if (global_ns() - w0 > WAIT_LIMIT_NS) return false;
+    return true;
+}
+
 __device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
@@ -170,6 +208,18 @@ __device__ __forceinline__ uint64_t smem_desc_sw64(uint32_t addr, uint32_t sbo) 
     d |= (uint64_t)4 << 61;  // layout type: 64-byte swizzle
     return d;
 }
+// K-major operand in 128-byte-swizzled atoms (8 rows x 128 bytes, 1024 bytes apart):
+// the layout a SWIZZLE_128B TMA box of 128-byte rows writes. A 32-byte K slice (K = 32 int8 or K = 16 fp16) at byte
+// offset 32j inside the atom is addressed by advancing the start address.
+__device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t addr) {
+    uint64_t d = 0;
+    d |= (uint64_t)((addr >> 4) & 0x3FFFu);
+    d |= (uint64_t)1 << 16;                 // leading offset: unused for swizzled K-major
+    d |= (uint64_t)(1024 >> 4) << 32;       // 8-row groups 1024 bytes apart
+    d |= (uint64_t)1 << 46;                 // descriptor version for sm_100
+    d |= (uint64_t)2 << 61;                 // layout type: 128-byte swizzle
+    return d;
+}
 // Instruction descriptor, kind::f16: f16 A and B (K-major), f32 accumulator, M x N
 __host__ __device__ constexpr uint32_t idesc_f16(int M, int N) {
     return (1u << 4) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
@@ -183,6 +233,27 @@ __device__ __forceinline__ void mma_f16_ss(uint32_t tmem_d, uint64_t adesc, uint
         "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
         : "memory");
 }
+// D[tmem] (+)= A[tmem] * B[smem]^T: A is M lanes x K columns of packed fp16 pairs (the
+// 32-bit column c of lane m holds A[m][2c] in its low half and A[m][2c + 1] in its high
+// half), issued by one thread
+__device__ __forceinline__ void mma_f16_ts(uint32_t tmem_d, uint32_t tmem_a, uint64_t bdesc, uint32_t idesc,
+                                           uint32_t accumulate) {
+    asm volatile(
+        "{.reg .pred p; setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;}" ::"r"(tmem_d),
+        "r"(tmem_a), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+// 32 lanes x 16 consecutive 32-bit columns from 16 registers per thread
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t *r) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(
+            taddr),
+        "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
+        "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+        : "memory");
+}
+__device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 // the mbarrier fires when all previously issued tcgen05 ops of this thread complete
 __device__ __forceinline__ void mma_commit(uint64_t *bar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
@@ -197,6 +268,14 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
           "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
           "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
           "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr));
+}
+// 32 lanes x 16 consecutive 32-bit columns -> 16 registers per thread
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t *r) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
         : "r"(taddr));
 }
 // 16 lanes x 4 x 256 bits: thread t gets, for i = 0..3, lane (t/4) columns 8i + 2(t%4) + {0,1}
