@@ -203,14 +203,19 @@ __global__ void __launch_bounds__(h3k::NTHREADS, 1)
                     const int nk = 2 * min(2, nb - 2 * ss);  // 16-wide K steps with data
                     const uint32_t ah = sA + sa * STAGE, bh = sB + sb * STAGE;
                     const uint32_t dm = tbase + (uint32_t)(db * SBUF), dc = dm + (uint32_t)np2;
+                    // a 32-byte K step advances the descriptors' start address field by 2
+                    const uint64_t ahd = tc::smem_desc_sw128(ah), ald = tc::smem_desc_sw128(ah + PART);
+                    const uint64_t bd = tc::smem_desc_sw128(bh);
+                    TC_PROF_T(p_mma);
                     for (int kk = 0; kk < nk; kk++) {
-                        const uint64_t ahd = tc::smem_desc_sw128(ah + kk * 32), ald = tc::smem_desc_sw128(ah + PART + kk * 32);
-                        const uint64_t bd = tc::smem_desc_sw128(bh + kk * 32);
-                        tc::mma_f16_ss(dm, ahd, bd, idesc2, !(first && kk == 0));  // A_hi B_hi | A_hi B_lo
-                        tc::mma_f16_ss(dc, ald, bd, idesc1, 1);                    // + A_lo B_hi (cross)
+                        tc::mma_f16_ss(dm, ahd + 2 * kk, bd + 2 * kk, idesc2, !(first && kk == 0));  // A_hi B_hi | A_hi B_lo
+                        tc::mma_f16_ss(dc, ald + 2 * kk, bd + 2 * kk, idesc1, 1);                    // + A_lo B_hi (cross)
                     }
+                    TC_PROF_ADD(50, p_mma);
+                    TC_PROF_T(p_cmt);
                     tc::mma_commit(&aempty[sa]);  // operand stages free once these MMAs complete
                     tc::mma_commit(&bempty[sb]);
+                    TC_PROF_ADD(51, p_cmt);
                     if (last) {
                         tc::mma_commit(&sfull[db]);  // the chunk's sums are ready
                         gc++;

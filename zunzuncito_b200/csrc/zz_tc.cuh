@@ -109,9 +109,20 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, volati
     return false;
 }
 
+// non-blocking probe of the phase with the given parity (mbarrier.test_wait: no
+// suspension window, so a completed phase costs one shared-memory round trip)
+__device__ __forceinline__ bool mbar_test(uint64_t *bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{.reg .pred p; mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p;}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
 // bounded wait without back-off, for the roles on a pipeline's critical path (the MMA
-// issuer, copy issuers, operand producers): the phase change is seen within one try
-// instead of after a sleep. The clock and the abort flag are read every 256 tries.
+// issuer, copy issuers, operand producers): the phase change is seen within one probe
+// instead of after a sleep. The clock and the abort flag are read every 256 probes.
 __device__ __forceinline__ bool mbar_wait_spin(uint64_t *bar, uint32_t parity, volatile int *abort, int *err,
                                                int code) {
 #ifdef ZZ_TC_PROF
@@ -125,11 +136,11 @@ __device__ __forceinline__ bool mbar_wait_spin(uint64_t *bar, uint32_t parity, v
         }
     } acc_{t0, code};
 #endif
-    if (mbar_try(bar, parity)) return true;
+    if (mbar_test(bar, parity)) return true;
     const unsigned long long w0 = global_ns();
     for (;;) {
         for (int i = 0; i < 256; i++)
-            if (mbar_try(bar, parity)) return true;
+            if (mbar_test(bar, parity)) return true;
         if (*abort) return false;
         if (global_ns() - w0 > WAIT_LIMIT_NS) break;
     }

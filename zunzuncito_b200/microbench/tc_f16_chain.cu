@@ -1,0 +1,105 @@
+// tc_f16_chain.cu -- how fast one thread's chain of tcgen05.mma kind::f16 instructions
+// (M = 128, K = 16, A and B from shared memory) runs, by accumulator pattern.
+//
+// The folded-scale expert engine (zz_moe_h3.cu) issues per 16-wide K step one MMA of
+// N = 2 np2 columns (main | cross sums) and one of N = np2 columns into the cross half,
+// so consecutive MMAs write overlapping but different TMEM column ranges. This program
+// times, one CTA per SM and 4096 MMAs per CTA, the cycles per MMA (max over SMs) of:
+//   same N        every MMA into the same columns (a GEMM's K loop)
+//   overlap       the engine's pattern: N = 2n into [0, 2n), then N = n into [n, 2n)
+//   disjoint      N = 2n into [0, 2n), then N = n into [2n, 3n)
+// against the arithmetic alone (M N K 2 / 8192 flops per SM cycle). Every wait is
+// bounded (100 ms of %globaltimer).
+//
+// build: nvcc -gencode arch=compute_100a,code=sm_100a -O3 -std=c++17 \
+//            -I zunzuncito_b200/csrc -I include zunzuncito_b200/microbench/tc_f16_chain.cu -o tc_f16_chain
+#include <cstdint>
+#include <cstdio>
+#include <cuda_runtime.h>
+#include "zz_common.cuh"
+#include "zz_tc.cuh"
+using namespace zz;
+
+namespace {
+constexpr int NMMA = 4096;
+struct Case {
+    const char *name;
+    int n1, off1, n2, off2;  // first MMA: N, column offset; second (n2 = 0: none)
+};
+__global__ void __launch_bounds__(128, 1) k_chain(Case c, unsigned long long *cycles, int *err) {
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+    uint64_t *bar = reinterpret_cast<uint64_t *>(smem + 3 * 32768);
+    uint32_t *tslot = reinterpret_cast<uint32_t *>(bar + 1);
+    const int tid = threadIdx.x, warp = tid >> 5;
+    // operands: zeros (the timing does not depend on the values)
+    for (int i = tid; i < 3 * 32768 / 16; i += 128) reinterpret_cast<uint4 *>(smem)[i] = make_uint4(0, 0, 0, 0);
+    if (tid == 0) { tc::mbar_init(bar, 1); tc::mbar_init_fence(); }
+    tc::fence_proxy_async();
+    if (warp == 0) tc::tmem_alloc(tslot, 512);
+    tc::tc_fence_before();
+    __syncthreads();
+    tc::tc_fence_after();
+    const uint32_t tbase = *tslot;
+    if (tid == 0) {
+        const uint32_t sa = tc::smem_u32(smem), sb = tc::smem_u32(smem + 32768);
+        const uint64_t ad = tc::smem_desc_sw128(sa), bd = tc::smem_desc_sw128(sb);
+        const uint32_t id1 = tc::idesc_f16(128, c.n1), id2 = c.n2 ? tc::idesc_f16(128, c.n2) : 0;
+        const long long t0 = clock64();
+        for (int i = 0; i < NMMA; i += c.n2 ? 2 : 1) {
+            const int kk = (i >> 1) & 3;
+            tc::mma_f16_ss(tbase + c.off1, ad + 2 * kk, bd + 2 * kk, id1, i != 0);
+            if (c.n2) tc::mma_f16_ss(tbase + c.off2, ad + 2 * kk, bd + 2 * kk, id2, 1);
+        }
+        tc::mma_commit(bar);
+        const unsigned long long w0 = tc::global_ns();
+        while (!tc::mbar_try(bar, 0))
+            if (tc::global_ns() - w0 > 100000000ull) { atomicExch(err, 1); break; }
+        const long long t1 = clock64();
+        atomicMax(cycles, (unsigned long long)(t1 - t0));
+    }
+    tc::tc_fence_before();
+    __syncthreads();
+    if (warp == 0) {
+        tc::tc_fence_after();
+        tc::tmem_dealloc(tbase, 512);
+    }
+}
+}  // namespace
+
+int main() {
+    int sms = 0;
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, 0);
+    const int smem = 3 * 32768 + 64 + 1024;
+    cudaFuncSetAttribute(k_chain, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    unsigned long long *cyc;
+    int *err;
+    cudaMalloc(&cyc, 8);
+    cudaMalloc(&err, 4);
+    cudaMemset(err, 0, 4);
+    const Case cases[] = {
+        {"same N=256", 256, 0, 0, 0},      {"same N=128", 128, 0, 0, 0},      {"same N=64", 64, 0, 0, 0},
+        {"same N=32", 32, 0, 0, 0},        {"same N=16", 16, 0, 0, 0},
+        {"overlap 256+128", 256, 0, 128, 128}, {"disjoint 256+128", 256, 0, 128, 256},
+        {"overlap 64+32", 64, 0, 32, 32},  {"disjoint 64+32", 64, 0, 32, 64},
+        {"overlap 32+16", 32, 0, 16, 16},  {"disjoint 32+16", 32, 0, 16, 32},
+    };
+    printf("%-20s %10s %10s %8s\n", "case", "cyc/MMA", "arith", "ratio");
+    for (const Case &c : cases) {
+        for (int rep = 0; rep < 2; rep++) {  // the first launch warms up
+            cudaMemset(cyc, 0, 8);
+            k_chain<<<sms, 128, smem>>>(c, cyc, err);
+            cudaDeviceSynchronize();
+        }
+        unsigned long long h = 0;
+        int e = 0;
+        cudaMemcpy(&h, cyc, 8, cudaMemcpyDeviceToHost);
+        cudaMemcpy(&e, err, 4, cudaMemcpyDeviceToHost);
+        const double per = (double)h / NMMA;
+        const double arith = c.n2 ? (128.0 * (c.n1 + c.n2) * 16 * 2 / 8192) / 2 : 128.0 * c.n1 * 16 * 2 / 8192;
+        printf("%-20s %10.1f %10.1f %8.2f%s\n", c.name, per, arith, per / arith, e ? "  (wait ran out)" : "");
+    }
+    const cudaError_t r = cudaGetLastError();
+    printf("status: %s\n", cudaGetErrorString(r));
+    return r != cudaSuccess;
+}
