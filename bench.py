@@ -574,6 +574,20 @@ def sub_benchmarks(zz, torch, synth, stream, banks, hbm_peak):
     res["prefill_4096_layer"] = {"unit": "int8 TOPS", "value": tops, "frac_int8_peak": tops / peak["value"],
                                  "frac_int8_spec_4500": tops / 4500.0,
                                  "ms_per_layer": ms, "tok_per_s": S4 / (ms / 1e3)}
+    # the same layers on the folded-scale tcgen05 engine (opt-in; fp16 tensor-core work is
+    # 3 products per weight-activation pair, reported against the same effective ops)
+    prev = os.environ.get("ZZ_MOE_KERNEL")
+    os.environ["ZZ_MOE_KERNEL"] = "h3"
+    try:
+        ms_h3 = timed(torch, pre, 5, 2, stream) / 2
+    finally:
+        if prev is None:
+            del os.environ["ZZ_MOE_KERNEL"]
+        else:
+            os.environ["ZZ_MOE_KERNEL"] = prev
+    tops_h3 = 2 * S4 * K * MACS_PER_PAIR / (ms_h3 / 1e3) / 1e12
+    res["prefill_4096_layer_h3"] = {"unit": "int8 TOPS", "value": tops_h3, "frac_int8_peak": tops_h3 / peak["value"],
+                                    "ms_per_layer": ms_h3, "engine": "tcgen05 kind::f16, folded block scales"}
     for b in banks[:2]:
         b._ws = None
     res.update(maple_tq2(zz, torch, synth, stream, hbm_peak))
