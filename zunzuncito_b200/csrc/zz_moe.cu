@@ -67,7 +67,7 @@ static int moe_engine(int P, const zz_expert_bank *b) {
     if (P <= DEC_MAX_PAIRS) return ENG_DEC;
     return (long)P >= (long)WIDE_PAIRS_PER_EXPERT * b->n_experts ? ENG_MMA8W : ENG_MMA8;
 }
-constexpr int I8_BN = 128;
+constexpr int I8_BN = 128, H3_BN = 64;
 
 constexpr int MOE_BN = 32, MOE_BN_WIDE = 64;
 constexpr int ROW_ALIGN = 4;
@@ -465,7 +465,7 @@ static int moe_impl(const zz_expert_bank *b, const float *X, const int8_t *xq_in
     prof_mark(st);
     const int eng = moe_engine(P, b);
     const bool h3 = eng == ENG_H3, i8 = eng == ENG_I8 || h3, wide = eng == ENG_MMA8W;
-    const int bn = i8 ? I8_BN : eng == ENG_DEC ? DEC_BN : wide ? MOE_BN_WIDE : MOE_BN;
+    const int bn = h3 ? H3_BN : i8 ? I8_BN : eng == ENG_DEC ? DEC_BN : wide ? MOE_BN_WIDE : MOE_BN;
     const int maxit = P / bn + E + 1;
     const int8_t *xq = xq_in;
     const float *xs = xs_in;

@@ -37,21 +37,24 @@
 //   warps 0-3   epilogue: thread = TMEM lane = weight row; per chunk the f32 sums, at the
 //               tile end through shared memory to the fused GeGLU / SwiGLU + q8_0 requant
 //               (bit-exact with q40_quant_act) or the weighted scatter-add into OUT
-//   warps 4-7   A producers: thread r streams weight row m0 + r (32 code bytes and two
-//               fp16 scales per stage, cp.async DEPTH stages ahead) and writes A_hi and
-//               A_lo in the 128-byte-swizzled K-major layout the MMA reads
-//   warp 8      TMA: the stage's B_hi and B_lo boxes (128 bytes x np2 rows, swizzled)
-//   warp 9      MMA: one thread issues 2 x 4 tcgen05.mma kind::f16 per stage (M = 128,
+//   warps 4-11  A producers, two per TMEM lane quarter: thread r of warp set hb streams
+//               block hb of each stage of weight row m0 + r (16 code bytes and the
+//               fp16 scales, cp.async DEPTH stages ahead) and writes its A_hi and A_lo
+//               columns into TMEM lane r (tcgen05.st)
+//   warp 12     TMA: the stage's B_hi and B_lo boxes (128 bytes x np2 rows, swizzled)
+//   warp 13     MMA: one elected lane issues 2 x 4 tcgen05.mma kind::f16 per stage (M = 128,
 //               N = 2 np2 and np2, K = 16)
 // Every wait is bounded (2 s of %globaltimer); one that runs out sets the kernel's error
 // word and the CTA drains (copies and MMAs in flight, bounded by time only), frees its
 // TMEM and returns.
 //
 // Measured (B200, Gemma-4 layer, 128 q4_0 experts): parity with the oracle at every
-// benched shape, but slower than the int8 mma.sync engine (S = 4096 gate/up 1.72 ms
-// against 1.13 ms): the one MMA-issuing thread needs ~1.9k cycles per stage against the
-// ~770 the eight MMAs' arithmetic takes, and waits a quarter of its time on the chunk
-// hand-off. It stays opt-in (ZZ_MOE_KERNEL=h3).
+// benched shape; S = 4096 layer 2.03 ms against 1.97 for the int8 mma.sync engine with
+// 64-row items, S = 512 0.46 against 0.35 ms. What sets the pace (profiles/, the MMA-chain
+// microbenchmark): the MMA issue sequence must be a fixed, unrolled run per stage (a loop
+// with a run-time trip count costs 3.5x per MMA), operands are issued by a whole warp
+// with one elected lane, and the weight producers' per-stage latency is the remaining
+// bound. It stays opt-in (ZZ_MOE_KERNEL=h3).
 #include <cuda.h>
 #include <cudaTypedefs.h>
 #include "zz_gemm.cuh"
@@ -60,28 +63,30 @@
 namespace zz {
 
 namespace h3k {
-constexpr int NTHREADS = 320;
-constexpr int BN = 128;                 // max routed rows per tile
-constexpr int PART = 128 * 128;         // one operand part: 128 rows x 128 bytes (64 fp16)
-constexpr int NSA = 2, NSB = 3;         // operand stages in shared memory
-constexpr int STAGE = 2 * PART;         // hi, lo
-constexpr int DEPTH = 6;                // A producers: cp.async stages in flight per thread
-constexpr int RA = 128 * 32, RW = 128 * 4;  // raw code / scale bytes per stage
+constexpr int NTHREADS = 448;
+constexpr int BN = 64;                  // max routed rows per tile
+constexpr int PART = BN * 128;          // one B part: 64 rows x 128 bytes (64 fp16)
+constexpr int NS = 4;                   // operand stages: A in TMEM, B in shared memory
+constexpr int B_STAGE = 2 * PART;       // [B_hi; B_lo], np2 rows each
+constexpr int DEPTH = 8;                // A producers: cp.async stages in flight per thread
+constexpr int RA = 128 * 32, RW = 256 * 4;  // raw code / scale bytes per stage
 constexpr int CTX = 33;                 // tile-end exchange: 128 rows x 32 columns, padded
 constexpr int CT_BYTES = 128 * CTX * 4;
-constexpr int OFF_A = 0;                // 1 KB aligned (swizzled operands)
-constexpr int OFF_B = OFF_A + NSA * STAGE;
-constexpr int OFF_RA = OFF_B + NSB * STAGE;
+constexpr int OFF_B = 0;                // 1 KB aligned (swizzled operands)
+constexpr int OFF_RA = OFF_B + NS * B_STAGE;
 constexpr int OFF_RW = OFF_RA + DEPTH * RA;
 constexpr int OFF_CT = OFF_RW + DEPTH * RW;
 constexpr int OFF_BAR = OFF_CT + CT_BYTES;
-constexpr int NBAR = 2 * NSA + 2 * NSB + 2 * 2 + 1;
+constexpr int NBAR = 2 * NS + 2 * 2 + 1;
 constexpr int SMEM = OFF_BAR + NBAR * 8 + 16 + 1024;  // + slack to align the base to 1 KB
 static_assert(SMEM <= 232448, "shared memory");
-// TMEM: two chunk buffers of 256 columns; a chunk's sums are [main (np2) | cross (np2)]
-constexpr int TMEM_COLS = 512, SBUF = 256;
+// TMEM columns: two chunk buffers of 2 BN columns (a chunk's sums are [main (np2) | cross
+// (np2)]), then NS stages of A (64 weights: 32 columns of A_hi pairs, 32 of A_lo pairs)
+constexpr int SBUF = 2 * BN, TM_A = 2 * SBUF, A_COLS = 64;
+constexpr int TMEM_COLS = 512;
+static_assert(TM_A + NS * A_COLS <= TMEM_COLS, "TMEM columns");
 constexpr int CH = 4;                   // stages per TMEM sum (16 K steps of 16)
-constexpr int WARP_TMA = 8, WARP_MMA = 9;
+constexpr int WARP_TMA = 12, WARP_MMA = 13;
 }  // namespace h3k
 
 // fp16 pair -> (hi, lo) with hi = fp16(v * s), lo = fp16(v * s - hi) exactly
@@ -143,12 +148,12 @@ __global__ void __launch_bounds__(256) k_split_rows(const int *__restrict__ pair
 }
 
 struct BMapsH {
-    CUtensorMap hi[4], lo[4];  // 128-byte (64 fp16) boxes of 16, 32, 64, 128 rows
+    CUtensorMap hi[3], lo[3];  // 128-byte (64 fp16) boxes of 16, 32, 64 rows
 };
 
 __device__ __forceinline__ int np2_rows(int count) {
     const int N = (count + 15) & ~15;
-    return N <= 16 ? 16 : N <= 32 ? 32 : N <= 64 ? 64 : 128;
+    return N <= 16 ? 16 : N <= 32 ? 32 : 64;
 }
 
 template <int EPI>
@@ -158,8 +163,10 @@ __global__ void __launch_bounds__(h3k::NTHREADS, 1)
     extern __shared__ __align__(128) uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem + OFF_BAR);
-    uint64_t *afull = bars, *aempty = afull + NSA, *bfull = aempty + NSA, *bempty = bfull + NSB;
-    uint64_t *sfull = bempty + NSB, *sempty = sfull + 2, *drain = sempty + 2;
+    // a stage is full when the 8 producer warps have written A and the B copies have landed
+    // (8 arrivals + the copy thread's arrive with its byte count), empty when its MMAs are done
+    uint64_t *opfull = bars, *opempty = opfull + NS;
+    uint64_t *sfull = opempty + NS, *sempty = sfull + 2, *drain = sempty + 2;
     uint32_t *tmem_base_smem = reinterpret_cast<uint32_t *>(smem + OFF_BAR + NBAR * 8);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + OFF_BAR + NBAR * 8 + 4);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -167,8 +174,7 @@ __global__ void __launch_bounds__(h3k::NTHREADS, 1)
     const int T = *a.n_items * MT;
 
     if (tid == 0) {
-        for (int i = 0; i < NSA; i++) { tc::mbar_init(&afull[i], 4); tc::mbar_init(&aempty[i], 1); }
-        for (int i = 0; i < NSB; i++) { tc::mbar_init(&bfull[i], 1); tc::mbar_init(&bempty[i], 1); }
+        for (int i = 0; i < NS; i++) { tc::mbar_init(&opfull[i], 9); tc::mbar_init(&opempty[i], 1); }
         for (int i = 0; i < 2; i++) { tc::mbar_init(&sfull[i], 1); tc::mbar_init(&sempty[i], 4); }
         tc::mbar_init(drain, 1);
         *abort_flag = 0;
@@ -182,51 +188,51 @@ __global__ void __launch_bounds__(h3k::NTHREADS, 1)
     TC_PROF_T(prof_t0);
 
     if (warp == WARP_MMA) {
-        // ---------------- MMA issue ----------------
-        if (lane == 0) {
-            uint32_t g = 0, gc = 0;
-            bool ok = true;
-            const uint32_t sA = tc::smem_u32(smem + OFF_A), sB = tc::smem_u32(smem + OFF_B);
-            for (int t = blockIdx.x; t < T && ok; t += gridDim.x) {
-                const WorkItem it = a.items[t / MT];
-                const int np2 = np2_rows(it.count);
-                // [B_hi; B_lo] as one operand of 2 np2 rows: main and cross columns together
-                const uint32_t idesc2 = tc::idesc_f16(128, 2 * np2), idesc1 = tc::idesc_f16(128, np2);
-                for (int ss = 0; ss < nss; ss++, g++) {
-                    const int sa = g % NSA, sb = g % NSB, db = gc & 1;
-                    const bool first = ss % CH == 0, last = ss % CH == CH - 1 || ss == nss - 1;
-                    if (!tc::mbar_wait_spin(&afull[sa], (g / NSA) & 1, abort_flag, err, 32)) { ok = false; break; }
-                    if (!tc::mbar_wait_spin(&bfull[sb], (g / NSB) & 1, abort_flag, err, 33)) { ok = false; break; }
-                    // the epilogue has taken chunk gc - 2's sums out of this buffer
-                    if (first && gc >= 2 && !tc::mbar_wait_spin(&sempty[db], ((gc >> 1) - 1) & 1, abort_flag, err, 31)) { ok = false; break; }
-                    tc::tc_fence_after();
-                    const int nk = 2 * min(2, nb - 2 * ss);  // 16-wide K steps with data
-                    const uint32_t ah = sA + sa * STAGE, bh = sB + sb * STAGE;
-                    const uint32_t dm = tbase + (uint32_t)(db * SBUF), dc = dm + (uint32_t)np2;
-                    // a 32-byte K step advances the descriptors' start address field by 2
-                    const uint64_t ahd = tc::smem_desc_sw128(ah), ald = tc::smem_desc_sw128(ah + PART);
-                    const uint64_t bd = tc::smem_desc_sw128(bh);
-                    TC_PROF_T(p_mma);
-                    for (int kk = 0; kk < nk; kk++) {
-                        tc::mma_f16_ss(dm, ahd + 2 * kk, bd + 2 * kk, idesc2, !(first && kk == 0));  // A_hi B_hi | A_hi B_lo
-                        tc::mma_f16_ss(dc, ald + 2 * kk, bd + 2 * kk, idesc1, 1);                    // + A_lo B_hi (cross)
-                    }
-                    TC_PROF_ADD(50, p_mma);
-                    TC_PROF_T(p_cmt);
-                    tc::mma_commit(&aempty[sa]);  // operand stages free once these MMAs complete
-                    tc::mma_commit(&bempty[sb]);
-                    TC_PROF_ADD(51, p_cmt);
-                    if (last) {
-                        tc::mma_commit(&sfull[db]);  // the chunk's sums are ready
-                        gc++;
-                    }
+        // ---------------- MMA issue: the whole warp runs the loop, one elected lane issues ----------------
+        uint32_t g = 0, gc = 0;
+        bool ok = true;
+        const uint32_t sB = tc::smem_u32(smem + OFF_B);
+        for (int t = blockIdx.x; t < T && ok; t += gridDim.x) {
+            const WorkItem it = a.items[t / MT];
+            const int np2 = np2_rows(it.count);
+            // [B_hi; B_lo] as one operand of 2 np2 rows: main and cross columns together
+            const uint32_t idesc2 = tc::idesc_f16(128, 2 * np2), idesc1 = tc::idesc_f16(128, np2);
+            for (int ss = 0; ss < nss; ss++, g++) {
+                const int st = g % NS, db = gc & 1;
+                const bool first = ss % CH == 0, last = ss % CH == CH - 1 || ss == nss - 1;
+                if (!tc::mbar_wait_spin(&opfull[st], (g / NS) & 1, abort_flag, err, 32)) ok = false;
+                // the epilogue has taken chunk gc - 2's sums out of this buffer
+                if (ok && first && gc >= 2 && !tc::mbar_wait_spin(&sempty[db], ((gc >> 1) - 1) & 1, abort_flag, err, 31))
+                    ok = false;
+                if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
+                tc::tc_fence_after();
+                const uint32_t ah = tbase + (uint32_t)(TM_A + st * A_COLS);
+                const uint32_t dm = tbase + (uint32_t)(db * SBUF), dc = dm + (uint32_t)np2;
+                // a 32-byte K step advances the descriptor's start address field by 2
+                const uint64_t bd = tc::smem_desc_sw128(sB + st * B_STAGE);
+                // K is a multiple of 64 (launch_moe_h3), so every stage has 4 K steps: a fixed,
+                // fully unrolled sequence of 8 MMAs issues back to back (a loop with a run-time
+                // trip count measured 3.5x slower per MMA, tc_f16_chain.cu)
+                TC_PROF_T(p_mma);
+#pragma unroll
+                for (int kk = 0; kk < 4; kk++) {
+                    tc::mma_f16_ts_warp(dm, ah + 8 * kk, bd + 2 * kk, idesc2, !(first && kk == 0));  // A_hi B_hi | A_hi B_lo
+                    tc::mma_f16_ts_warp(dc, ah + 32 + 8 * kk, bd + 2 * kk, idesc1, 1);               // + A_lo B_hi (cross)
                 }
+                TC_PROF_ADD(50, p_mma);
+                TC_PROF_T(p_cmt);
+                tc::mma_commit_warp(&opempty[st]);  // the stage is free once these MMAs complete
+                if (last) {
+                    tc::mma_commit_warp(&sfull[db]);  // the chunk's sums are ready
+                    gc++;
+                }
+                TC_PROF_ADD(51, p_cmt);
             }
-            // every MMA issued has completed before TMEM may be freed (bounded, whatever
-            // the abort flag says)
-            tc::mma_commit(drain);
-            tc::mbar_drain(drain, 0);
         }
+        // every MMA issued has completed before TMEM may be freed (bounded, whatever the
+        // abort flag says)
+        tc::mma_commit_warp(drain);
+        tc::mbar_drain(drain, 0);
     } else if (warp == WARP_TMA) {
         // ---------------- TMA: [B_hi; B_lo] of the item's rows, np2 rows each ----------------
         if (lane == 0) {
@@ -234,52 +240,68 @@ __global__ void __launch_bounds__(h3k::NTHREADS, 1)
             bool ok = true;
             for (int t = blockIdx.x; t < T && ok && !*abort_flag; t += gridDim.x) {
                 const WorkItem it = a.items[t / MT];
-                const int np2 = np2_rows(it.count), sel = np2 == 16 ? 0 : np2 == 32 ? 1 : np2 == 64 ? 2 : 3;
+                const int np2 = np2_rows(it.count), sel = np2 == 16 ? 0 : np2 == 32 ? 1 : 2;
                 for (int ss = 0; ss < nss; ss++, g++) {
-                    const int st = g % NSB;
-                    if (g >= NSB && !tc::mbar_wait_spin(&bempty[st], ((g / NSB) - 1) & 1, abort_flag, err, 37)) { ok = false; break; }
-                    tc::mbar_arrive_tx(&bfull[st], 2u * (uint32_t)np2 * 128u);
-                    uint8_t *dst = smem + OFF_B + st * STAGE, *dlo = dst + np2 * 128;
+                    const int st = g % NS;
+                    if (g >= NS && !tc::mbar_wait_spin(&opempty[st], ((g / NS) - 1) & 1, abort_flag, err, 37)) { ok = false; break; }
+                    tc::mbar_arrive_tx(&opfull[st], 2u * (uint32_t)np2 * 128u);
+                    uint8_t *dst = smem + OFF_B + st * B_STAGE, *dlo = dst + np2 * 128;
                     const int x = ss * 128;  // bytes: 64 fp16 per stage
                     // the maps are named with constant indices so they stay in parameter space
                     switch (sel) {
-                        case 0: tc::tma_load_2d(dst, &bmaps.hi[0], x, it.row0, &bfull[st]);
-                                tc::tma_load_2d(dlo, &bmaps.lo[0], x, it.row0, &bfull[st]); break;
-                        case 1: tc::tma_load_2d(dst, &bmaps.hi[1], x, it.row0, &bfull[st]);
-                                tc::tma_load_2d(dlo, &bmaps.lo[1], x, it.row0, &bfull[st]); break;
-                        case 2: tc::tma_load_2d(dst, &bmaps.hi[2], x, it.row0, &bfull[st]);
-                                tc::tma_load_2d(dlo, &bmaps.lo[2], x, it.row0, &bfull[st]); break;
-                        default: tc::tma_load_2d(dst, &bmaps.hi[3], x, it.row0, &bfull[st]);
-                                 tc::tma_load_2d(dlo, &bmaps.lo[3], x, it.row0, &bfull[st]); break;
+                        case 0: tc::tma_load_2d(dst, &bmaps.hi[0], x, it.row0, &opfull[st]);
+                                tc::tma_load_2d(dlo, &bmaps.lo[0], x, it.row0, &opfull[st]); break;
+                        case 1: tc::tma_load_2d(dst, &bmaps.hi[1], x, it.row0, &opfull[st]);
+                                tc::tma_load_2d(dlo, &bmaps.lo[1], x, it.row0, &opfull[st]); break;
+                        default: tc::tma_load_2d(dst, &bmaps.hi[2], x, it.row0, &opfull[st]);
+                                 tc::tma_load_2d(dlo, &bmaps.lo[2], x, it.row0, &opfull[st]); break;
                     }
                 }
             }
             // the last copies land before the CTA may exit
             // (bounded by time only: after an abort the copies still land in this CTA's memory)
-            for (uint32_t k = g > (uint32_t)NSB ? g - NSB : 0; k < g; k++) tc::mbar_drain(&bfull[k % NSB], (k / NSB) & 1);
+            // (each slot's latest use; the phase also needs the producers' arrivals, which
+            // come unless the kernel aborted, so this drain is bounded by time as well)
+            for (uint32_t k = g > (uint32_t)NS ? g - NS : 0; k < g; k++) tc::mbar_drain(&opfull[k % NS], (k / NS) & 1);
         }
     } else if (warp >= 4) {
-        // ---------------- A producers: weight row m0 + r -> A_hi, A_lo (swizzled) ----------------
-        const int r = tid - 128;
+        // ---------------- A producers: weight row m0 + r -> A_hi, A_lo in TMEM lane r ----------------
+        // warps 4-7 take the stage's first 32-weight block, warps 8-11 the second, so each SM
+        // sub-partition runs two independent producer chains
+        const int r = (warp & 3) * 32 + lane;      // TMEM lane (warp % 4 selects the lane quarter)
+        const int hb = (warp - 4) >> 2;            // block of the stage
+        const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
         const int nbp = (nb + 7) & ~7;
-        uint8_t *rawc = smem + OFF_RA + r * 32, *raws = smem + OFF_RW + r * 4;
-        // the stage sequence of this CTA's tiles, DEPTH - 1 stages ahead of consumption
-        int pt = blockIdx.x, pss = 0, pitem = -1;
-        WorkItem pit{};
+        uint8_t *rawc = smem + OFF_RA + r * 32 + hb * 16, *raws = smem + OFF_RW + (hb * 128 + r) * 4;
+        // the stage sequence of this CTA's tiles, DEPTH - 1 stages ahead of consumption: tile
+        // pt = item pi, row tile pm; the next tile of this CTA is pt + gridDim.x, reached by
+        // a fixed quotient and remainder (no division per stage), and the row's code and
+        // scale pointers are formed once per tile
+        const int dq = (int)gridDim.x / MT, dr = (int)gridDim.x % MT;
+        int pt = blockIdx.x, pi = (int)blockIdx.x / MT, pm = (int)blockIdx.x % MT, pss = 0;
+        const uint8_t *psrc = nullptr, *pscl = nullptr;
+        auto load_tile = [&]() {
+            if (pt >= T) return;
+            const WorkItem pit = a.items[pi];
+            const int row = pm * 128 + r;
+            psrc = a.codes + (long)pit.group * a.codes_gstride + (size_t)row * (nb * 16) + hb * 16;
+            pscl = reinterpret_cast<const uint8_t *>(a.scale) + (long)pit.group * a.scale_gstride + (size_t)row * nbp * 2;
+        };
+        load_tile();
         auto issue = [&](int slot) {
-            if (pt / MT != pitem) { pitem = pt / MT; pit = a.items[pitem]; }
-            const int m0 = (pt % MT) * 128;
-            const int nbl = min(2, nb - 2 * pss);
-            const uint8_t *src = a.codes + (long)pit.group * a.codes_gstride + (size_t)(m0 + r) * (nb * 16) +
-                                 (size_t)pss * 32;
-            cp_async16_zfill(rawc + slot * RA, src, true);
-            cp_async16_zfill(rawc + slot * RA + 16, nbl > 1 ? src + 16 : src, nbl > 1);
-            const uint8_t *sc = reinterpret_cast<const uint8_t *>(a.scale) + (long)pit.group * a.scale_gstride +
-                                ((size_t)(m0 + r) * nbp + 2 * pss) * 2;
-            cp_async4_zfill(raws + slot * RW, sc, true);  // rows are padded to 8 blocks: in bounds
+            const bool has = 2 * pss + hb < nb;  // this warp's block exists
+            cp_async16_zfill(rawc + slot * RA, has ? psrc + pss * 32 : psrc, has);
+            cp_async4_zfill(raws + slot * RW, pscl + pss * 4, true);  // rows are padded to 8 blocks: in bounds
         };
         auto advance = [&]() {
-            if (++pss == nss) { pss = 0; pt += gridDim.x; }
+            if (++pss == nss) {
+                pss = 0;
+                pt += gridDim.x;
+                pi += dq;
+                pm += dr;
+                if (pm >= MT) { pm -= MT; pi++; }
+                load_tile();
+            }
         };
 #pragma unroll
         for (int d = 0; d < DEPTH - 1; d++) {
@@ -290,46 +312,66 @@ __global__ void __launch_bounds__(h3k::NTHREADS, 1)
         bool ok = true;
         const int ntile = T > (int)blockIdx.x ? (T - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
         const uint32_t G = (uint32_t)ntile * nss;
-        for (uint32_t g = 0; g < G && ok; g++) {
+        // stage g: its codes in from the copy ring, converted into (H, L), the block's 32
+        // values in k order as fp16 pairs (q4_0: byte i holds k = i in its low nibble and
+        // k = i + 16 in its high nibble)
+        auto convert = [&](uint32_t g, uint32_t (&H)[16], uint32_t (&L)[16]) {
             if (pt < T) issue((int)((g + DEPTH - 1) % DEPTH));
             cp_async_commit();
             advance();
             cp_async_wait<DEPTH - 1>();  // this thread's copies of stage g have landed
-            const int slot = g % DEPTH, st = g % NSA;
-            const uint4 w0 = *reinterpret_cast<const uint4 *>(rawc + slot * RA);
-            const uint4 w1 = *reinterpret_cast<const uint4 *>(rawc + slot * RA + 16);
+            const int slot = g % DEPTH;
+            const uint4 w = *reinterpret_cast<const uint4 *>(rawc + slot * RA);
             const uint32_t sc = *reinterpret_cast<const uint32_t *>(raws + slot * RW);
             const __half2 hs2 = *reinterpret_cast<const __half2 *>(&sc);
-            uint32_t H[32], L[32];  // the stage's 64 values in k order, as fp16 pairs
+            const __half2 s = hb ? __high2half2(hs2) : __low2half2(hs2);
+            const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
-            for (int j = 0; j < 2; j++) {
-                // q4_0: byte i holds k = i (low nibble) and k = i + 16 (high)
-                const __half2 s = j ? __high2half2(hs2) : __low2half2(hs2);
-                const uint4 w = j ? w1 : w0;
-                const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
-#pragma unroll
-                for (int i = 0; i < 4; i++) {
-                    const uint32_t p01 = __byte_perm(ww[i], 0u, 0x4140u), p23 = __byte_perm(ww[i], 0u, 0x4342u);
-                    split_h2(q4lo_h2(p01), s, H[16 * j + 2 * i], L[16 * j + 2 * i]);
-                    split_h2(q4lo_h2(p23), s, H[16 * j + 2 * i + 1], L[16 * j + 2 * i + 1]);
-                    split_h2(q4hi_h2(p01), s, H[16 * j + 8 + 2 * i], L[16 * j + 8 + 2 * i]);
-                    split_h2(q4hi_h2(p23), s, H[16 * j + 8 + 2 * i + 1], L[16 * j + 8 + 2 * i + 1]);
-                }
+            for (int i = 0; i < 4; i++) {
+                const uint32_t p01 = __byte_perm(ww[i], 0u, 0x4140u), p23 = __byte_perm(ww[i], 0u, 0x4342u);
+                split_h2(q4lo_h2(p01), s, H[2 * i], L[2 * i]);
+                split_h2(q4lo_h2(p23), s, H[2 * i + 1], L[2 * i + 1]);
+                split_h2(q4hi_h2(p01), s, H[8 + 2 * i], L[8 + 2 * i]);
+                split_h2(q4hi_h2(p23), s, H[8 + 2 * i + 1], L[8 + 2 * i + 1]);
             }
-            // the slot is free once the MMAs of stage g - NSA have completed
-            if (g >= NSA && !tc::mbar_wait_spin(&aempty[st], ((g / NSA) - 1) & 1, abort_flag, err, 34)) { ok = false; break; }
-            uint8_t *hi = smem + OFF_A + st * STAGE, *lo = hi + PART;
-#pragma unroll
-            for (int q = 0; q < 8; q++) {
-                const uint32_t off = sw128_off(r, q);
-                *reinterpret_cast<uint4 *>(hi + off) = make_uint4(H[4 * q], H[4 * q + 1], H[4 * q + 2], H[4 * q + 3]);
-                *reinterpret_cast<uint4 *>(lo + off) = make_uint4(L[4 * q], L[4 * q + 1], L[4 * q + 2], L[4 * q + 3]);
-            }
-            // shared stores of the stage before the tensor cores' reads (async proxy)
-            tc::fence_proxy_async();
+        };
+        // stage g's columns into TMEM once its slot is free (the MMAs of stage g - NS done)
+        auto store = [&](uint32_t g, const uint32_t (&H)[16], const uint32_t (&L)[16]) {
+            const int st = g % NS;
+            if (g >= NS && !tc::mbar_wait_spin(&opempty[st], ((g / NS) - 1) & 1, abort_flag, err, 34)) ok = false;
+            ok = __all_sync(0xffffffffu, ok);  // tcgen05.st is warp-collective
+            if (!ok) return;
+            tc::tc_fence_after();
+            const uint32_t ta = tbase + lane_base + (uint32_t)(TM_A + st * A_COLS + 16 * hb);
+            tc::tmem_st16(ta, H);
+            tc::tmem_st16(ta + 32, L);
+        };
+        // stage g's stores have landed: publish it to the MMA
+        auto publish = [&](uint32_t g) {
+            tc::tmem_st_wait();
+            tc::tc_fence_before();
             __syncwarp();
-            if (lane == 0) tc::mbar_arrive(&afull[st]);
+            if (lane == 0) tc::mbar_arrive(&opfull[g % NS]);
+        };
+        // two register sets: stage g + 1 is converted while stage g's stores complete
+        uint32_t H0[16], L0[16], H1[16], L1[16];
+        if (G > 0) {
+            convert(0, H0, L0);
+            store(0, H0, L0);
         }
+        for (uint32_t g = 1; g < G && ok; g++) {
+            if (g & 1) {
+                convert(g, H1, L1);
+                publish(g - 1);
+                store(g, H1, L1);
+            } else {
+                convert(g, H0, L0);
+                publish(g - 1);
+                store(g, H0, L0);
+            }
+        }
+        if (G > 0 && ok) publish(G - 1);
+        tc::tmem_st_wait();  // no store of this thread is in flight when the CTA frees TMEM
         cp_async_wait<0>();
     } else {
         // ---------------- epilogue (warps 0-3): per-stage sums into f32 registers ----------------
@@ -494,7 +536,7 @@ static int launch_h3_t(const GemmArgs &a, int *err, cudaStream_t st) {
     }
     BMapsH maps;
     const long rb = (long)a.I * 2;
-    for (int i = 0; i < 4; i++) {
+    for (int i = 0; i < 3; i++) {
         if (!make_plane_map(&maps.hi[i], a.xhs, a.rows_cap, rb, 16 << i)) return 0;
         if (!make_plane_map(&maps.lo[i], a.xhs + (size_t)a.rows_cap * a.I, a.rows_cap, rb, 16 << i)) return 0;
     }

@@ -121,8 +121,9 @@ __device__ __forceinline__ bool mbar_test(uint64_t *bar, uint32_t parity) {
     return ok != 0;
 }
 // bounded wait without back-off, for the roles on a pipeline's critical path (the MMA
-// issuer, copy issuers, operand producers): the phase change is seen within one probe
-// instead of after a sleep. The clock and the abort flag are read every 256 probes.
+// issuer, copy issuers, operand producers): a ready phase costs one probe, and a pending
+// one is waited for in hardware (try_wait) instead of a sleep. The clock and the abort flag
+// are read every 16 tries.
 __device__ __forceinline__ bool mbar_wait_spin(uint64_t *bar, uint32_t parity, volatile int *abort, int *err,
                                                int code) {
 #ifdef ZZ_TC_PROF
@@ -139,8 +140,10 @@ __device__ __forceinline__ bool mbar_wait_spin(uint64_t *bar, uint32_t parity, v
     if (mbar_test(bar, parity)) return true;
     const unsigned long long w0 = global_ns();
     for (;;) {
-        for (int i = 0; i < 256; i++)
-            if (mbar_test(bar, parity)) return true;
+        // try_wait parks the thread in hardware until the phase completes (or a short
+        // time-out), so a waiting warp takes no issue slots from the warps doing the work
+        for (int i = 0; i < 16; i++)
+            if (mbar_try(bar, parity)) return true;
         if (*abort) return false;
         if (global_ns() - w0 > WAIT_LIMIT_NS) break;
     }
@@ -242,6 +245,33 @@ __device__ __forceinline__ void mma_f16_ss(uint32_t tmem_d, uint64_t adesc, uint
         "{.reg .pred p; setp.ne.b32 p, %4, 0;\n\t"
         "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;}" ::"r"(tmem_d),
         "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+// the same MMA issued by a whole warp in uniform control flow: one elected lane issues
+// it, and the operands (warp-uniform values) can stay in uniform registers
+__device__ __forceinline__ void mma_f16_ss_warp(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                                uint32_t accumulate) {
+    asm volatile(
+        "{.reg .pred p, e; setp.ne.b32 p, %4, 0;\n\t"
+        "elect.sync _|e, 0xffffffff;\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;}" ::"r"(tmem_d),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+__device__ __forceinline__ void mma_f16_ts_warp(uint32_t tmem_d, uint32_t tmem_a, uint64_t bdesc, uint32_t idesc,
+                                                uint32_t accumulate) {
+    asm volatile(
+        "{.reg .pred p, e; setp.ne.b32 p, %4, 0;\n\t"
+        "elect.sync _|e, 0xffffffff;\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;}" ::"r"(tmem_d),
+        "r"(tmem_a), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+// commit issued by one elected lane of a warp in uniform control flow
+__device__ __forceinline__ void mma_commit_warp(uint64_t *bar) {
+    asm volatile(
+        "{.reg .pred e; elect.sync _|e, 0xffffffff;\n\t"
+        "@e tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];}" ::"r"(smem_u32(bar))
         : "memory");
 }
 // D[tmem] (+)= A[tmem] * B[smem]^T: A is M lanes x K columns of packed fp16 pairs (the
