@@ -39,7 +39,7 @@ __global__ void k_rows_sx(const int8_t *__restrict__ xq, const float *__restrict
                           float *__restrict__ xsx);
 int launch_moe_i8(int fmt, int epi, const GemmArgs &a, int n_groups, int *err, cudaStream_t st);
 bool moe_i8_supported(int fmt, int D, int MI);
-int launch_moe_h3(int epi, const GemmArgs &a, int *err, cudaStream_t st);
+int launch_moe_h3(int epi, const GemmArgs &a, int n_groups, int *err, cudaStream_t st);
 int launch_split_rows(const int *pair_src, int K, const int8_t *xq, const float *xs, int D, int cap, __half *xhs,
                       int *err, cudaStream_t st);
 bool moe_h3_supported(int fmt, int D, int MI);
@@ -533,7 +533,7 @@ static int moe_impl(const zz_expert_bank *b, const float *X, const int8_t *xq_in
     if (h3) {
         g.hsT = nullptr;  // the down GEMM reads the fp16 planes instead
         g.xhs = w.xhs; g.hhs = w.hhs;
-        if (!launch_moe_h3(EPI_GATEUP, g, w.tcerr, st)) return 0;
+        if (!launch_moe_h3(EPI_GATEUP, g, E, w.tcerr, st)) return 0;
     } else if (i8) {
         if (!launch_moe_i8(fmt, EPI_GATEUP, g, E, w.tcerr, st)) return 0;
     } else if (!(wide ? launch_gemm<EPI_GATEUP, MOE_BN_WIDE, false, true>(fmt, g, dim3((2 * MI) / G_BM, maxit), st)
@@ -552,7 +552,7 @@ static int moe_impl(const zz_expert_bank *b, const float *X, const int8_t *xq_in
     d.out = OUT; d.pair_w = w.pair_w; d.pair_src = w.pair_src; d.K = K;
     d.xg8 = w.hq; d.xsT = w.hsT; d.ldT = (int)w.ldT; d.rows_cap = (int)w.cap;
     d.xhs = w.hhs;
-    int ok = h3 ? launch_moe_h3(EPI_DOWN, d, w.tcerr, st)
+    int ok = h3 ? launch_moe_h3(EPI_DOWN, d, E, w.tcerr, st)
            : i8 ? launch_moe_i8(fmt, EPI_DOWN, d, E, w.tcerr, st)
            : wide ? launch_gemm<EPI_DOWN, MOE_BN_WIDE, false, true>(fmt, d, dim3((D + G_BM - 1) / G_BM, maxit), st)
                   : launch_gemm<EPI_DOWN, MOE_BN, false, true>(fmt, d, dim3((D + G_BM - 1) / G_BM, maxit), st);

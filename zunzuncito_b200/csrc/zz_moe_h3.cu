@@ -31,19 +31,20 @@
 // hidden rows next to hq / hs. The weight side is converted per tile from the q4_0
 // planes, so HBM still carries 18 bytes per 32 weights.
 //
-// Persistent, warp-specialised, one CTA per SM (320 threads); work tiles are (item,
-// 128 weight rows), items being (expert, <= 128 routed rows) listed by the router in
+// Persistent, warp-specialised, one CTA per SM (480 threads); work tiles are (item,
+// 128 weight rows), items being (expert, <= 64 routed rows) listed by the router in
 // decreasing row count. K advances in stages of 64 weights (two blocks):
 //   warps 0-3   epilogue: thread = TMEM lane = weight row; per chunk the f32 sums, at the
 //               tile end through shared memory to the fused GeGLU / SwiGLU + q8_0 requant
 //               (bit-exact with q40_quant_act) or the weighted scatter-add into OUT
-//   warps 4-11  A producers, two per TMEM lane quarter: thread r of warp set hb streams
-//               block hb of each stage of weight row m0 + r (16 code bytes and the
-//               fp16 scales, cp.async DEPTH stages ahead) and writes its A_hi and A_lo
-//               columns into TMEM lane r (tcgen05.st)
+//   warps 4-11  A producers, two per TMEM lane quarter: thread r of warp set hb takes
+//               block hb of each stage of weight row m0 + r from the code slot, converts
+//               it to A_hi and A_lo and writes them into TMEM lane r (tcgen05.st)
 //   warp 12     TMA: the stage's B_hi and B_lo boxes (128 bytes x np2 rows, swizzled)
 //   warp 13     MMA: one elected lane issues 2 x 4 tcgen05.mma kind::f16 per stage (M = 128,
 //               N = 2 np2 and np2, K = 16)
+//   warp 14     TMA: the weight codes (128 rows x 128 bytes, swizzled: 4 stages) and their
+//               fp16 block scales into a ring of RC slots
 // Every wait is bounded (2 s of %globaltimer); one that runs out sets the kernel's error
 // word and the CTA drains (copies and MMAs in flight, bounded by time only), frees its
 // TMEM and returns.
@@ -63,21 +64,22 @@
 namespace zz {
 
 namespace h3k {
-constexpr int NTHREADS = 448;
+constexpr int NTHREADS = 480;
 constexpr int BN = 64;                  // max routed rows per tile
 constexpr int PART = BN * 128;          // one B part: 64 rows x 128 bytes (64 fp16)
 constexpr int NS = 4;                   // operand stages: A in TMEM, B in shared memory
 constexpr int B_STAGE = 2 * PART;       // [B_hi; B_lo], np2 rows each
-constexpr int DEPTH = 8;                // A producers: cp.async stages in flight per thread
-constexpr int RA = 128 * 32, RW = 256 * 4;  // raw code / scale bytes per stage
+constexpr int RC = 3;                   // code / scale slots of 4 stages (TMA)
+constexpr int C_SLOT = 128 * 128;       // 128 weight rows x 128 code bytes (256 weights)
+constexpr int W_SLOT = 128 * 16;        // their 8 fp16 block scales per row
 constexpr int CTX = 33;                 // tile-end exchange: 128 rows x 32 columns, padded
 constexpr int CT_BYTES = 128 * CTX * 4;
-constexpr int OFF_B = 0;                // 1 KB aligned (swizzled operands)
-constexpr int OFF_RA = OFF_B + NS * B_STAGE;
-constexpr int OFF_RW = OFF_RA + DEPTH * RA;
-constexpr int OFF_CT = OFF_RW + DEPTH * RW;
+constexpr int OFF_B = 0;                // 1 KB aligned (swizzled operands and boxes)
+constexpr int OFF_C = OFF_B + NS * B_STAGE;
+constexpr int OFF_W = OFF_C + RC * C_SLOT;
+constexpr int OFF_CT = OFF_W + RC * W_SLOT;
 constexpr int OFF_BAR = OFF_CT + CT_BYTES;
-constexpr int NBAR = 2 * NS + 2 * 2 + 1;
+constexpr int NBAR = 2 * NS + 2 * RC + 2 * 2 + 1;
 constexpr int SMEM = OFF_BAR + NBAR * 8 + 16 + 1024;  // + slack to align the base to 1 KB
 static_assert(SMEM <= 232448, "shared memory");
 // TMEM columns: two chunk buffers of 2 BN columns (a chunk's sums are [main (np2) | cross
@@ -86,7 +88,7 @@ constexpr int SBUF = 2 * BN, TM_A = 2 * SBUF, A_COLS = 64;
 constexpr int TMEM_COLS = 512;
 static_assert(TM_A + NS * A_COLS <= TMEM_COLS, "TMEM columns");
 constexpr int CH = 4;                   // stages per TMEM sum (16 K steps of 16)
-constexpr int WARP_TMA = 12, WARP_MMA = 13;
+constexpr int WARP_TMA = 12, WARP_MMA = 13, WARP_CODE = 14;
 }  // namespace h3k
 
 // fp16 pair -> (hi, lo) with hi = fp16(v * s), lo = fp16(v * s - hi) exactly
@@ -158,7 +160,8 @@ __device__ __forceinline__ int np2_rows(int count) {
 
 template <int EPI>
 __global__ void __launch_bounds__(h3k::NTHREADS, 1)
-    k_moe_h3(const GemmArgs a, const __grid_constant__ BMapsH bmaps, int *err) {
+    k_moe_h3(const GemmArgs a, const __grid_constant__ BMapsH bmaps, const __grid_constant__ CUtensorMap codes_map,
+             const __grid_constant__ CUtensorMap scale_map, int *err) {
     using namespace h3k;
     extern __shared__ __align__(128) uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
@@ -167,6 +170,9 @@ __global__ void __launch_bounds__(h3k::NTHREADS, 1)
     // (8 arrivals + the copy thread's arrive with its byte count), empty when its MMAs are done
     uint64_t *opfull = bars, *opempty = opfull + NS;
     uint64_t *sfull = opempty + NS, *sempty = sfull + 2, *drain = sempty + 2;
+    // a code slot (4 stages of 128 weight rows) is full when its two boxes have landed,
+    // empty when the 8 producer warps have read it
+    uint64_t *cfull = drain + 1, *cempty = cfull + RC;
     uint32_t *tmem_base_smem = reinterpret_cast<uint32_t *>(smem + OFF_BAR + NBAR * 8);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + OFF_BAR + NBAR * 8 + 4);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -177,6 +183,7 @@ __global__ void __launch_bounds__(h3k::NTHREADS, 1)
         for (int i = 0; i < NS; i++) { tc::mbar_init(&opfull[i], 9); tc::mbar_init(&opempty[i], 1); }
         for (int i = 0; i < 2; i++) { tc::mbar_init(&sfull[i], 1); tc::mbar_init(&sempty[i], 4); }
         tc::mbar_init(drain, 1);
+        for (int i = 0; i < RC; i++) { tc::mbar_init(&cfull[i], 1); tc::mbar_init(&cempty[i], 8); }
         *abort_flag = 0;
         tc::mbar_init_fence();
     }
@@ -264,6 +271,26 @@ __global__ void __launch_bounds__(h3k::NTHREADS, 1)
             // come unless the kernel aborted, so this drain is bounded by time as well)
             for (uint32_t k = g > (uint32_t)NS ? g - NS : 0; k < g; k++) tc::mbar_drain(&opfull[k % NS], (k / NS) & 1);
         }
+    } else if (warp == WARP_CODE) {
+        // ---------------- TMA: weight codes and block scales, 4 stages per slot ----------------
+        if (lane == 0) {
+            uint32_t gq = 0;
+            bool ok = true;
+            const int ng = (nss + 3) / 4;
+            for (int t = blockIdx.x; t < T && ok && !*abort_flag; t += gridDim.x) {
+                const WorkItem it = a.items[t / MT];
+                const int m0 = (t % MT) * 128, y = it.group * a.O + m0;
+                for (int q = 0; q < ng; q++, gq++) {
+                    const int c = gq % RC;
+                    if (gq >= RC && !tc::mbar_wait_spin(&cempty[c], ((gq / RC) - 1) & 1, abort_flag, err, 39)) { ok = false; break; }
+                    tc::mbar_arrive_tx(&cfull[c], C_SLOT + W_SLOT);
+                    tc::tma_load_2d(smem + OFF_C + c * C_SLOT, &codes_map, q * 128, y, &cfull[c]);
+                    tc::tma_load_3d(smem + OFF_W + c * W_SLOT, &scale_map, q * 8, m0, it.group, &cfull[c]);
+                }
+            }
+            // the last copies land before the CTA may exit (bounded by time only)
+            for (uint32_t k = gq > (uint32_t)RC ? gq - RC : 0; k < gq; k++) tc::mbar_drain(&cfull[k % RC], (k / RC) & 1);
+        }
     } else if (warp >= 4) {
         // ---------------- A producers: weight row m0 + r -> A_hi, A_lo in TMEM lane r ----------------
         // warps 4-7 take the stage's first 32-weight block, warps 8-11 the second, so each SM
@@ -271,108 +298,52 @@ __global__ void __launch_bounds__(h3k::NTHREADS, 1)
         const int r = (warp & 3) * 32 + lane;      // TMEM lane (warp % 4 selects the lane quarter)
         const int hb = (warp - 4) >> 2;            // block of the stage
         const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
-        const int nbp = (nb + 7) & ~7;
-        uint8_t *rawc = smem + OFF_RA + r * 32 + hb * 16, *raws = smem + OFF_RW + (hb * 128 + r) * 4;
-        // the stage sequence of this CTA's tiles, DEPTH - 1 stages ahead of consumption: tile
-        // pt = item pi, row tile pm; the next tile of this CTA is pt + gridDim.x, reached by
-        // a fixed quotient and remainder (no division per stage), and the row's code and
-        // scale pointers are formed once per tile
-        const int dq = (int)gridDim.x / MT, dr = (int)gridDim.x % MT;
-        int pt = blockIdx.x, pi = (int)blockIdx.x / MT, pm = (int)blockIdx.x % MT, pss = 0;
-        const uint8_t *psrc = nullptr, *pscl = nullptr;
-        auto load_tile = [&]() {
-            if (pt >= T) return;
-            const WorkItem pit = a.items[pi];
-            const int row = pm * 128 + r;
-            psrc = a.codes + (long)pit.group * a.codes_gstride + (size_t)row * (nb * 16) + hb * 16;
-            pscl = reinterpret_cast<const uint8_t *>(a.scale) + (long)pit.group * a.scale_gstride + (size_t)row * nbp * 2;
-        };
-        load_tile();
-        auto issue = [&](int slot) {
-            const bool has = 2 * pss + hb < nb;  // this warp's block exists
-            cp_async16_zfill(rawc + slot * RA, has ? psrc + pss * 32 : psrc, has);
-            cp_async4_zfill(raws + slot * RW, pscl + pss * 4, true);  // rows are padded to 8 blocks: in bounds
-        };
-        auto advance = [&]() {
-            if (++pss == nss) {
-                pss = 0;
-                pt += gridDim.x;
-                pi += dq;
-                pm += dr;
-                if (pm >= MT) { pm -= MT; pi++; }
-                load_tile();
-            }
-        };
-#pragma unroll
-        for (int d = 0; d < DEPTH - 1; d++) {
-            if (pt < T) issue(d);
-            cp_async_commit();
-            advance();
-        }
+        uint32_t g = 0, gq = 0;
         bool ok = true;
-        const int ntile = T > (int)blockIdx.x ? (T - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
-        const uint32_t G = (uint32_t)ntile * nss;
-        // stage g: its codes in from the copy ring, converted into (H, L), the block's 32
-        // values in k order as fp16 pairs (q4_0: byte i holds k = i in its low nibble and
-        // k = i + 16 in its high nibble)
-        auto convert = [&](uint32_t g, uint32_t (&H)[16], uint32_t (&L)[16]) {
-            if (pt < T) issue((int)((g + DEPTH - 1) % DEPTH));
-            cp_async_commit();
-            advance();
-            cp_async_wait<DEPTH - 1>();  // this thread's copies of stage g have landed
-            const int slot = g % DEPTH;
-            const uint4 w = *reinterpret_cast<const uint4 *>(rawc + slot * RA);
-            const uint32_t sc = *reinterpret_cast<const uint32_t *>(raws + slot * RW);
-            const __half2 hs2 = *reinterpret_cast<const __half2 *>(&sc);
-            const __half2 s = hb ? __high2half2(hs2) : __low2half2(hs2);
-            const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
+        for (int t = blockIdx.x; t < T && ok; t += gridDim.x) {
+            for (int ss = 0; ss < nss && ok; ss++, g++) {
+                const int j = ss & 3, c = gq % RC, st = g % NS;
+                if (j == 0) ok = tc::mbar_wait_spin(&cfull[c], (gq / RC) & 1, abort_flag, err, 30);
+                // this row's 16 code bytes of block 2 ss + hb (128-byte swizzled box) and the
+                // stage's two fp16 scales
+                const uint8_t *cs = smem + OFF_C + c * C_SLOT + r * 128;
+                const uint4 w = *reinterpret_cast<const uint4 *>(cs + (((2 * j + hb) ^ (r & 7)) << 4));
+                const uint32_t sc = *reinterpret_cast<const uint32_t *>(smem + OFF_W + c * W_SLOT + r * 16 + 4 * j);
+                if (j == 3 || ss == nss - 1) {
+                    // the slot's last stage is read: hand it back to the copy warp
+                    asm volatile("" ::"r"(w.x), "r"(w.y), "r"(w.z), "r"(w.w), "r"(sc) : "memory");
+                    tc::fence_proxy_async();
+                    __syncwarp();
+                    if (lane == 0) tc::mbar_arrive(&cempty[c]);
+                    gq++;
+                }
+                const __half2 hs2 = *reinterpret_cast<const __half2 *>(&sc);
+                // q4_0: byte i holds k = i (low nibble) and k = i + 16 (high)
+                const __half2 s = hb ? __high2half2(hs2) : __low2half2(hs2);
+                const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
+                uint32_t H[16], L[16];  // the block's 32 values in k order, as fp16 pairs
 #pragma unroll
-            for (int i = 0; i < 4; i++) {
-                const uint32_t p01 = __byte_perm(ww[i], 0u, 0x4140u), p23 = __byte_perm(ww[i], 0u, 0x4342u);
-                split_h2(q4lo_h2(p01), s, H[2 * i], L[2 * i]);
-                split_h2(q4lo_h2(p23), s, H[2 * i + 1], L[2 * i + 1]);
-                split_h2(q4hi_h2(p01), s, H[8 + 2 * i], L[8 + 2 * i]);
-                split_h2(q4hi_h2(p23), s, H[8 + 2 * i + 1], L[8 + 2 * i + 1]);
-            }
-        };
-        // stage g's columns into TMEM once its slot is free (the MMAs of stage g - NS done)
-        auto store = [&](uint32_t g, const uint32_t (&H)[16], const uint32_t (&L)[16]) {
-            const int st = g % NS;
-            if (g >= NS && !tc::mbar_wait_spin(&opempty[st], ((g / NS) - 1) & 1, abort_flag, err, 34)) ok = false;
-            ok = __all_sync(0xffffffffu, ok);  // tcgen05.st is warp-collective
-            if (!ok) return;
-            tc::tc_fence_after();
-            const uint32_t ta = tbase + lane_base + (uint32_t)(TM_A + st * A_COLS + 16 * hb);
-            tc::tmem_st16(ta, H);
-            tc::tmem_st16(ta + 32, L);
-        };
-        // stage g's stores have landed: publish it to the MMA
-        auto publish = [&](uint32_t g) {
-            tc::tmem_st_wait();
-            tc::tc_fence_before();
-            __syncwarp();
-            if (lane == 0) tc::mbar_arrive(&opfull[g % NS]);
-        };
-        // two register sets: stage g + 1 is converted while stage g's stores complete
-        uint32_t H0[16], L0[16], H1[16], L1[16];
-        if (G > 0) {
-            convert(0, H0, L0);
-            store(0, H0, L0);
-        }
-        for (uint32_t g = 1; g < G && ok; g++) {
-            if (g & 1) {
-                convert(g, H1, L1);
-                publish(g - 1);
-                store(g, H1, L1);
-            } else {
-                convert(g, H0, L0);
-                publish(g - 1);
-                store(g, H0, L0);
+                for (int i = 0; i < 4; i++) {
+                    const uint32_t p01 = __byte_perm(ww[i], 0u, 0x4140u), p23 = __byte_perm(ww[i], 0u, 0x4342u);
+                    split_h2(q4lo_h2(p01), s, H[2 * i], L[2 * i]);
+                    split_h2(q4lo_h2(p23), s, H[2 * i + 1], L[2 * i + 1]);
+                    split_h2(q4hi_h2(p01), s, H[8 + 2 * i], L[8 + 2 * i]);
+                    split_h2(q4hi_h2(p23), s, H[8 + 2 * i + 1], L[8 + 2 * i + 1]);
+                }
+                // the TMEM stage is free once the MMAs of stage g - NS have completed
+                if (ok && g >= NS && !tc::mbar_wait_spin(&opempty[st], ((g / NS) - 1) & 1, abort_flag, err, 34)) ok = false;
+                ok = __all_sync(0xffffffffu, ok);  // tcgen05.st is warp-collective
+                if (!ok) break;
+                tc::tc_fence_after();
+                const uint32_t ta = tbase + lane_base + (uint32_t)(TM_A + st * A_COLS + 16 * hb);
+                tc::tmem_st16(ta, H);
+                tc::tmem_st16(ta + 32, L);
+                tc::tmem_st_wait();
+                tc::tc_fence_before();
+                __syncwarp();
+                if (lane == 0) tc::mbar_arrive(&opfull[st]);
             }
         }
-        if (G > 0 && ok) publish(G - 1);
-        tc::tmem_st_wait();  // no store of this thread is in flight when the CTA frees TMEM
-        cp_async_wait<0>();
     } else {
         // ---------------- epilogue (warps 0-3): per-stage sums into f32 registers ----------------
         const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
@@ -525,8 +496,12 @@ static int make_plane_map(CUtensorMap *map, const void *base, long rows, long ro
     return 1;
 }
 
+int make_u8_map(CUtensorMap *map, const void *base, long rows, long row_bytes, int box_w, int box_rows,
+                const char *what);
+int make_scale_map(CUtensorMap *map, const void *scale, int E, int O, int nbp, long gstride);
+
 template <int EPI>
-static int launch_h3_t(const GemmArgs &a, int *err, cudaStream_t st) {
+static int launch_h3_t(const GemmArgs &a, int n_groups, int *err, cudaStream_t st) {
     static bool attr = false;  // per process: the attribute is a property of the function
     if (!attr) {
         if (!check_cuda(cudaFuncSetAttribute(k_moe_h3<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, h3k::SMEM),
@@ -540,10 +515,13 @@ static int launch_h3_t(const GemmArgs &a, int *err, cudaStream_t st) {
         if (!make_plane_map(&maps.hi[i], a.xhs, a.rows_cap, rb, 16 << i)) return 0;
         if (!make_plane_map(&maps.lo[i], a.xhs + (size_t)a.rows_cap * a.I, a.rows_cap, rb, 16 << i)) return 0;
     }
+    CUtensorMap cmap, smap;
+    if (!make_u8_map(&cmap, a.codes, (long)n_groups * a.O, a.I / 2, 128, 128, "h3 weight codes")) return 0;
+    if (!make_scale_map(&smap, a.scale, n_groups, a.O, ((a.I / ZZ_BLK) + 7) & ~7, a.scale_gstride)) return 0;
     int dev = 0, sms = 148;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    k_moe_h3<EPI><<<sms, h3k::NTHREADS, h3k::SMEM, st>>>(a, maps, err);
+    k_moe_h3<EPI><<<sms, h3k::NTHREADS, h3k::SMEM, st>>>(a, maps, cmap, smap, err);
     return check_cuda(cudaGetLastError(), "h3 launch");
 }
 
@@ -556,14 +534,17 @@ int launch_split_rows(const int *pair_src, int K, const int8_t *xq, const float 
 // Whether the folded-scale fp16 engine takes a layer of this shape: q4_0 banks, weight
 // rows in whole 128-row tiles, K in whole 64-weight stages on both GEMMs.
 bool moe_h3_supported(int fmt, int D, int MI) {
-    return fmt == GPU_FMT_Q40 && (2 * MI) % 128 == 0 && D % 128 == 0 && MI % 64 == 0;
+    // consecutive experts' code planes exactly O * row_bytes apart (one tensor map spans
+    // the bank): true for a packed bank when the plane is a multiple of 256 bytes
+    return fmt == GPU_FMT_Q40 && (2 * MI) % 128 == 0 && D % 128 == 0 && MI % 64 == 0 &&
+           ((long)2 * MI * (D / 2)) % 256 == 0 && ((long)D * (MI / 2)) % 256 == 0;
 }
 
 // The expert GEMMs (gate/up with the fused activation + requant, or down with the fused
 // scatter-add) over the router's items, folded-scale fp16 operands on tcgen05.
-int launch_moe_h3(int epi, const GemmArgs &a, int *err, cudaStream_t st) {
+int launch_moe_h3(int epi, const GemmArgs &a, int n_groups, int *err, cudaStream_t st) {
     if (a.O % 128 || a.I % 64 || !a.xhs) return fail("h3: O=%d / I=%d not multiples of 128 / 64", a.O, a.I);
-    return epi == EPI_GATEUP ? launch_h3_t<EPI_GATEUP>(a, err, st) : launch_h3_t<EPI_DOWN>(a, err, st);
+    return epi == EPI_GATEUP ? launch_h3_t<EPI_GATEUP>(a, n_groups, err, st) : launch_h3_t<EPI_DOWN>(a, n_groups, err, st);
 }
 
 }  // namespace zz

@@ -721,7 +721,7 @@ static int get_encode() {
 
 // 2-D uint8 map over [rows][row_bytes] with a box of `box_w` bytes x `box_rows` rows,
 // swizzled by the box width (128 / 64 bytes)
-static int make_u8_map(CUtensorMap *map, const void *base, long rows, long row_bytes, int box_w, int box_rows,
+int make_u8_map(CUtensorMap *map, const void *base, long rows, long row_bytes, int box_w, int box_rows,
                        const char *what) {
     if (!get_encode()) return 0;
     if ((uintptr_t)base & 15 || row_bytes % 16) return fail("i8: %s not 16-byte aligned", what);
@@ -739,7 +739,7 @@ static int make_u8_map(CUtensorMap *map, const void *base, long rows, long row_b
 
 // fp16 weight-scale planes of a bank: [experts][O][nbp] (rows padded to 8 blocks), each
 // expert `gstride` bytes apart; one box is 128 rows x 8 scales (one stage)
-static int make_scale_map(CUtensorMap *map, const void *scale, int E, int O, int nbp, long gstride) {
+int make_scale_map(CUtensorMap *map, const void *scale, int E, int O, int nbp, long gstride) {
     if (!get_encode()) return 0;
     if ((uintptr_t)scale & 15 || gstride % 16 || nbp % 8) return fail("i8: scale planes not 16-byte aligned");
     cuuint64_t dims[3] = {(cuuint64_t)nbp, (cuuint64_t)O, (cuuint64_t)E};

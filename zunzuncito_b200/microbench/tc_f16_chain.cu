@@ -13,6 +13,7 @@
 //                 lane issuing each MMA (operands in uniform registers)
 //   unrolled      the engine's loop shape: per stage a probe, a fence and a commit around
 //                 4 fully unrolled MMA pairs
+//   A in TMEM     the same with the A operand read from TMEM ([a-tmem] form)
 //   stage=4       plus, every 4 MMA pairs (one 64-weight stage), a probe of a completed
 //                 barrier phase and a commit: the engine's per-stage bookkeeping
 // against the arithmetic alone (M N K 2 / 8192 flops per SM cycle). Every wait is
@@ -83,7 +84,7 @@ __global__ void __launch_bounds__(128, 1) k_chain(Case c, unsigned long long *cy
             if (tc::global_ns() - w0 > 100000000ull) { atomicExch(err, 1); break; }
         const long long t1 = clock64();
         if (tid == 0) atomicMax(cycles, (unsigned long long)(t1 - t0));
-    } else if (c.warp_issue == 2 && warp == 0) {
+    } else if (c.warp_issue >= 2 && warp == 0) {
         // the engine's loop shape: per stage a probe, a fence and a commit, then the stage's
         // 4 MMA pairs fully unrolled with descriptors formed once per stage
         const uint32_t sa = tc::smem_u32(smem), sb = tc::smem_u32(smem + 32768);
@@ -93,10 +94,20 @@ __global__ void __launch_bounds__(128, 1) k_chain(Case c, unsigned long long *cy
             while (!tc::mbar_test(bar + 2, 0)) {}
             tc::tc_fence_after();
             const uint64_t ad = tc::smem_desc_sw128(sa + (st & 1) * 16384), bd = tc::smem_desc_sw128(sb + (st & 1) * 16384);
+            if (c.warp_issue == 3) {
+                // A from TMEM (columns 256.. of the allocation, packed fp16 pairs)
+                const uint32_t at = tbase + 256 + (st & 1) * 64;
 #pragma unroll
-            for (int kk = 0; kk < 4; kk++) {
-                tc::mma_f16_ss_warp(tbase + c.off1, ad + 2 * kk, bd + 2 * kk, id1, (st | kk) != 0);
-                tc::mma_f16_ss_warp(tbase + c.off2, ad + 2 * kk, bd + 2 * kk, id2, 1);
+                for (int kk = 0; kk < 4; kk++) {
+                    tc::mma_f16_ts_warp(tbase + c.off1, at + 8 * kk, bd + 2 * kk, id1, (st | kk) != 0);
+                    tc::mma_f16_ts_warp(tbase + c.off2, at + 32 + 8 * kk, bd + 2 * kk, id2, 1);
+                }
+            } else {
+#pragma unroll
+                for (int kk = 0; kk < 4; kk++) {
+                    tc::mma_f16_ss_warp(tbase + c.off1, ad + 2 * kk, bd + 2 * kk, id1, (st | kk) != 0);
+                    tc::mma_f16_ss_warp(tbase + c.off2, ad + 2 * kk, bd + 2 * kk, id2, 1);
+                }
             }
             tc::mma_commit_warp(bar + 3);
         }
@@ -165,6 +176,8 @@ int main() {
         {"  commit only", 64, 0, 32, 32, 0, 1, 4, 4}, {"  commit, stage=8", 64, 0, 32, 32, 0, 1, 8, 4},
         {"unrolled stage 64+32", 64, 0, 32, 32, 0, 2},    {"unrolled stage 128+64", 128, 0, 64, 64, 0, 2},
         {"unrolled stage 32+16", 32, 0, 16, 16, 0, 2},
+        {"A in TMEM 64+32", 64, 0, 32, 32, 0, 3},         {"A in TMEM 128+64", 128, 0, 64, 64, 0, 3},
+        {"A in TMEM 32+16", 32, 0, 16, 16, 0, 3},
     };
     printf("%-20s %10s %10s %8s\n", "case", "cyc/MMA", "arith", "ratio");
     for (const Case &c : cases) {
