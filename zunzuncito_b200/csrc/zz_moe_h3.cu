@@ -50,12 +50,12 @@
 // TMEM and returns.
 //
 // Measured (B200, Gemma-4 layer, 128 q4_0 experts): parity with the oracle at every
-// benched shape; S = 4096 layer 2.03 ms against 1.97 for the int8 mma.sync engine with
-// 64-row items, S = 512 0.46 against 0.35 ms. What sets the pace (profiles/, the MMA-chain
-// microbenchmark): the MMA issue sequence must be a fixed, unrolled run per stage (a loop
-// with a run-time trip count costs 3.5x per MMA), operands are issued by a whole warp
-// with one elected lane, and the weight producers' per-stage latency is the remaining
-// bound. It stays opt-in (ZZ_MOE_KERNEL=h3).
+// benched shape; S = 4096 layer 1.98 ms, the same as the int8 mma.sync engine with 64-row
+// items (down GEMM 18% faster, gate/up 5% slower, plus the per-layer split of B), S = 512
+// 0.45 against 0.35 ms. What sets the pace (profiles/, the MMA-chain microbenchmark): the
+// MMA issue sequence must be a fixed, unrolled run per stage (a loop with a run-time trip
+// count costs 3.5x per MMA), issued by a whole warp with one elected lane; what remains
+// is the pipeline's own hand-offs between roles. It stays opt-in (ZZ_MOE_KERNEL=h3).
 #include <cuda.h>
 #include <cudaTypedefs.h>
 #include "zz_gemm.cuh"
@@ -67,7 +67,8 @@ namespace h3k {
 constexpr int NTHREADS = 480;
 constexpr int BN = 64;                  // max routed rows per tile
 constexpr int PART = BN * 128;          // one B part: 64 rows x 128 bytes (64 fp16)
-constexpr int NS = 4;                   // operand stages: A in TMEM, B in shared memory
+constexpr int NS = 4;                   // A stages (TMEM)
+constexpr int NB = 4;                   // B stages (shared memory; 8 measured slower)
 constexpr int B_STAGE = 2 * PART;       // [B_hi; B_lo], np2 rows each
 constexpr int RC = 3;                   // code / scale slots of 4 stages (TMA)
 constexpr int C_SLOT = 128 * 128;       // 128 weight rows x 128 code bytes (256 weights)
@@ -75,11 +76,11 @@ constexpr int W_SLOT = 128 * 16;        // their 8 fp16 block scales per row
 constexpr int CTX = 33;                 // tile-end exchange: 128 rows x 32 columns, padded
 constexpr int CT_BYTES = 128 * CTX * 4;
 constexpr int OFF_B = 0;                // 1 KB aligned (swizzled operands and boxes)
-constexpr int OFF_C = OFF_B + NS * B_STAGE;
+constexpr int OFF_C = OFF_B + NB * B_STAGE;
 constexpr int OFF_W = OFF_C + RC * C_SLOT;
 constexpr int OFF_CT = OFF_W + RC * W_SLOT;
 constexpr int OFF_BAR = OFF_CT + CT_BYTES;
-constexpr int NBAR = 2 * NS + 2 * RC + 2 * 2 + 1;
+constexpr int NBAR = 2 * NS + 2 * NB + 2 * RC + 2 * 2 + 1;
 constexpr int SMEM = OFF_BAR + NBAR * 8 + 16 + 1024;  // + slack to align the base to 1 KB
 static_assert(SMEM <= 232448, "shared memory");
 // TMEM columns: two chunk buffers of 2 BN columns (a chunk's sums are [main (np2) | cross
@@ -166,10 +167,10 @@ __global__ void __launch_bounds__(h3k::NTHREADS, 1)
     extern __shared__ __align__(128) uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem + OFF_BAR);
-    // a stage is full when the 8 producer warps have written A and the B copies have landed
-    // (8 arrivals + the copy thread's arrive with its byte count), empty when its MMAs are done
-    uint64_t *opfull = bars, *opempty = opfull + NS;
-    uint64_t *sfull = opempty + NS, *sempty = sfull + 2, *drain = sempty + 2;
+    // an A stage is full when the 8 producer warps have written it, a B stage when its
+    // copies have landed; both are empty when the stage's MMAs are done
+    uint64_t *opfull = bars, *opempty = opfull + NS, *bfull = opempty + NS, *bempty = bfull + NB;
+    uint64_t *sfull = bempty + NB, *sempty = sfull + 2, *drain = sempty + 2;
     // a code slot (4 stages of 128 weight rows) is full when its two boxes have landed,
     // empty when the 8 producer warps have read it
     uint64_t *cfull = drain + 1, *cempty = cfull + RC;
@@ -180,7 +181,8 @@ __global__ void __launch_bounds__(h3k::NTHREADS, 1)
     const int T = *a.n_items * MT;
 
     if (tid == 0) {
-        for (int i = 0; i < NS; i++) { tc::mbar_init(&opfull[i], 9); tc::mbar_init(&opempty[i], 1); }
+        for (int i = 0; i < NS; i++) { tc::mbar_init(&opfull[i], 8); tc::mbar_init(&opempty[i], 1); }
+        for (int i = 0; i < NB; i++) { tc::mbar_init(&bfull[i], 1); tc::mbar_init(&bempty[i], 1); }
         for (int i = 0; i < 2; i++) { tc::mbar_init(&sfull[i], 1); tc::mbar_init(&sempty[i], 4); }
         tc::mbar_init(drain, 1);
         for (int i = 0; i < RC; i++) { tc::mbar_init(&cfull[i], 1); tc::mbar_init(&cempty[i], 8); }
@@ -205,9 +207,10 @@ __global__ void __launch_bounds__(h3k::NTHREADS, 1)
             // [B_hi; B_lo] as one operand of 2 np2 rows: main and cross columns together
             const uint32_t idesc2 = tc::idesc_f16(128, 2 * np2), idesc1 = tc::idesc_f16(128, np2);
             for (int ss = 0; ss < nss; ss++, g++) {
-                const int st = g % NS, db = gc & 1;
+                const int st = g % NS, sb = g % NB, db = gc & 1;
                 const bool first = ss % CH == 0, last = ss % CH == CH - 1 || ss == nss - 1;
                 if (!tc::mbar_wait_spin(&opfull[st], (g / NS) & 1, abort_flag, err, 32)) ok = false;
+                if (ok && !tc::mbar_wait_spin(&bfull[sb], (g / NB) & 1, abort_flag, err, 33)) ok = false;
                 // the epilogue has taken chunk gc - 2's sums out of this buffer
                 if (ok && first && gc >= 2 && !tc::mbar_wait_spin(&sempty[db], ((gc >> 1) - 1) & 1, abort_flag, err, 31))
                     ok = false;
@@ -216,7 +219,7 @@ __global__ void __launch_bounds__(h3k::NTHREADS, 1)
                 const uint32_t ah = tbase + (uint32_t)(TM_A + st * A_COLS);
                 const uint32_t dm = tbase + (uint32_t)(db * SBUF), dc = dm + (uint32_t)np2;
                 // a 32-byte K step advances the descriptor's start address field by 2
-                const uint64_t bd = tc::smem_desc_sw128(sB + st * B_STAGE);
+                const uint64_t bd = tc::smem_desc_sw128(sB + sb * B_STAGE);
                 // K is a multiple of 64 (launch_moe_h3), so every stage has 4 K steps: a fixed,
                 // fully unrolled sequence of 8 MMAs issues back to back (a loop with a run-time
                 // trip count measured 3.5x slower per MMA, tc_f16_chain.cu)
@@ -228,7 +231,8 @@ __global__ void __launch_bounds__(h3k::NTHREADS, 1)
                 }
                 TC_PROF_ADD(50, p_mma);
                 TC_PROF_T(p_cmt);
-                tc::mma_commit_warp(&opempty[st]);  // the stage is free once these MMAs complete
+                tc::mma_commit_warp(&opempty[st]);  // the stages are free once these MMAs complete
+                tc::mma_commit_warp(&bempty[sb]);
                 if (last) {
                     tc::mma_commit_warp(&sfull[db]);  // the chunk's sums are ready
                     gc++;
@@ -249,27 +253,26 @@ __global__ void __launch_bounds__(h3k::NTHREADS, 1)
                 const WorkItem it = a.items[t / MT];
                 const int np2 = np2_rows(it.count), sel = np2 == 16 ? 0 : np2 == 32 ? 1 : 2;
                 for (int ss = 0; ss < nss; ss++, g++) {
-                    const int st = g % NS;
-                    if (g >= NS && !tc::mbar_wait_spin(&opempty[st], ((g / NS) - 1) & 1, abort_flag, err, 37)) { ok = false; break; }
-                    tc::mbar_arrive_tx(&opfull[st], 2u * (uint32_t)np2 * 128u);
+                    const int st = g % NB;
+                    if (g >= NB && !tc::mbar_wait_spin(&bempty[st], ((g / NB) - 1) & 1, abort_flag, err, 37)) { ok = false; break; }
+                    tc::mbar_arrive_tx(&bfull[st], 2u * (uint32_t)np2 * 128u);
                     uint8_t *dst = smem + OFF_B + st * B_STAGE, *dlo = dst + np2 * 128;
                     const int x = ss * 128;  // bytes: 64 fp16 per stage
                     // the maps are named with constant indices so they stay in parameter space
                     switch (sel) {
-                        case 0: tc::tma_load_2d(dst, &bmaps.hi[0], x, it.row0, &opfull[st]);
-                                tc::tma_load_2d(dlo, &bmaps.lo[0], x, it.row0, &opfull[st]); break;
-                        case 1: tc::tma_load_2d(dst, &bmaps.hi[1], x, it.row0, &opfull[st]);
-                                tc::tma_load_2d(dlo, &bmaps.lo[1], x, it.row0, &opfull[st]); break;
-                        default: tc::tma_load_2d(dst, &bmaps.hi[2], x, it.row0, &opfull[st]);
-                                 tc::tma_load_2d(dlo, &bmaps.lo[2], x, it.row0, &opfull[st]); break;
+                        case 0: tc::tma_load_2d(dst, &bmaps.hi[0], x, it.row0, &bfull[st]);
+                                tc::tma_load_2d(dlo, &bmaps.lo[0], x, it.row0, &bfull[st]); break;
+                        case 1: tc::tma_load_2d(dst, &bmaps.hi[1], x, it.row0, &bfull[st]);
+                                tc::tma_load_2d(dlo, &bmaps.lo[1], x, it.row0, &bfull[st]); break;
+                        default: tc::tma_load_2d(dst, &bmaps.hi[2], x, it.row0, &bfull[st]);
+                                 tc::tma_load_2d(dlo, &bmaps.lo[2], x, it.row0, &bfull[st]); break;
                     }
                 }
             }
             // the last copies land before the CTA may exit
             // (bounded by time only: after an abort the copies still land in this CTA's memory)
-            // (each slot's latest use; the phase also needs the producers' arrivals, which
-            // come unless the kernel aborted, so this drain is bounded by time as well)
-            for (uint32_t k = g > (uint32_t)NS ? g - NS : 0; k < g; k++) tc::mbar_drain(&opfull[k % NS], (k / NS) & 1);
+            // (each slot's latest use)
+            for (uint32_t k = g > (uint32_t)NB ? g - NB : 0; k < g; k++) tc::mbar_drain(&bfull[k % NB], (k / NB) & 1);
         }
     } else if (warp == WARP_CODE) {
         // ---------------- TMA: weight codes and block scales, 4 stages per slot ----------------
@@ -396,23 +399,27 @@ __global__ void __launch_bounds__(h3k::NTHREADS, 1)
                         // rows 0-63 gate and 64-127 up of the same 64 features; thread = (block qb
                         // of 32 features, column): h = act(gate, up), then the q8_0 block
                         // (q40.h:124-138), and the down GEMM's fp16 planes of d * q
+                        // a thread pair per (32-feature block qb, column): 16 features each, the
+                        // block's absolute maximum combined with one shuffle (the same value)
                         const int MI = a.O / 2, nbh = MI / 32, f0 = (m0 / 128) * 64;
-                        const int n = tid & 31, qb = tid >> 5, col = 32 * hc + n;
-                        if (qb < 2 && col < ncols) {
-                            const size_t pr = (size_t)(it.row0 + col);
-                            float hv[32];
-                            float amax = 0.f;
+                        const int half = tid & 1, n = (tid >> 1) & 31, qb = tid >> 6, col = 32 * hc + n;
+                        const bool act_ok = col < ncols;
+                        const size_t pr = (size_t)(it.row0 + (act_ok ? col : 0));
+                        float hv[16];
+                        float amax = 0.f;
 #pragma unroll
-                            for (int j = 0; j < 32; j++) {
-                                const int fl = 32 * qb + j;
-                                hv[j] = gated_act(a.act, ct[fl * CTX + n], ct[(64 + fl) * CTX + n], a.clamp);
-                                amax = fmaxf(amax, fabsf(hv[j]));
-                            }
+                        for (int j = 0; j < 16; j++) {
+                            const int fl = 32 * qb + 16 * half + j;
+                            hv[j] = gated_act(a.act, ct[fl * CTX + n], ct[(64 + fl) * CTX + n], a.clamp);
+                            amax = fmaxf(amax, fabsf(hv[j]));
+                        }
+                        amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+                        if (act_ok) {
                             const float d = __fdiv_rn(amax, 127.0f);
                             const float id = d != 0.f ? __fdiv_rn(1.0f, d) : 0.0f;
-                            uint32_t wq[8], H[16], L[16];
+                            uint32_t wq[4], H[8], L[8];
 #pragma unroll
-                            for (int j4 = 0; j4 < 8; j4++) {
+                            for (int j4 = 0; j4 < 4; j4++) {
                                 uint32_t word = 0;
                                 int qv[4];
 #pragma unroll
@@ -425,17 +432,15 @@ __global__ void __launch_bounds__(h3k::NTHREADS, 1)
                                 split_f2(make_float2((float)qv[0] * d, (float)qv[1] * d), H[2 * j4], L[2 * j4]);
                                 split_f2(make_float2((float)qv[2] * d, (float)qv[3] * d), H[2 * j4 + 1], L[2 * j4 + 1]);
                             }
-                            uint4 *dst = reinterpret_cast<uint4 *>(a.hq + pr * MI + f0 + 32 * qb);
-                            dst[0] = make_uint4(wq[0], wq[1], wq[2], wq[3]);
-                            dst[1] = make_uint4(wq[4], wq[5], wq[6], wq[7]);
-                            uint4 *dh = reinterpret_cast<uint4 *>(a.hhs + pr * MI + f0 + 32 * qb);
-                            uint4 *dl = reinterpret_cast<uint4 *>(a.hhs + (size_t)a.rows_cap * MI + pr * MI + f0 + 32 * qb);
-#pragma unroll
-                            for (int q = 0; q < 4; q++) {
-                                dh[q] = make_uint4(H[4 * q], H[4 * q + 1], H[4 * q + 2], H[4 * q + 3]);
-                                dl[q] = make_uint4(L[4 * q], L[4 * q + 1], L[4 * q + 2], L[4 * q + 3]);
-                            }
-                            a.hs[pr * nbh + f0 / 32 + qb] = d;
+                            const int f = f0 + 32 * qb + 16 * half;
+                            *reinterpret_cast<uint4 *>(a.hq + pr * MI + f) = make_uint4(wq[0], wq[1], wq[2], wq[3]);
+                            uint4 *dh = reinterpret_cast<uint4 *>(a.hhs + pr * MI + f);
+                            uint4 *dl = reinterpret_cast<uint4 *>(a.hhs + (size_t)a.rows_cap * MI + pr * MI + f);
+                            dh[0] = make_uint4(H[0], H[1], H[2], H[3]);
+                            dh[1] = make_uint4(H[4], H[5], H[6], H[7]);
+                            dl[0] = make_uint4(L[0], L[1], L[2], L[3]);
+                            dl[1] = make_uint4(L[4], L[5], L[6], L[7]);
+                            if (half == 0) a.hs[pr * nbh + f0 / 32 + qb] = d;
                         }
                     } else {
                         // OUT[token, m0 + 4 o4 .. + 3] += w * C (each warp instruction covers 512
