@@ -133,7 +133,7 @@ def check_pairs(orc, kind, blobs, X, eidx, ewt, out_gpu, bank, pairs=None):
     return flipped_tok
 
 
-@pytest.fixture(params=["auto", "i8", "mma8", "mma8w", "h3"])
+@pytest.fixture(params=["auto", "i8", "mma8", "mma8w", "h3", "hyb"])
 def engine(request, monkeypatch):
     """every expert engine: auto (the decode GEMV kernels for calls of <= 64 pairs, else the
     int8 mma.sync GEMM with 32- or 64-row items by the rows per expert), and the int8

@@ -581,6 +581,13 @@ __device__ __forceinline__ void gemm_item(const GemmArgs &a, int item_idx) {
             const size_t pr = (size_t)(it.row0 + n);
             a.hq[pr * MI + f0 + f] = q;
             if (a.hh) a.hh[pr * MI + f0 + f] = __int2half_rn(q);
+            if (a.hhs) {
+                // the folded-scale down GEMM's B planes: fp16 hi and lo of d * q
+                const float v = (float)q * d;
+                const __half hi = __float2half_rn(v);
+                a.hhs[pr * MI + f0 + f] = hi;
+                a.hhs[(size_t)a.rows_cap * MI + pr * MI + f0 + f] = __float2half_rn(v - __half2float(hi));
+            }
             if (lane == 0) a.hs[pr * nbh + f0 / 32 + hb] = d;
             if (FMT == GPU_FMT_TQ2) {
                 int s = q;

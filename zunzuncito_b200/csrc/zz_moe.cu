@@ -46,15 +46,17 @@ bool moe_h3_supported(int fmt, int D, int MI);
 int launch_moe_dec(int fmt, const GemmArgs &gu, const GemmArgs &dn, int P, float *hbuf, cudaStream_t st);
 
 // Expert engine. Default ("auto"): the small-batch GEMV kernels (zz_moe_dec.cu) when
-// S*K <= DEC_MAX_PAIRS; else the int8 mma.sync GEMM (k_gemm<..., S8>), the fastest
-// measured, with work items of up to 32 routed rows, or of up to 64 rows when the experts
-// average at least WIDE_PAIRS_PER_EXPERT rows (prefill: the weight fragments then serve
-// twice the columns; at S=512 top-8 the narrow items are faster). ZZ_MOE_KERNEL=i8
+// S*K <= DEC_MAX_PAIRS; else the int8 mma.sync GEMM (k_gemm<..., S8>) with work items of
+// up to 32 routed rows; when the experts average at least WIDE_PAIRS_PER_EXPERT rows
+// (prefill), 64-row items with the gate/up GEMM on mma.sync and the down GEMM on the
+// folded-scale tcgen05 engine (hyb; q4_0 banks, else both on mma.sync). At S=512 top-8
+// the narrow mma.sync items are the fastest. ZZ_MOE_KERNEL=i8
 // selects the int8 tcgen05 engine (zz_moe_i8.cu) where the layer's shape allows it;
 // =mma8 / =mma8w force the narrow / wide mma.sync items; =h3 the folded-scale fp16
-// tcgen05 engine (zz_moe_h3.cu, q4_0 banks). The int8 engines are exact per block; h3
-// carries every product to a relative 2^-21.
-enum { ENG_DEC = 0, ENG_MMA8 = 3, ENG_I8 = 5, ENG_MMA8W = 6, ENG_H3 = 7 };
+// tcgen05 engine (zz_moe_h3.cu, q4_0 banks); =hyb the wide mma.sync gate/up GEMM (which
+// then also writes the hidden rows' fp16 planes) followed by the h3 down GEMM. The int8
+// engines are exact per block; h3 carries every product to a relative 2^-21.
+enum { ENG_DEC = 0, ENG_MMA8 = 3, ENG_I8 = 5, ENG_MMA8W = 6, ENG_H3 = 7, ENG_HYB = 8 };
 constexpr int DEC_MAX_PAIRS = 64, WIDE_PAIRS_PER_EXPERT = 128;
 static int moe_engine(int P, const zz_expert_bank *b) {
     const char *e = getenv("ZZ_MOE_KERNEL");
@@ -63,9 +65,13 @@ static int moe_engine(int P, const zz_expert_bank *b) {
     if (e && !strcmp(e, "mma8w")) return ENG_MMA8W;
     if (e && !strcmp(e, "i8")) return i8_ok ? ENG_I8 : ENG_MMA8;
     if (e && !strcmp(e, "h3")) return moe_h3_supported(b->fmt, b->hidden, b->inter) ? ENG_H3 : ENG_MMA8;
+    if (e && !strcmp(e, "hyb")) return moe_h3_supported(b->fmt, b->hidden, b->inter) ? ENG_HYB : ENG_MMA8W;
     // the decode kernels take calls of up to DEC_MAX_PAIRS pairs
     if (P <= DEC_MAX_PAIRS) return ENG_DEC;
-    return (long)P >= (long)WIDE_PAIRS_PER_EXPERT * b->n_experts ? ENG_MMA8W : ENG_MMA8;
+    if ((long)P < (long)WIDE_PAIRS_PER_EXPERT * b->n_experts) return ENG_MMA8;
+    // prefill: the wide mma.sync gate/up GEMM and the tcgen05 down GEMM (S=4096 Gemma-4
+    // layer 1.83 ms against 1.98 with both GEMMs on mma.sync)
+    return moe_h3_supported(b->fmt, b->hidden, b->inter) ? ENG_HYB : ENG_MMA8W;
 }
 constexpr int I8_BN = 128, H3_BN = 64;
 
@@ -294,9 +300,9 @@ static MoeWs moe_layout(const zz_expert_bank *b, int S, int K, uint8_t *base) {
     w.hs = (float *)take(cap * (MI / 32) * 4);
     w.hblk = (int *)take(cap * (MI / 32) * 4);
     w.hf = (float *)take(P <= (size_t)DEC_MAX_PAIRS ? cap * MI * 4 : 0);
-    const bool h3 = moe_engine((int)P, b) == ENG_H3;
-    w.xhs = (__half *)take(h3 ? cap * D * 4 : 0);
-    w.hhs = (__half *)take(h3 ? cap * MI * 4 : 0);
+    const int eng = moe_engine((int)P, b);
+    w.xhs = (__half *)take(eng == ENG_H3 ? cap * D * 4 : 0);
+    w.hhs = (__half *)take(eng == ENG_H3 || eng == ENG_HYB ? cap * MI * 4 : 0);
     w.bad = (int *)take(4);
     w.tcerr = (int *)take(4);
     w.total = o;
@@ -464,7 +470,7 @@ static int moe_impl(const zz_expert_bank *b, const float *X, const int8_t *xq_in
     }
     prof_mark(st);
     const int eng = moe_engine(P, b);
-    const bool h3 = eng == ENG_H3, i8 = eng == ENG_I8 || h3, wide = eng == ENG_MMA8W;
+    const bool hyb = eng == ENG_HYB, h3 = eng == ENG_H3, i8 = eng == ENG_I8 || h3, wide = eng == ENG_MMA8W || hyb;
     const int bn = h3 ? H3_BN : i8 ? I8_BN : eng == ENG_DEC ? DEC_BN : wide ? MOE_BN_WIDE : MOE_BN;
     const int maxit = P / bn + E + 1;
     const int8_t *xq = xq_in;
@@ -477,7 +483,7 @@ static int moe_impl(const zz_expert_bank *b, const float *X, const int8_t *xq_in
         return 0;
     k_route<<<1, 1024, 4 * E * sizeof(int), side->s>>>(eidx, ewt, P, E, bn,
                                                       (int)w.cap, w.pair_src, w.pair_w, w.items, w.n_items, w.tcerr,
-                                                      i8 ? 1 : 0);
+                                                      i8 || hyb ? 1 : 0);
     if (!check_cuda(cudaGetLastError(), "route launch")) return 0;
     if (!check_cuda(cudaEventRecord(side->join, side->s), "join")) return 0;
     if (X) {
@@ -536,6 +542,9 @@ static int moe_impl(const zz_expert_bank *b, const float *X, const int8_t *xq_in
         if (!launch_moe_h3(EPI_GATEUP, g, E, w.tcerr, st)) return 0;
     } else if (i8) {
         if (!launch_moe_i8(fmt, EPI_GATEUP, g, E, w.tcerr, st)) return 0;
+    } else if (hyb) {
+        g.hhs = w.hhs;  // the h3 down GEMM's B planes
+        if (!launch_gemm<EPI_GATEUP, MOE_BN_WIDE, false, true>(fmt, g, dim3((2 * MI) / G_BM, maxit), st)) return 0;
     } else if (!(wide ? launch_gemm<EPI_GATEUP, MOE_BN_WIDE, false, true>(fmt, g, dim3((2 * MI) / G_BM, maxit), st)
                       : launch_gemm<EPI_GATEUP, MOE_BN, false, true>(fmt, g, dim3((2 * MI) / G_BM, maxit), st))) {
         return 0;
@@ -552,7 +561,7 @@ static int moe_impl(const zz_expert_bank *b, const float *X, const int8_t *xq_in
     d.out = OUT; d.pair_w = w.pair_w; d.pair_src = w.pair_src; d.K = K;
     d.xg8 = w.hq; d.xsT = w.hsT; d.ldT = (int)w.ldT; d.rows_cap = (int)w.cap;
     d.xhs = w.hhs;
-    int ok = h3 ? launch_moe_h3(EPI_DOWN, d, E, w.tcerr, st)
+    int ok = h3 || hyb ? launch_moe_h3(EPI_DOWN, d, E, w.tcerr, st)
            : i8 ? launch_moe_i8(fmt, EPI_DOWN, d, E, w.tcerr, st)
            : wide ? launch_gemm<EPI_DOWN, MOE_BN_WIDE, false, true>(fmt, d, dim3((D + G_BM - 1) / G_BM, maxit), st)
                   : launch_gemm<EPI_DOWN, MOE_BN, false, true>(fmt, d, dim3((D + G_BM - 1) / G_BM, maxit), st);
