@@ -105,3 +105,25 @@ def test_noalloc_capacity_matches_header(fmt, E, D, MI, smax):
     assert zz.lib.zz_moe_workspace_bytes(ctypes.byref(b), smax, 8) <= cap
     assert zz.lib.zz_moe_workspace_bytes(ctypes.byref(b), smax + 1, 8) > cap
     assert f"S > {smax}" in open(HDR).read()
+
+
+def test_workspace_follows_engine(monkeypatch):
+    """the layer's workspace holds the fp16 operand planes of the tcgen05 engines only for
+    calls those engines take: the hidden rows' planes (4 bytes per element) from the
+    prefill size on (experts averaging >= 128 routed rows: S = 2048 at top-8 over 128
+    experts), the gathered activation rows' planes too when h3 is forced"""
+    monkeypatch.delenv("ZZ_MOE_KERNEL", raising=False)
+    b = zz.ExpertBank(zz.GPU_FMT_Q40, 128, 2816, 704, None, None, None, None)
+    ws = lambda S: zz.lib.zz_moe_workspace_bytes(ctypes.byref(b), S, 8)  # noqa: E731
+    step = ws(2047) - ws(2046)
+    assert ws(2048) - ws(2047) > 2047 * 8 * 704 * 4          # the hidden planes appear
+    monkeypatch.setenv("ZZ_MOE_KERNEL", "mma8w")
+    assert ws(2048) - ws(2047) < 4 * step                    # no planes on mma.sync alone
+    monkeypatch.setenv("ZZ_MOE_KERNEL", "mma8")
+    plain = ws(512)
+    monkeypatch.setenv("ZZ_MOE_KERNEL", "h3")
+    assert ws(512) - plain >= 512 * 8 * (2816 + 704) * 4    # both operand planes
+    q8 = zz.ExpertBank(zz.GPU_FMT_Q80, 128, 2816, 704, None, None, None, None)
+    monkeypatch.delenv("ZZ_MOE_KERNEL")
+    w8 = lambda S: zz.lib.zz_moe_workspace_bytes(ctypes.byref(q8), S, 8)  # noqa: E731
+    assert w8(2048) - w8(2047) < 4 * (w8(2047) - w8(2046))   # q8_0 banks stay on mma.sync
